@@ -1,0 +1,445 @@
+// extern "C" entry points (include/aipu_q4k.h) and the per-device context.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/aipu_q4k.h"
+#include "common.cuh"
+#include "deq.cuh"
+#include "gemv.cuh"
+#include "kernels.h"
+#include "launch.h"
+
+namespace aipu {
+
+static thread_local std::string g_err;
+
+int set_error(int code, const char* msg) {
+  g_err = msg ? msg : "";
+  return code;
+}
+int set_cuda_error(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return OK;
+  g_err = std::string(where) + ": " + cudaGetErrorString(e);
+  return ECUDA_;
+}
+const char* last_error() { return g_err.c_str(); }
+
+int launch_kernel(const void* kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, bool pdl, void* arg0) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  void* args[1] = {arg0};
+  return set_cuda_error(cudaLaunchKernelExC(&cfg, kern, args), "cudaLaunchKernelExC");
+}
+
+int num_sms_of_current_device() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 1;
+}
+
+}  // namespace aipu
+
+using namespace aipu;
+
+// one stream-K workspace: partial sums per CTA and arrival counters per tile
+struct Workspace {
+  float* partials = nullptr;
+  int* counters = nullptr;
+  int max_tiles = 0;
+};
+
+struct aipu_ctx {
+  int device = 0;
+  int num_sms = 1;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  Workspace ws[2];  // [0] main stream, [1] side stream
+  int* status = nullptr;
+  int* router_counters = nullptr;  // [1024 + 1]
+  // MoE scratch (grown on demand)
+  void* moe = nullptr;
+  size_t moe_bytes = 0;
+  int flags = 0;  // AIPU_FLAG_*
+};
+
+static const int kMaxTiles = 1 << 16;
+
+static int ws_alloc(Workspace& w, int num_sms) {
+  if (cudaMalloc(&w.partials, sizeof(float) * gemv_partials_floats(num_sms)) != cudaSuccess)
+    return set_error(ENOMEM_, "cudaMalloc(partials)");
+  if (cudaMalloc(&w.counters, sizeof(int) * kMaxTiles) != cudaSuccess) return set_error(ENOMEM_, "cudaMalloc(counters)");
+  if (cudaMemset(w.counters, 0, sizeof(int) * kMaxTiles) != cudaSuccess) return set_error(ECUDA_, "cudaMemset");
+  w.max_tiles = kMaxTiles;
+  return OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+extern "C" {
+
+int aipu_version(void) { return 100; }
+const char* aipu_last_error(void) { return last_error(); }
+
+int64_t aipu_row_bytes(int wtype, int64_t K) {
+  if (K <= 0) return 0;
+  if ((wtype == AIPU_Q4_K || wtype == AIPU_Q6_K) && K % 256) return 0;
+  if (wtype == AIPU_Q8_0 && K % 32) return 0;
+  if (wtype < 0 || wtype > 4) return 0;
+  return row_bytes_of(wtype, K);
+}
+
+int aipu_ctx_create(aipu_ctx** out, int device) {
+  if (!out) return set_error(EINVAL_, "ctx_create: null out pointer");
+  *out = nullptr;
+  DeviceGuard dg(device);
+  aipu_ctx* c = new aipu_ctx();
+  c->device = device;
+  c->num_sms = num_sms_of_current_device();
+  int rc = OK;
+  if ((rc = ws_alloc(c->ws[0], c->num_sms)) || (rc = ws_alloc(c->ws[1], c->num_sms))) {
+    aipu_ctx_destroy(c);
+    return rc;
+  }
+  if (cudaMalloc(&c->status, sizeof(int)) != cudaSuccess || cudaMemset(c->status, 0, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&c->router_counters, sizeof(int) * 1040) != cudaSuccess ||
+      cudaMemset(c->router_counters, 0, sizeof(int) * 1040) != cudaSuccess) {
+    aipu_ctx_destroy(c);
+    return set_error(ENOMEM_, "ctx_create: cudaMalloc");
+  }
+  if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming) != cudaSuccess) {
+    aipu_ctx_destroy(c);
+    return set_error(ECUDA_, "ctx_create: stream/event");
+  }
+  *out = c;
+  return OK;
+}
+
+int aipu_ctx_destroy(aipu_ctx* c) {
+  if (!c) return OK;
+  DeviceGuard dg(c->device);
+  for (auto& w : c->ws) {
+    cudaFree(w.partials);
+    cudaFree(w.counters);
+  }
+  cudaFree(c->status);
+  cudaFree(c->router_counters);
+  cudaFree(c->moe);
+  if (c->side) cudaStreamDestroy(c->side);
+  if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+  if (c->ev_join) cudaEventDestroy(c->ev_join);
+  delete c;
+  return OK;
+}
+
+int aipu_ctx_set_flags(aipu_ctx* c, int flags) {
+  if (!c || (flags & ~AIPU_FLAG_PDL)) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
+  c->flags = flags;
+  return OK;
+}
+
+int aipu_ctx_status(aipu_ctx* c, int* status) {
+  if (!c || !status) return set_error(EINVAL_, "ctx_status: null pointer");
+  DeviceGuard dg(c->device);
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, c->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_cuda_error(e, "ctx_status");
+  cudaMemset(c->status, 0, sizeof(int));
+  *status = v;
+  return OK;
+}
+
+int aipu_q4k_dequant(int wtype, const void* w, int64_t nrows, int64_t K, void* out, int out_dtype, void* stream) {
+  if (!w || !out || nrows < 0 || aipu_row_bytes(wtype, K) == 0 || (out_dtype != AIPU_DT_F32 && out_dtype != AIPU_DT_BF16))
+    return set_error(EINVAL_, "dequant: bad arguments");
+  return dequant_launch(wtype, w, nrows, K, out, out_dtype == AIPU_DT_BF16, static_cast<cudaStream_t>(stream));
+}
+
+int aipu_act_eval(int kind, const void* x, int64_t n, void* out, void* stream) {
+  if (!x || !out || n < 0 || (kind != 0 && kind != 1)) return set_error(EINVAL_, "act_eval: bad arguments");
+  return act_launch(kind, x, n, out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// fast GEMM on one stream-K workspace, splitting M into blocks the kernel takes
+static int gemm_fast(aipu_ctx* c, Workspace& ws, int wtype, const void* w, int64_t N, int64_t K, const void* x,
+                     int xt, int64_t M, void* y, cudaStream_t s, bool pdl) {
+  const int mb = (xt == AIPU_DT_F32) ? 4 : 8;
+  const int esz = (xt == AIPU_DT_F32) ? 4 : 2;
+  if ((N + 15) / 16 > ws.max_tiles) return set_error(EINVAL_, "gemm: N too large for the workspace");
+  for (int64_t m0 = 0; m0 < M; m0 += mb) {
+    GemvParams p = {};
+    p.w0 = static_cast<const uint8_t*>(w);
+    p.row_bytes = row_bytes_of(wtype, K);
+    p.n_groups = 1;
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.x = static_cast<const uint8_t*>(x) + m0 * K * esz;
+    p.M = static_cast<int>(std::min<int64_t>(mb, M - m0));
+    p.y = static_cast<uint16_t*>(y) + m0 * N;
+    p.partials = ws.partials;
+    p.counters = ws.counters;
+    p.status = c->status;
+    int rc = gemv_launch(wtype, xt == AIPU_DT_F32 ? XT_F32 : XT_BF16, EPI_STORE, p, c->num_sms, s, pdl);
+    if (rc) return rc;
+  }
+  return OK;
+}
+
+extern "C" int aipu_q4k_gemm(aipu_ctx* c, int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype,
+                             int64_t M, void* y, float* y_f32, int mode, void* stream) {
+  if (!c || !w || !x || (!y && !y_f32) || N <= 0 || M <= 0 || aipu_row_bytes(wtype, K) == 0 ||
+      (x_dtype != AIPU_DT_F32 && x_dtype != AIPU_DT_BF16) || N > INT32_MAX || K > INT32_MAX)
+    return set_error(EINVAL_, "gemm: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0) return set_error(EINVAL_, "gemm: weights must be 16-byte aligned");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int xt = x_dtype == AIPU_DT_F32 ? XT_F32 : XT_BF16;
+  if (mode == AIPU_MODE_STRICT || wtype == AIPU_F32 || y_f32) {
+    return strict_gemm_launch(wtype, w, static_cast<int>(N), static_cast<int>(K), x, xt, static_cast<int>(M),
+                              static_cast<uint16_t*>(y), y_f32, s);
+  }
+  if (mode != AIPU_MODE_FAST) return set_error(EINVAL_, "gemm: unknown mode");
+  if (K % 256) return set_error(EINVAL_, "gemm: fast mode needs K to be a multiple of 256");
+  return gemm_fast(c, c->ws[0], wtype, w, N, K, x, x_dtype, M, y, s, (c->flags & AIPU_FLAG_PDL) != 0);
+}
+
+extern "C" int aipu_moe_router(aipu_ctx* c, int wt, const void* w, const float* bias, const void* x, int64_t M,
+                               int64_t K, int64_t E, int topk, float scale, int32_t* sel, void* sel_w, void* gate,
+                               void* logits, void* stream) {
+  if (!c || !w || !x || !sel || !sel_w || M <= 0 || M > 1024 || E <= 0 || E > 1024 || topk <= 0 || topk > 16 ||
+      topk > E || (wt != AIPU_F32 && aipu_row_bytes(wt, K) == 0) || K <= 0)
+    return set_error(EINVAL_, "router: bad arguments");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint16_t* gbuf = static_cast<uint16_t*>(gate);
+  uint16_t* tmp = nullptr;
+  if (!gbuf) {
+    if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), sizeof(uint16_t) * M * E, s) != cudaSuccess)
+      return set_error(ENOMEM_, "router: gate scratch");
+    gbuf = tmp;
+  }
+  RouterParams p = {};
+  p.wt = wt;
+  p.w = static_cast<const uint8_t*>(w);
+  p.bias = bias;
+  p.x = static_cast<const uint16_t*>(x);
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.E = static_cast<int>(E);
+  p.topk = topk;
+  p.scale = scale;
+  p.gate = gbuf;
+  p.logits = static_cast<uint16_t*>(logits);
+  p.sel = sel;
+  p.sel_w = static_cast<uint16_t*>(sel_w);
+  p.counters = c->router_counters;
+  int rc = router_launch(p, s, false);
+  if (tmp) cudaFreeAsync(tmp, s);
+  return rc;
+}
+
+// ------------------------------------------------------------------ MoE decode layer
+struct MoeScratch {
+  uint16_t* gate;     // [M, E]
+  int32_t* sel;       // [M, T]
+  uint16_t* sel_w;    // [M, T]
+  int32_t* union_ids; // [U]
+  int32_t* n_union;   // [1]
+  int32_t* slot_map;  // [M, T]
+  uint16_t* h;        // [U, M, F]
+  uint16_t* y;        // [U, M, H]
+  uint16_t* h_sh;     // [M, F]
+  uint16_t* y_sh;     // [M, H]
+};
+
+static size_t al256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+static int moe_scratch(aipu_ctx* c, int64_t M, int64_t E, int T, int64_t H, int64_t F, MoeScratch& sc) {
+  const int64_t U = std::min<int64_t>(E, M * T);
+  size_t sz[10] = {al256(2 * M * E), al256(4 * M * T), al256(2 * M * T), al256(4 * U), al256(4),
+                   al256(4 * M * T), al256(2 * U * M * F), al256(2 * U * M * H), al256(2 * M * F), al256(2 * M * H)};
+  size_t total = 0;
+  for (size_t v : sz) total += v;
+  if (total > c->moe_bytes) {
+    cudaFree(c->moe);
+    c->moe = nullptr;
+    c->moe_bytes = 0;
+    if (cudaMalloc(&c->moe, total) != cudaSuccess) return set_error(ENOMEM_, "moe: scratch allocation");
+    c->moe_bytes = total;
+  }
+  uint8_t* b = static_cast<uint8_t*>(c->moe);
+  void* ptr[10];
+  for (int i = 0; i < 10; ++i) {
+    ptr[i] = b;
+    b += sz[i];
+  }
+  sc.gate = static_cast<uint16_t*>(ptr[0]);
+  sc.sel = static_cast<int32_t*>(ptr[1]);
+  sc.sel_w = static_cast<uint16_t*>(ptr[2]);
+  sc.union_ids = static_cast<int32_t*>(ptr[3]);
+  sc.n_union = static_cast<int32_t*>(ptr[4]);
+  sc.slot_map = static_cast<int32_t*>(ptr[5]);
+  sc.h = static_cast<uint16_t*>(ptr[6]);
+  sc.y = static_cast<uint16_t*>(ptr[7]);
+  sc.h_sh = static_cast<uint16_t*>(ptr[8]);
+  sc.y_sh = static_cast<uint16_t*>(ptr[9]);
+  return OK;
+}
+
+// SwiGLU on groups of experts: h[g] = bf16(silu(x Wg_e) * (x Wu_e)), y[g] = h[g] Wd_e
+static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, const void* uw, int dwt, const void* dw,
+                         int64_t H, int64_t F, const int* group_ids, const int* n_groups_dev, int n_groups,
+                         const void* x, int64_t M, uint16_t* h, uint16_t* y, cudaStream_t s, bool pdl) {
+  const int64_t gstride = F * row_bytes_of(gwt, H), dstride = H * row_bytes_of(dwt, F);
+  for (int64_t m0 = 0; m0 < M; m0 += 8) {
+    const int mb = static_cast<int>(std::min<int64_t>(8, M - m0));
+    GemvParams p = {};
+    p.w0 = static_cast<const uint8_t*>(gw);
+    p.w1 = static_cast<const uint8_t*>(uw);
+    p.row_bytes = row_bytes_of(gwt, H);
+    p.expert_stride = gstride;
+    p.group_ids = group_ids;
+    p.n_groups_dev = n_groups_dev;
+    p.n_groups = n_groups;
+    p.N = static_cast<int>(F);
+    p.K = static_cast<int>(H);
+    p.x = static_cast<const uint16_t*>(x) + m0 * H;
+    p.x_group_stride = 0;
+    p.M = mb;
+    p.y = h + m0 * F;
+    p.y_group_stride = M * F;
+    p.partials = ws.partials;
+    p.counters = ws.counters;
+    p.status = c->status;
+    int rc = gemv_launch(gwt, XT_BF16, EPI_SWIGLU, p, c->num_sms, s, pdl);
+    if (rc) return rc;
+    GemvParams q = p;
+    q.w0 = static_cast<const uint8_t*>(dw);
+    q.w1 = nullptr;
+    q.row_bytes = row_bytes_of(dwt, F);
+    q.expert_stride = dstride;
+    q.N = static_cast<int>(H);
+    q.K = static_cast<int>(F);
+    q.x = h + m0 * F;
+    q.x_group_stride = M * F;
+    q.y = y + m0 * H;
+    q.y_group_stride = M * H;
+    rc = gemv_launch(dwt, XT_BF16, EPI_STORE, q, c->num_sms, s, pdl);
+    if (rc) return rc;
+  }
+  return OK;
+}
+
+extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y,
+                              int32_t* sel_out, void* sel_w_out, void* stream) {
+  if (!c || !W || !x || !y || M <= 0 || M > 1024) return set_error(EINVAL_, "moe_layer: bad arguments");
+  const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
+  const int T = W->topk;
+  if (H % 256 || F % 256 || E <= 0 || E > 1024 || T <= 0 || T > 16 || T > E || !W->gate_w || !W->up_w ||
+      !W->down_w || !W->router_w || W->gate_wtype != W->up_wtype || W->gate_wtype == AIPU_F32 ||
+      W->down_wtype == AIPU_F32)
+    return set_error(EINVAL_, "moe_layer: bad weights descriptor");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MoeScratch sc = {};
+  int rc = moe_scratch(c, M, E, T, H, F, sc);
+  if (rc) return rc;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
+  if (shared) {
+    // shared expert on the side stream, overlapping the (serial) router
+    if ((rc = set_cuda_error(cudaEventRecord(c->ev_fork, s), "eventRecord"))) return rc;
+    if ((rc = set_cuda_error(cudaStreamWaitEvent(c->side, c->ev_fork, 0), "streamWaitEvent"))) return rc;
+    rc = swiglu_groups(c, c->ws[1], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
+                       H, F, nullptr, nullptr, 1, x, M, sc.h_sh, sc.y_sh, c->side, false);
+    if (rc) return rc;
+    if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
+  }
+  RouterParams rp = {};
+  rp.wt = W->router_wtype;
+  rp.w = static_cast<const uint8_t*>(W->router_w);
+  rp.bias = W->router_bias;
+  rp.x = static_cast<const uint16_t*>(x);
+  rp.M = static_cast<int>(M);
+  rp.K = static_cast<int>(H);
+  rp.E = static_cast<int>(E);
+  rp.topk = T;
+  rp.scale = W->scale;
+  rp.gate = sc.gate;
+  rp.sel = sc.sel;
+  rp.sel_w = sc.sel_w;
+  rp.union_ids = sc.union_ids;
+  rp.n_union = sc.n_union;
+  rp.slot_map = sc.slot_map;
+  rp.counters = c->router_counters;
+  if ((rc = router_launch(rp, s, false))) return rc;
+  const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
+  rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F, sc.union_ids,
+                     sc.n_union, Umax, x, M, sc.h, sc.y, s, true);
+  if (rc) return rc;
+  if (shared && (rc = set_cuda_error(cudaStreamWaitEvent(s, c->ev_join, 0), "streamWaitEvent"))) return rc;
+  CombineParams cp = {};
+  cp.M = static_cast<int>(M);
+  cp.H = static_cast<int>(H);
+  cp.topk = T;
+  cp.slot_map = sc.slot_map;
+  cp.sel_w = sc.sel_w;
+  cp.y_union = sc.y;
+  cp.y_shared = shared ? sc.y_sh : nullptr;
+  cp.out = static_cast<uint16_t*>(y);
+  if ((rc = combine_launch(cp, s, true))) return rc;
+  if (sel_out && (rc = set_cuda_error(cudaMemcpyAsync(sel_out, sc.sel, 4 * M * T, cudaMemcpyDeviceToDevice, s), "copy sel")))
+    return rc;
+  if (sel_w_out &&
+      (rc = set_cuda_error(cudaMemcpyAsync(sel_w_out, sc.sel_w, 2 * M * T, cudaMemcpyDeviceToDevice, s), "copy sel_w")))
+    return rc;
+  return OK;
+}
+
+extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt, const void* uw, int dwt,
+                                  const void* dw, int64_t H, int64_t F, const void* x, int64_t M, void* h, void* y,
+                                  void* stream) {
+  if (!c || !gw || !uw || !dw || !x || !y || M <= 0 || H % 256 || F % 256 || gwt != uwt || gwt == AIPU_F32 ||
+      dwt == AIPU_F32)
+    return set_error(EINVAL_, "swiglu_expert: bad arguments");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint16_t* hb = static_cast<uint16_t*>(h);
+  uint16_t* tmp = nullptr;
+  if (!hb) {
+    if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), 2 * M * F, s) != cudaSuccess)
+      return set_error(ENOMEM_, "swiglu: scratch");
+    hb = tmp;
+  }
+  int rc = swiglu_groups(c, c->ws[0], gwt, gw, uw, dwt, dw, H, F, nullptr, nullptr, 1, x, M, hb,
+                         static_cast<uint16_t*>(y), s, false);
+  if (tmp) cudaFreeAsync(tmp, s);
+  return rc;
+}

@@ -1,0 +1,568 @@
+// Decode dequant GEMV kernel bodies and host launchers (design notes in gemv.cuh).
+#include <algorithm>
+#include <cstdio>
+
+#include "gemv.cuh"
+#include "launch.h"
+
+namespace aipu {
+
+// ------------------------------------------------------------------ shared-memory layout
+struct GemvLayout {
+  int off_misc, off_red, off_xs, off_sxs, off_ring, total;
+};
+
+__host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int nstages, int pitch, int xpitch) {
+  GemvLayout L;
+  L.off_misc = 2 * GEMV_MAXST * 8;                 // mbarriers first
+  L.off_red = L.off_misc + 256;
+  L.off_xs = L.off_red + GEMV_NCW * 32 * 16;       // 4096 B of reduction space
+  L.off_sxs = L.off_xs + ncols * xpitch;
+  int sx = (wt == WT_Q4K) ? ncols * (K / 256) * 32 : 0;
+  L.off_ring = (L.off_sxs + sx + 127) & ~127;
+  L.total = L.off_ring + nstages * 16 * pitch;
+  return L;
+}
+
+// ------------------------------------------------------------------ shared-memory loads
+__device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
+  if ((reinterpret_cast<uintptr_t>(p) & 3u) == 0u) return *reinterpret_cast<const uint32_t*>(p);
+  const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+  return static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16);
+}
+
+constexpr uint32_t H2_1024 = 0x64006400u;   // (1024, 1024)
+constexpr uint32_t H2_M1024 = 0xE400E400u;  // (-1024, -1024)
+constexpr uint32_t H2_1056 = 0x64206420u;   // (1056, 1056)
+constexpr uint32_t H2_1152 = 0x64806480u;   // (1152, 1152)
+constexpr uint32_t H2_16TH = 0x2C002C00u;   // (1/16, 1/16)
+constexpr uint32_t H2_M64 = 0xD400D400u;    // (-64, -64)
+
+__device__ __forceinline__ uint32_t byte_pair_sel(int idx) {
+  return 0x4040u | static_cast<uint32_t>(idx) | (static_cast<uint32_t>(idx) << 8);
+}
+
+// ------------------------------------------------------------------ per-type unit compute
+// A unit = 16 weight rows (g and g+8 of this thread) x 256 weights at super-block column `sb`.
+// xcol: this thread's activation column (fp16) in shared memory; colok: the column is a live
+// token column (others feed zeros).
+
+__device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol,
+                                         const uint32_t* sxcol, bool colok, int sb, int t, float (&acc)[4]) {
+  const uint4 hg = *reinterpret_cast<const uint4*>(rg);
+  const uint4 h8 = *reinterpret_cast<const uint4*>(rg8);
+  const float dg = f16_bits_to_f32(hg.x), dmg = f16_bits_to_f32(hg.x >> 16);
+  const float d8 = f16_bits_to_f32(h8.x), dm8 = f16_bits_to_f32(h8.x >> 16);
+  // 8 six-bit scales / mins per row, as packed bytes (get_scale_min_k4 for j = 0..7 at once)
+  const uint32_t sc03g = hg.y & 0x3F3F3F3Fu, m03g = hg.z & 0x3F3F3F3Fu;
+  const uint32_t sc47g = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+  const uint32_t m47g = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+  const uint32_t sc038 = h8.y & 0x3F3F3F3Fu, m038 = h8.z & 0x3F3F3F3Fu;
+  const uint32_t sc478 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+  const uint32_t m478 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+
+  float P[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint8_t* xb = xcol + 2 * (sb * 256 + 8 * t);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t wg = (p < 2) ? sc03g : sc47g;
+    const uint32_t w8 = (p < 2) ? sc038 : sc478;
+    const int il = (2 * p) & 3, ih = (2 * p + 1) & 3;
+    // (sc, sc) as fp16 pairs; low-nibble constants (sc, -1024 sc), high-nibble (sc/16, -64 sc)
+    const uint32_t slg = hsub2_u32(prmt(wg, 0x64u, byte_pair_sel(il)), H2_1024);
+    const uint32_t shg = hsub2_u32(prmt(wg, 0x64u, byte_pair_sel(ih)), H2_1024);
+    const uint32_t sl8 = hsub2_u32(prmt(w8, 0x64u, byte_pair_sel(il)), H2_1024);
+    const uint32_t sh8 = hsub2_u32(prmt(w8, 0x64u, byte_pair_sel(ih)), H2_1024);
+    const uint32_t alg = hmul2_u32(slg, H2_M1024), al8 = hmul2_u32(sl8, H2_M1024);
+    const uint32_t mhg = hmul2_u32(shg, H2_16TH), mh8 = hmul2_u32(sh8, H2_16TH);
+    const uint32_t ahg = hmul2_u32(shg, H2_M64), ah8 = hmul2_u32(sh8, H2_M64);
+    const uint2 qg = *reinterpret_cast<const uint2*>(rg + 16 + 32 * p + 8 * t);
+    const uint2 q8 = *reinterpret_cast<const uint2*>(rg8 + 16 + 32 * p + 8 * t);
+    uint4 xl = make_uint4(0, 0, 0, 0), xh = make_uint4(0, 0, 0, 0);
+    if (colok) {
+      xl = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p));
+      xh = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p + 32));
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t w = j ? qg.y : qg.x, v = j ? q8.y : q8.x;
+      const uint32_t ws = w >> 8, vs = v >> 8;
+      uint32_t a[4];
+      a[0] = hfma2_u32(lop3_and_or(w, 0x000F000Fu, H2_1024), slg, alg);
+      a[1] = hfma2_u32(lop3_and_or(v, 0x000F000Fu, H2_1024), sl8, al8);
+      a[2] = hfma2_u32(lop3_and_or(ws, 0x000F000Fu, H2_1024), slg, alg);
+      a[3] = hfma2_u32(lop3_and_or(vs, 0x000F000Fu, H2_1024), sl8, al8);
+      mma_f16_16816(P, a, j ? xl.z : xl.x, j ? xl.w : xl.y);
+      a[0] = hfma2_u32(lop3_and_or(w, 0x00F000F0u, H2_1024), mhg, ahg);
+      a[1] = hfma2_u32(lop3_and_or(v, 0x00F000F0u, H2_1024), mh8, ah8);
+      a[2] = hfma2_u32(lop3_and_or(ws, 0x00F000F0u, H2_1024), mhg, ahg);
+      a[3] = hfma2_u32(lop3_and_or(vs, 0x00F000F0u, H2_1024), mh8, ah8);
+      mma_f16_16816(P, a, j ? xh.z : xh.x, j ? xh.w : xh.y);
+    }
+  }
+  // min term: Cm[row, col] = sum_j m_j * (Sx_hi + Sx_lo)[col, j]
+  float Cm[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
+    const uint32_t mg = hsub2_u32(prmt((t < 2) ? m03g : m47g, 0x64u, sel), H2_1024);
+    const uint32_t m8 = hsub2_u32(prmt((t < 2) ? m038 : m478, 0x64u, sel), H2_1024);
+    uint32_t a[4] = {mg, m8, mg, m8};
+    uint32_t b0 = 0, b1 = 0;
+    if (colok) {
+      b0 = sxcol[sb * 8 + t];
+      b1 = sxcol[sb * 8 + 4 + t];
+    }
+    mma_f16_16816(Cm, a, b0, b1);
+  }
+  acc[0] = fmaf(-dmg, Cm[0], fmaf(dg, P[0], acc[0]));
+  acc[1] = fmaf(-dmg, Cm[1], fmaf(dg, P[1], acc[1]));
+  acc[2] = fmaf(-dm8, Cm[2], fmaf(d8, P[2], acc[2]));
+  acc[3] = fmaf(-dm8, Cm[3], fmaf(d8, P[3], acc[3]));
+}
+
+__device__ __forceinline__ void unit_q6k(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol, bool colok,
+                                         int sb, int t, float (&acc)[4]) {
+  const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg + 208));
+  const float d8 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg8 + 208));
+  const int8_t* scg = reinterpret_cast<const int8_t*>(rg + 192);
+  const int8_t* sc8 = reinterpret_cast<const int8_t*>(rg8 + 192);
+  const uint8_t* xb = xcol + 2 * (sb * 256 + 4 * t);
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+    for (int lh = 0; lh < 2; ++lh) {
+      const int off = 16 * lh + 4 * t;
+      const uint32_t qa = lds_u32_any(rg + 64 * hf + off), qb = lds_u32_any(rg + 64 * hf + 32 + off);
+      const uint32_t qh = lds_u32_any(rg + 128 + 32 * hf + off);
+      const uint32_t ra = lds_u32_any(rg8 + 64 * hf + off), rb = lds_u32_any(rg8 + 64 * hf + 32 + off);
+      const uint32_t rh = lds_u32_any(rg8 + 128 + 32 * hf + off);
+      uint32_t cg[4], c8[4];
+      cg[0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
+      cg[1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
+      cg[2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
+      cg[3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+      c8[0] = (ra & 0x0F0F0F0Fu) | ((rh << 4) & 0x30303030u);
+      c8[1] = (rb & 0x0F0F0F0Fu) | ((rh << 2) & 0x30303030u);
+      c8[2] = ((ra >> 4) & 0x0F0F0F0Fu) | (rh & 0x30303030u);
+      c8[3] = ((rb >> 4) & 0x0F0F0F0Fu) | ((rh >> 2) & 0x30303030u);
+#pragma unroll
+      for (int qi = 0; qi < 4; ++qi) {
+        const int grp = 8 * hf + 2 * qi + lh;
+        uint32_t a[4];
+        a[0] = hsub2_u32(lop3_and_or(cg[qi], 0x003F003Fu, H2_1024), H2_1056);
+        a[1] = hsub2_u32(lop3_and_or(c8[qi], 0x003F003Fu, H2_1024), H2_1056);
+        a[2] = hsub2_u32(lop3_and_or(cg[qi] >> 8, 0x003F003Fu, H2_1024), H2_1056);
+        a[3] = hsub2_u32(lop3_and_or(c8[qi] >> 8, 0x003F003Fu, H2_1024), H2_1056);
+        uint2 xv = make_uint2(0, 0);
+        if (colok) xv = *reinterpret_cast<const uint2*>(xb + 2 * (128 * hf + 32 * qi + 16 * lh));
+        float P[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_f16_16816(P, a, xv.x, xv.y);
+        const float sg = __fmul_rn(dg, static_cast<float>(scg[grp]));
+        const float s8 = __fmul_rn(d8, static_cast<float>(sc8[grp]));
+        acc[0] = fmaf(sg, P[0], acc[0]);
+        acc[1] = fmaf(sg, P[1], acc[1]);
+        acc[2] = fmaf(s8, P[2], acc[2]);
+        acc[3] = fmaf(s8, P[3], acc[3]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void unit_q80(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol, bool colok,
+                                         int sb, int t, float (&acc)[4]) {
+  const uint8_t* xb = xcol + 2 * (sb * 256 + 4 * t);
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const uint8_t* bg = rg + 34 * b;
+    const uint8_t* b8 = rg8 + 34 * b;
+    const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(bg));
+    const float d8 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(b8));
+    float P[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2) {
+      const uint32_t u = lds_u32_any(bg + 2 + 16 * j2 + 4 * t) ^ 0x80808080u;
+      const uint32_t v = lds_u32_any(b8 + 2 + 16 * j2 + 4 * t) ^ 0x80808080u;
+      uint32_t a[4];
+      a[0] = hsub2_u32(prmt(u, 0x64u, 0x4240u), H2_1152);
+      a[1] = hsub2_u32(prmt(v, 0x64u, 0x4240u), H2_1152);
+      a[2] = hsub2_u32(prmt(u, 0x64u, 0x4341u), H2_1152);
+      a[3] = hsub2_u32(prmt(v, 0x64u, 0x4341u), H2_1152);
+      uint2 xv = make_uint2(0, 0);
+      if (colok) xv = *reinterpret_cast<const uint2*>(xb + 2 * (32 * b + 16 * j2));
+      mma_f16_16816(P, a, xv.x, xv.y);
+    }
+    acc[0] = fmaf(dg, P[0], acc[0]);
+    acc[1] = fmaf(dg, P[1], acc[1]);
+    acc[2] = fmaf(d8, P[2], acc[2]);
+    acc[3] = fmaf(d8, P[3], acc[3]);
+  }
+}
+
+__device__ __forceinline__ void unit_f16(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol, bool colok,
+                                         int sb, int t, float (&acc)[4]) {
+  const uint8_t* xb = xcol + 2 * (sb * 256 + 4 * t);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint2 wg = *reinterpret_cast<const uint2*>(rg + 2 * (16 * i + 4 * t));
+    const uint2 w8 = *reinterpret_cast<const uint2*>(rg8 + 2 * (16 * i + 4 * t));
+    uint32_t a[4] = {wg.x, w8.x, wg.y, w8.y};
+    uint2 xv = make_uint2(0, 0);
+    if (colok) xv = *reinterpret_cast<const uint2*>(xb + 2 * (16 * i));
+    mma_f16_16816(acc, a, xv.x, xv.y);
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int WT, int XT, int EPI>
+struct GemvGeom {
+  static constexpr int RPT = (EPI == EPI_SWIGLU) ? 8 : 16;  // matrix rows per tile
+  static constexpr int UB = unit_bytes(WT);
+};
+
+template <int WT, int XT, int EPI>
+__device__ __forceinline__ const uint8_t* gemv_row_ptr(const GemvParams& p, int grp, int lt, int r) {
+  constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
+  const int e = p.group_ids ? p.group_ids[grp] : grp;
+  int n = lt * RPT + (EPI == EPI_SWIGLU ? (r & 7) : r);
+  n = n < p.N ? n : p.N - 1;
+  const uint8_t* base = (EPI == EPI_SWIGLU && r >= 8) ? p.w1 : p.w0;
+  return base + static_cast<int64_t>(e) * p.expert_stride + static_cast<int64_t>(n) * p.row_bytes;
+}
+
+__device__ __forceinline__ int cta_of_unit(int64_t u, int64_t U, int G) {
+  return static_cast<int>(((u + 1) * G - 1) / U);
+}
+
+template <int WT, int XT, int EPI>
+__device__ void gemv_epilogue(const GemvParams& p, const int* misc, int grp, int lt, const float (&v)[4], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  uint16_t* y = p.y + static_cast<int64_t>(grp) * p.y_group_stride;
+  if (EPI == EPI_STORE) {
+    const int n0 = lt * 16 + g, n1 = n0 + 8;
+    if (XT == XT_BF16) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = 2 * t + h;
+        if (c < p.M) {
+          const float s = exp2i(misc[c]);
+          if (n0 < p.N) y[static_cast<int64_t>(c) * p.N + n0] = bf16_rne_bits(__fmul_rn(v[h], s));
+          if (n1 < p.N) y[static_cast<int64_t>(c) * p.N + n1] = bf16_rne_bits(__fmul_rn(v[2 + h], s));
+        }
+      }
+    } else {
+      if (t < p.M) {
+        const float s = exp2i(misc[2 * t]);
+        if (n0 < p.N) y[static_cast<int64_t>(t) * p.N + n0] = bf16_rne_bits(__fmul_rn(__fadd_rn(v[0], v[1]), s));
+        if (n1 < p.N) y[static_cast<int64_t>(t) * p.N + n1] = bf16_rne_bits(__fmul_rn(__fadd_rn(v[2], v[3]), s));
+      }
+    }
+  } else {  // EPI_SWIGLU: rows g = gate row n, g+8 = up row n; h = bf16(silu(bf16 g) * bf16 u)
+    const int n = lt * 8 + g;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = 2 * t + h;
+      if (c < p.M && n < p.N) {
+        const float s = exp2i(misc[c]);
+        const float gb = bf16_round_f(__fmul_rn(v[h], s));
+        const float ub = bf16_round_f(__fmul_rn(v[2 + h], s));
+        y[static_cast<int64_t>(c) * p.N + n] = bf16_rne_bits(__fmul_rn(glm_silu_bf(gb), ub));
+      }
+    }
+  }
+}
+
+template <int WT, int XT, int EPI>
+__device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int ncols) {
+  const int tid = threadIdx.x;  // consumer threads 0..255
+  constexpr int NT = GEMV_NCW * 32;
+  int* misc = reinterpret_cast<int*>(smem + L.off_misc);
+  float* red = reinterpret_cast<float*>(smem + L.off_red);
+  const int K = p.K, M = p.M;
+  const int64_t xo = static_cast<int64_t>(grp) * p.x_group_stride;
+  const float* xf = reinterpret_cast<const float*>(p.x) + xo;
+  const uint16_t* xh = reinterpret_cast<const uint16_t*>(p.x) + xo;
+  auto ldx = [&](int64_t i) -> float { return XT == XT_F32 ? xf[i] : bf16_bits_to_f32(xh[i]); };
+  // 1. per-token max |x| -> power-of-two prescale so that max * 2^-s lies in [2^9, 2^10)
+  for (int m = 0; m < M; ++m) {
+    float mx = 0.f;
+    for (int k = tid; k < K; k += NT) mx = fmaxf(mx, fabsf(ldx(static_cast<int64_t>(m) * K + k)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = mx;
+  }
+  named_bar_sync(1, NT);
+  if (tid < M) {
+    float mx = 0.f;
+    for (int w = 0; w < GEMV_NCW; ++w) mx = fmaxf(mx, red[w * 8 + tid]);
+    int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
+    int s = (mx == 0.f) ? 0 : (e - 127 - 9);
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+    if (XT == XT_F32) {
+      misc[2 * tid] = s;
+      misc[2 * tid + 1] = s;
+    } else {
+      misc[tid] = s;
+    }
+  }
+  named_bar_sync(1, NT);
+  // 2. convert to fp16 columns (bf16: exact; fp32: hi + lo), with the per-type k order
+  constexpr bool swz = (WT != WT_F16);
+  uint8_t* xs = smem + L.off_xs;
+  for (int64_t i = tid; i < static_cast<int64_t>(M) * K; i += NT) {
+    const int m = static_cast<int>(i / K), k = static_cast<int>(i - static_cast<int64_t>(m) * K);
+    const float v = __fmul_rn(ldx(i), exp2i(-misc[XT == XT_F32 ? 2 * m : m]));
+    const __half hi = __float2half_rn(v);
+    const int kk = xswz(k, swz);
+    if (XT == XT_F32) {
+      const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+      reinterpret_cast<__half*>(xs + (2 * m) * p.xpitch)[kk] = hi;
+      reinterpret_cast<__half*>(xs + (2 * m + 1) * p.xpitch)[kk] = lo;
+    } else {
+      reinterpret_cast<__half*>(xs + m * p.xpitch)[kk] = hi;
+    }
+  }
+  if (WT == WT_Q4K) {
+    named_bar_sync(1, NT);
+    // 3. per-(column, 32-weight sub-block) activation sums, split hi/lo fp16
+    const int nsub = K / 32;
+    uint8_t* sxs = smem + L.off_sxs;
+    for (int it = tid; it < ncols * nsub; it += NT) {
+      const int c = it / nsub, sub = it - c * nsub;
+      const __half* col = reinterpret_cast<const __half*>(xs + c * p.xpitch) + sub * 32;
+      float s = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) s = __fadd_rn(s, __half2float(col[i]));
+      const __half hi = __float2half_rn(s);
+      const __half lo = __float2half_rn(__fsub_rn(s, __half2float(hi)));
+      __half* dst = reinterpret_cast<__half*>(sxs + (c * (K / 256) + sub / 8) * 32);
+      dst[sub & 7] = hi;
+      dst[8 + (sub & 7)] = lo;
+    }
+  }
+}
+
+template <int WT, int XT, int EPI>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
+  constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncols = (XT == XT_F32) ? 2 * p.M : p.M;
+  const GemvLayout L = gemv_layout(WT, ncols, p.K, p.nstages, p.pitch, p.xpitch);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + GEMV_MAXST;
+  int* misc = reinterpret_cast<int*>(smem + L.off_misc);
+  volatile int* abort_flag = misc + 32;
+  uint8_t* ring = smem + L.off_ring;
+  const int NST = p.nstages;
+  const int stage_bytes = 16 * p.pitch;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GEMV_NCW);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const bool dyn = (p.group_ids != nullptr) || (p.n_groups_dev != nullptr);
+  const int nsb = p.K >> 8;
+  const int tpg = (p.N + RPT - 1) / RPT;
+  const int G = gridDim.x, c = blockIdx.x;
+
+  if (warp == GEMV_NCW) {
+    // ---------------------------------------------------------------- producer warp
+    if (dyn) pdl_wait();
+    const int ngroups = p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups;
+    const int64_t U = static_cast<int64_t>(ngroups) * tpg * nsb;
+    const int64_t u0 = U * c / G, u1 = U * (c + 1) / G;
+    int i = 0;
+    for (int64_t u = u0; u < u1; ++i) {
+      const int tile = static_cast<int>(u / nsb), sb0 = static_cast<int>(u - static_cast<int64_t>(tile) * nsb);
+      const int len = static_cast<int>(min(static_cast<int64_t>(min(GEMV_KC, nsb - sb0)), u1 - u));
+      const int slot = i % NST;
+      if (i >= NST) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((i / NST) - 1) & 1, p.status, ST_TIMEOUT_EMPTY);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok || *abort_flag) break;
+      }
+      uint32_t bytes = 0;
+      const uint8_t* lo = nullptr;
+      if (lane < 16) {
+        const int grp = tile / tpg, lt = tile - grp * tpg;
+        const uint8_t* src = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, lane) + static_cast<int64_t>(sb0) * UB;
+        lo = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15));
+        const uint32_t head = static_cast<uint32_t>(src - lo);
+        bytes = (head + len * UB + 15u) & ~15u;
+      }
+      uint32_t total = bytes;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], total);
+      __syncwarp();
+      if (lane < 16) bulk_g2s(ring + slot * stage_bytes + lane * p.pitch, lo, bytes, &full[slot]);
+      u += len;
+    }
+    // never leave with copies in flight: wait for the last issued phase of every slot
+    if (lane == 0) {
+      for (int j = max(0, i - NST); j < i; ++j) mbar_wait_bounded(&full[j % NST], (j / NST) & 1, p.status, ST_TIMEOUT_FULL, 200u);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumer warps
+  pdl_wait();
+  const int ngroups = p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups;
+  const int64_t U = static_cast<int64_t>(ngroups) * tpg * nsb;
+  const int64_t u0 = U * c / G, u1 = U * (c + 1) / G;
+  const int g = lane >> 2, t = lane & 3;
+  const bool colok = g < ncols;
+  float* red = reinterpret_cast<float*>(smem + L.off_red);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int staged = -1;
+  int i = 0;
+  for (int64_t u = u0; u < u1; ++i) {
+    const int tile = static_cast<int>(u / nsb), sb0 = static_cast<int>(u - static_cast<int64_t>(tile) * nsb);
+    const int len = static_cast<int>(min(static_cast<int64_t>(min(GEMV_KC, nsb - sb0)), u1 - u));
+    const int grp = tile / tpg, lt = tile - grp * tpg;
+    if (grp != staged) {
+      named_bar_sync(1, GEMV_NCW * 32);
+      gemv_stage_x<WT, XT, EPI>(p, smem, L, grp, ncols);
+      named_bar_sync(1, GEMV_NCW * 32);
+      staged = grp;
+    }
+    const int slot = i % NST;
+    bool ok = !*abort_flag;
+    if (ok) {
+      ok = mbar_wait_bounded(&full[slot], (i / NST) & 1, p.status, ST_TIMEOUT_FULL);
+      if (!ok) *abort_flag = 1;
+    }
+    if (ok && warp < len) {
+      const int sb = sb0 + warp;
+      const uint8_t* st = ring + slot * stage_bytes;
+      const uint8_t* sg = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g) + static_cast<int64_t>(sb0) * UB;
+      const uint8_t* s8 = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g + 8) + static_cast<int64_t>(sb0) * UB;
+      const uint8_t* rg = st + g * p.pitch + (reinterpret_cast<uintptr_t>(sg) & 15u) + warp * UB;
+      const uint8_t* r8 = st + (g + 8) * p.pitch + (reinterpret_cast<uintptr_t>(s8) & 15u) + warp * UB;
+      const uint8_t* xcol = smem + L.off_xs + g * p.xpitch;
+      if (WT == WT_Q4K) {
+        const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + g * nsb * 32);
+        unit_q4k(rg, r8, xcol, sxcol, colok, sb, t, acc);
+      } else if (WT == WT_Q6K) {
+        unit_q6k(rg, r8, xcol, colok, sb, t, acc);
+      } else if (WT == WT_Q80) {
+        unit_q80(rg, r8, xcol, colok, sb, t, acc);
+      } else {
+        unit_f16(rg, r8, xcol, colok, sb, t, acc);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    u += len;
+    if (sb0 + len == nsb || u == u1) {
+      // ---------------- this CTA's segment of `tile` is done: reduce the warps in order
+      const int64_t seg0 = max(u0, static_cast<int64_t>(tile) * nsb);
+      const bool whole = (seg0 == static_cast<int64_t>(tile) * nsb) && (u == static_cast<int64_t>(tile + 1) * nsb);
+      *reinterpret_cast<float4*>(red + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      named_bar_sync(1, GEMV_NCW * 32);
+      if (warp == 0) {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < GEMV_NCW; ++w) {
+          const float4 r = *reinterpret_cast<const float4*>(red + (w * 32 + lane) * 4);
+          v[0] = __fadd_rn(v[0], r.x);
+          v[1] = __fadd_rn(v[1], r.y);
+          v[2] = __fadd_rn(v[2], r.z);
+          v[3] = __fadd_rn(v[3], r.w);
+        }
+        if (whole) {
+          gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, v, lane);
+        } else {
+          const int slot2 = (tile == static_cast<int>(u0 / nsb)) ? 0 : 1;
+          *reinterpret_cast<float4*>(p.partials + ((static_cast<int64_t>(c) * 2 + slot2) * 32 + lane) * 4) =
+              make_float4(v[0], v[1], v[2], v[3]);
+          __threadfence();
+          __syncwarp();
+          int old = 0;
+          if (lane == 0) old = atomicAdd(&p.counters[tile], 1);
+          old = __shfl_sync(0xffffffffu, old, 0);
+          const int cf = cta_of_unit(static_cast<int64_t>(tile) * nsb, U, G);
+          const int cl = cta_of_unit(static_cast<int64_t>(tile + 1) * nsb - 1, U, G);
+          if (old == cl - cf) {
+            __threadfence();
+            float w4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int cc = cf; cc <= cl; ++cc) {
+              const int s2 = (tile == static_cast<int>((U * cc / G) / nsb)) ? 0 : 1;
+              const float4 r = __ldcg(reinterpret_cast<const float4*>(
+                  p.partials + ((static_cast<int64_t>(cc) * 2 + s2) * 32 + lane) * 4));
+              w4[0] = __fadd_rn(w4[0], r.x);
+              w4[1] = __fadd_rn(w4[1], r.y);
+              w4[2] = __fadd_rn(w4[2], r.z);
+              w4[3] = __fadd_rn(w4[3], r.w);
+            }
+            gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, w4, lane);
+            if (lane == 0) p.counters[tile] = 0;
+          }
+        }
+      }
+      named_bar_sync(1, GEMV_NCW * 32);
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// ------------------------------------------------------------------ host launch
+template <int WT, int XT, int EPI>
+static int launch_one(GemvParams p, int grid, int smem, cudaStream_t stream, bool pdl) {
+  auto kern = gemv_kernel<WT, XT, EPI>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(gemv)");
+    attr_set[dev & 63] = true;
+  }
+  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(GEMV_THREADS), smem, stream, pdl, &p);
+}
+
+int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl) {
+  const int ncols = (xt == XT_F32) ? 2 * p.M : p.M;
+  if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ncols > 8) return set_error(-1, "gemv: bad shape");
+  if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
+  p.pitch = gemv_stage_pitch(wt);
+  const int xb = p.K * 2;
+  p.xpitch = ((xb + 127) & ~127) + 64;
+  GemvLayout L0 = gemv_layout(wt, ncols, p.K, 0, p.pitch, p.xpitch);
+  const int per_stage = 16 * p.pitch;
+  int nst = (232448 - L0.off_ring) / per_stage;
+  if (nst > GEMV_MAXST) nst = GEMV_MAXST;
+  if (nst < 2) return set_error(-1, "gemv: activation block too large for shared memory");
+  p.nstages = nst;
+  const int smem = gemv_layout(wt, ncols, p.K, nst, p.pitch, p.xpitch).total;
+  const int rpt = (epi == EPI_SWIGLU) ? 8 : 16;
+  const int64_t U = static_cast<int64_t>(p.n_groups) * ((p.N + rpt - 1) / rpt) * (p.K / 256);
+  int grid = static_cast<int>(std::min<int64_t>(num_sms, U));
+  if (grid < 1) grid = 1;
+#define AIPU_GEMV_CASE(W, X, E)                                              \
+  if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, smem, stream, pdl);
+  AIPU_GEMV_CASE(WT_Q4K, XT_BF16, EPI_STORE)
+  AIPU_GEMV_CASE(WT_Q4K, XT_F32, EPI_STORE)
+  AIPU_GEMV_CASE(WT_Q6K, XT_BF16, EPI_STORE)
+  AIPU_GEMV_CASE(WT_Q6K, XT_F32, EPI_STORE)
+  AIPU_GEMV_CASE(WT_Q80, XT_BF16, EPI_STORE)
+  AIPU_GEMV_CASE(WT_Q80, XT_F32, EPI_STORE)
+  AIPU_GEMV_CASE(WT_F16, XT_BF16, EPI_STORE)
+  AIPU_GEMV_CASE(WT_F16, XT_F32, EPI_STORE)
+  AIPU_GEMV_CASE(WT_Q4K, XT_BF16, EPI_SWIGLU)
+  AIPU_GEMV_CASE(WT_Q6K, XT_BF16, EPI_SWIGLU)
+#undef AIPU_GEMV_CASE
+  return set_error(-1, "gemv: unsupported weight/activation type combination");
+}
+
+int gemv_partials_floats(int num_sms) { return num_sms * 2 * 128; }
+
+}  // namespace aipu

@@ -1,0 +1,73 @@
+// Decode-time dequant GEMV / small-M GEMM for B200 (sm_100a).
+//
+//   y[m, n] = bf16( sum_k x[m, k] * w[n, k] ),   w stored as GGUF rows (Q4_K / Q6_K / Q8_0 / F16)
+//
+// Contract followed: tools/q4k_ref.py:67-92 (exact ggml dequant, fp32 MAC, bf16 RNE out). The MAC
+// order differs from the reference's sequential K order (this kernel is within 1 bf16 ulp; the
+// strict kernel in strict.cu is the bit-exact one).
+//
+// Design (HBM-bound: ~0.56 B/weight for Q4_K, so the budget is ~3 thread-ops per weight):
+//   * Persistent grid, one CTA per SM: 8 consumer warps + 1 producer warp.
+//   * Work unit = 16 weight rows x 256 weights (one super-block column). The units of all tiles are
+//     laid end to end and split evenly over the CTAs ("stream-K"); a tile cut between CTAs is
+//     finished by the last CTA to arrive, which sums the partials in CTA order (deterministic).
+//   * The producer streams each chunk (16 rows x up to 8 units) with 1-D bulk copies
+//     (cp.async.bulk, the untiled TMA path; no multicast) into a multi-stage shared-memory ring,
+//     completion tracked by mbarriers. Weights do not depend on the previous kernel, so with
+//     programmatic dependent launch the ring fills before griddepcontrol.wait.
+//   * Consumers turn packed codes into exact fp16 operands with LOP3/PRMT magic-number tricks and
+//     use mma.sync m16n8k16 (fp16 in, fp32 accumulate) as an exact-product dot engine: weight rows
+//     are the 16 MMA rows, activation columns (tokens, or hi/lo halves of fp32 tokens) the 8 MMA
+//     columns.
+//   * Activations are staged once per CTA as fp16 with a per-token power-of-two prescale (exact
+//     for bf16 input; fp32 input is split into hi + lo fp16 columns).
+//   * Q4_K: A = sc*q (exact in fp16, <= 945), so one fp32 accumulator per super-block, then
+//     acc += d*P - dmin*Cm, where Cm = sum_j m_j * sum_{k in j} x_k comes from one more MMA with
+//     A = m (6-bit mins) and B = per-sub-block activation sums (hi/lo fp16).
+#pragma once
+#include "act.cuh"
+#include "common.cuh"
+
+namespace aipu {
+
+constexpr int GEMV_NCW = 8;                       // consumer warps
+constexpr int GEMV_THREADS = (GEMV_NCW + 1) * 32;
+constexpr int GEMV_KC = GEMV_NCW;                 // units per stage (one per consumer warp)
+constexpr int GEMV_MAXST = 16;
+
+enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1 };
+
+struct GemvParams {
+  const uint8_t* w0;         // rows of the matrix (or the gate rows for EPI_SWIGLU)
+  const uint8_t* w1;         // up rows (EPI_SWIGLU)
+  int64_t row_bytes;         // bytes per row
+  int64_t expert_stride;     // bytes between consecutive experts of w0/w1
+  const int* group_ids;      // device: expert id of each group, or nullptr (group g = expert g)
+  const int* n_groups_dev;   // device: number of groups, or nullptr (use n_groups)
+  int n_groups;              // number of groups (upper bound when n_groups_dev is set)
+  int N;                     // rows per matrix
+  int K;                     // reduction length (multiple of 256)
+  const void* x;             // activations [M, K] (fp32 or bf16), group g at x + g*x_group_stride
+  int64_t x_group_stride;    // elements
+  int M;                     // tokens (<= 8 bf16, <= 4 fp32)
+  uint16_t* y;               // bf16 out [M, N] per group (EPI_SWIGLU: h [M, N])
+  int64_t y_group_stride;    // elements
+  float* partials;           // stream-K workspace [grid][2][32][4]
+  int* counters;             // stream-K arrival counters, one per tile, zero between launches
+  int* status;               // device status word
+  int pitch;                 // shared-memory row pitch of a stage
+  int nstages;               // ring depth
+  int xpitch;                // shared-memory bytes per activation column
+};
+
+__host__ __device__ inline int gemv_stage_pitch(int wt) {
+  int p0 = ((GEMV_KC * unit_bytes(wt) + 16) + 15) & ~15;
+  return p0 + (((32 - p0 % 128) % 128) + 128) % 128;  // pitch = 32 mod 128 (bank spread)
+}
+
+// ---------------------------------------------------------------------------------- x staging
+// Q4_K/Q6_K/Q8_0 operands are built as pairs (k0,k2) and (k1,k3) of every aligned group of four
+// weights, so the activation columns are stored with the same order (0,2,1,3) in each group.
+__device__ __forceinline__ int xswz(int k, bool swz) { return swz ? ((k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1)) : k; }
+
+}  // namespace aipu

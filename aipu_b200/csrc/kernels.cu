@@ -1,0 +1,293 @@
+// Exact (bit-for-bit) kernels: dequant, strict sequential GEMM, strict router with sigmoid
+// top-K, and the MoE weighted combine. Each follows the reference golden op for op.
+#include <cstdio>
+
+#include "act.cuh"
+#include "deq.cuh"
+#include "kernels.h"
+#include "launch.h"
+
+namespace aipu {
+
+// ------------------------------------------------------------------ dequant
+// out[r, k] = exact dequant of weight k of row r (fp32, or bf16 RNE of that fp32)
+__global__ void dequant_kernel(int wt, const uint8_t* __restrict__ w, int64_t nrows, int64_t K, int64_t row_bytes,
+                               void* __restrict__ out, int out_bf16) {
+  const int64_t total = nrows * K;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / K, k = i - r * K;
+    const float v = deq_one(wt, w + r * row_bytes, k);
+    if (out_bf16)
+      reinterpret_cast<uint16_t*>(out)[i] = bf16_rne_bits(v);
+    else
+      reinterpret_cast<float*>(out)[i] = v;
+  }
+}
+
+int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, int out_bf16, cudaStream_t s) {
+  const int64_t total = nrows * K;
+  if (total <= 0) return OK;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 65536) blocks = 65536;
+  dequant_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(wt, static_cast<const uint8_t*>(w), nrows, K,
+                                                          row_bytes_of(wt, K), out, out_bf16);
+  return set_cuda_error(cudaGetLastError(), "dequant_kernel");
+}
+
+// ------------------------------------------------------------------ strict GEMM
+// y[m, n] = bf16( sequential fp32 sum_k fmul(x[m,k], w[n,k]) ), the reference's exact contract
+// (tools/q4k_ref.py:86-92). 32 rows per block, one thread per (row, token); weights of a 256-wide
+// K chunk are dequantised exactly into shared memory, then every thread runs its own chain.
+constexpr int STRICT_ROWS = 32;
+__global__ void strict_gemm_kernel(int wt, const uint8_t* __restrict__ w, int64_t row_bytes, int N, int K,
+                                   const void* __restrict__ x, int xt, int M, uint16_t* __restrict__ y,
+                                   float* __restrict__ y_f32) {
+  __shared__ float ws[STRICT_ROWS][257];
+  const int r = threadIdx.x & 31;
+  const int mloc = threadIdx.x >> 5;
+  const int m = blockIdx.y * 8 + mloc;
+  const int n = blockIdx.x * STRICT_ROWS + r;
+  const int nthr = blockDim.x;
+  float acc = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 256) {
+    const int kl = min(256, K - k0);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < STRICT_ROWS * kl; idx += nthr) {
+      const int rr = idx / kl, kk = idx - rr * kl;
+      const int nn = blockIdx.x * STRICT_ROWS + rr;
+      ws[rr][kk] = (nn < N) ? deq_one(wt, w + static_cast<int64_t>(nn) * row_bytes, k0 + kk) : 0.f;
+    }
+    __syncthreads();
+    if (m < M) {
+      const int64_t xo = static_cast<int64_t>(m) * K + k0;
+      for (int kk = 0; kk < kl; ++kk) {
+        const float xv = (xt == XT_F32) ? __ldg(reinterpret_cast<const float*>(x) + xo + kk)
+                                        : bf16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(x) + xo + kk));
+        acc = __fadd_rn(acc, __fmul_rn(xv, ws[r][kk]));
+      }
+    }
+  }
+  if (m < M && n < N) {
+    if (y) y[static_cast<int64_t>(m) * N + n] = bf16_rne_bits(acc);
+    if (y_f32) y_f32[static_cast<int64_t>(m) * N + n] = acc;
+  }
+}
+
+int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,
+                       cudaStream_t s) {
+  if (N <= 0 || M <= 0 || K <= 0) return OK;
+  const int mb = M < 8 ? M : 8;
+  dim3 grid((N + STRICT_ROWS - 1) / STRICT_ROWS, (M + 7) / 8);
+  strict_gemm_kernel<<<grid, 32 * mb, 0, s>>>(wt, static_cast<const uint8_t*>(w), row_bytes_of(wt, K), N, K, x, xt,
+                                              M, y, y_f32);
+  return set_cuda_error(cudaGetLastError(), "strict_gemm_kernel");
+}
+
+// ------------------------------------------------------------------ strict router
+// Stage 1 (one warp per 32 experts per token): logit = bf16(sequential fp32 chain) exactly as
+// moe_router's matmul_q4k (tools/glm_model_q4k_ref.py:667-668), gate = bf16 glm sigmoid.
+// Stage 2 (the last warp to finish a token): top-K by (order key of gate [+ bias], lower index
+// wins ties), balanced add tree, Quake rsqrt^2 renormalisation x SCALE (glm_model_q4k_ref.py:669-681).
+// Stage 3 (the last token to finish): the sorted union of selected experts over all tokens and
+// each (token, slot)'s index into it, for the grouped expert GEMVs and the combine.
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+
+__device__ void router_topk_token(const RouterParams& p, int m) {
+  const int lane = threadIdx.x & 31;
+  const int E = p.E, T = p.topk;
+  constexpr int MAXPL = 32;  // E <= 1024
+  unsigned long long key[MAXPL];
+  const int per = (E + 31) / 32;
+  for (int j = 0; j < MAXPL; ++j) {
+    key[j] = 0ull;
+    const int e = j * 32 + lane;
+    if (j < per && e < E) {
+      const float gate = bf16_bits_to_f32(__ldcg(p.gate + static_cast<int64_t>(m) * E + e));
+      const float score = p.bias ? __fadd_rn(gate, __ldg(p.bias + e)) : gate;
+      key[j] = (static_cast<unsigned long long>(f32_order_key(score)) << 32) | static_cast<uint32_t>(0x7FFFFFFF - e);
+    }
+  }
+  float win[16];
+  int sel[16];
+  for (int s = 0; s < T; ++s) {
+    unsigned long long best = 0ull;
+    for (int j = 0; j < per; ++j) best = key[j] > best ? key[j] : best;
+    best = warp_max_u64(best);
+    const int e = 0x7FFFFFFF - static_cast<int>(best & 0xFFFFFFFFull);
+    for (int j = 0; j < per; ++j)
+      if (key[j] == best) key[j] = 0ull;
+    sel[s] = e;
+    win[s] = bf16_bits_to_f32(__ldcg(p.gate + static_cast<int64_t>(m) * E + e));
+  }
+  if (lane == 0) {
+    // balanced fp32 add tree of ceil(log2 T) levels, +0 padded (glm_model_q4k_ref.py:691-699)
+    float node[16];
+    int lev = 1;
+    while ((1 << lev) < T) ++lev;
+    const int npow = 1 << lev;
+    for (int i = 0; i < npow; ++i) node[i] = i < T ? win[i] : 0.f;
+    for (int l = 0, n = npow; l < lev; ++l, n >>= 1)
+      for (int i = 0; i < n / 2; ++i) node[i] = __fadd_rn(node[2 * i], node[2 * i + 1]);
+    const float rr = quake_rsqrt(node[0]);
+    const float rs = __fmul_rn(__fmul_rn(rr, rr), p.scale);
+    for (int s = 0; s < T; ++s) {
+      p.sel[m * T + s] = sel[s];
+      p.sel_w[m * T + s] = bf16_rne_bits(__fmul_rn(win[s], rs));
+    }
+  }
+}
+
+__device__ void router_union(const RouterParams& p) {
+  // one warp: mark selected experts, emit them in ascending expert order
+  const int lane = threadIdx.x & 31;
+  const int T = p.topk, M = p.M;
+  __shared__ uint32_t mask[32];
+  mask[lane] = 0u;
+  __syncwarp();
+  for (int i = lane; i < M * T; i += 32) {
+    const int e = __ldcg(p.sel + i);
+    atomicOr(&mask[e >> 5], 1u << (e & 31));
+  }
+  __syncwarp();
+  // prefix counts over the 32 mask words
+  const uint32_t mw = mask[lane];
+  int cnt = __popc(mw), pre = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int v = __shfl_up_sync(0xffffffffu, pre, o);
+    if (lane >= o) pre += v;
+  }
+  const int base = pre - cnt;
+  int idx = base;
+  for (int b = 0; b < 32; ++b)
+    if (mw & (1u << b)) p.union_ids[idx++] = lane * 32 + b;
+  if (lane == 31) *p.n_union = pre;
+  __syncwarp();
+  for (int i = lane; i < M * T; i += 32) {
+    const int e = __ldcg(p.sel + i);
+    const int wd = e >> 5, bit = e & 31;
+    // rank of e = (count of set bits in words < wd) + popcount(mask[wd] & ((1<<bit)-1))
+    int rank = 0;
+    for (int w2 = 0; w2 < wd; ++w2) rank += __popc(mask[w2]);
+    rank += __popc(mask[wd] & ((1u << bit) - 1u));
+    p.slot_map[i] = rank;
+  }
+}
+
+__global__ void __launch_bounds__(32) router_strict_kernel(const RouterParams p) {
+  pdl_wait();
+  const int lane = threadIdx.x;
+  const int e = blockIdx.x * 32 + lane;
+  const int m = blockIdx.y;
+  const int K = p.K, E = p.E;
+  float acc = 0.f;
+  if (e < E) {
+    const int64_t xo = static_cast<int64_t>(m) * K;
+    if (p.wt == WT_F32) {
+      // dense fp32 router stored [K, E] (x @ W): coalesced across the warp at every k
+      const float* W = reinterpret_cast<const float*>(p.w);
+#pragma unroll 4
+      for (int k = 0; k < K; ++k) {
+        const float xv = bf16_bits_to_f32(__ldg(p.x + xo + k));
+        acc = __fadd_rn(acc, __fmul_rn(xv, __ldg(W + static_cast<int64_t>(k) * E + e)));
+      }
+    } else {
+      const uint8_t* row = p.w + static_cast<int64_t>(e) * row_bytes_of(p.wt, K);
+      for (int k = 0; k < K; ++k) {
+        const float xv = bf16_bits_to_f32(__ldg(p.x + xo + k));
+        acc = __fadd_rn(acc, __fmul_rn(xv, deq_one(p.wt, row, k)));
+      }
+    }
+    const float logit = bf16_round_f(acc);
+    p.gate[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(glm_sigmoid_bf(logit));
+    if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
+  }
+  // last warp of this token does the selection; the last token does the union
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = (atomicAdd(&p.counters[m], 1) == static_cast<int>(gridDim.x) - 1);
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  if (lane == 0) p.counters[m] = 0;
+  router_topk_token(p, m);
+  __threadfence();
+  __syncwarp();
+  int lastm = 0;
+  if (lane == 0) lastm = (atomicAdd(&p.counters[p.M], 1) == p.M - 1);
+  lastm = __shfl_sync(0xffffffffu, lastm, 0);
+  if (!lastm) return;
+  __threadfence();
+  if (lane == 0) p.counters[p.M] = 0;
+  if (p.union_ids) router_union(p);
+  pdl_launch_dependents();
+}
+
+int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
+  if (p.E <= 0 || p.E > 1024 || p.topk <= 0 || p.topk > 16 || p.topk > p.E || p.M <= 0)
+    return set_error(EINVAL_, "router: need 1 <= topk <= min(16, E), E <= 1024");
+  RouterParams q = p;
+  return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel), dim3((p.E + 31) / 32, p.M), dim3(32), 0,
+                       s, pdl, &q);
+}
+
+// ------------------------------------------------------------------ combine
+// out[m, d] = bf16( (sum over slots in slot order of fmul(w_slot, y_slot[d])) + y_shared[d] )
+// (tools/glm_model_q4k_ref.py:799-809)
+__global__ void combine_kernel(const CombineParams p) {
+  pdl_wait();
+  const int64_t total = static_cast<int64_t>(p.M) * p.H;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / p.H);
+    const int d = static_cast<int>(i - static_cast<int64_t>(m) * p.H);
+    float facc = 0.f;
+    for (int s = 0; s < p.topk; ++s) {
+      const int u = p.slot_map[m * p.topk + s];
+      const float wv = bf16_bits_to_f32(p.sel_w[m * p.topk + s]);
+      const float yv = bf16_bits_to_f32(p.y_union[(static_cast<int64_t>(u) * p.M + m) * p.H + d]);
+      facc = __fadd_rn(facc, __fmul_rn(wv, yv));
+    }
+    if (p.y_shared) facc = __fadd_rn(facc, bf16_bits_to_f32(p.y_shared[i]));
+    p.out[i] = bf16_rne_bits(facc);
+  }
+  pdl_launch_dependents();
+}
+
+int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl) {
+  const int64_t total = static_cast<int64_t>(p.M) * p.H;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 4096) blocks = 4096;
+  CombineParams q = p;
+  return launch_kernel(reinterpret_cast<const void*>(combine_kernel), dim3(blocks), dim3(256), 0, s, pdl, &q);
+}
+
+// ------------------------------------------------------------------ activations
+// out[i] = bf16 glm sigmoid (kind 0) or glm silu (kind 1) of bf16 x[i]
+__global__ void act_kernel(int kind, const uint16_t* __restrict__ x, int64_t n, uint16_t* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float v = bf16_bits_to_f32(x[i]);
+    out[i] = bf16_rne_bits(kind == 0 ? glm_sigmoid_bf(v) : glm_silu_bf(v));
+  }
+}
+
+int act_launch(int kind, const void* x, int64_t n, void* out, cudaStream_t s) {
+  if (n <= 0) return OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 8192) blocks = 8192;
+  act_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(kind, static_cast<const uint16_t*>(x), n,
+                                                      static_cast<uint16_t*>(out));
+  return set_cuda_error(cudaGetLastError(), "act_kernel");
+}
+
+}  // namespace aipu

@@ -1,0 +1,45 @@
+// Launch prototypes and parameter blocks of the exact kernels and the decode GEMV.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace aipu {
+
+struct GemvParams;
+
+struct RouterParams {
+  int wt;                  // WT_F32: dense router [K, E]; WT_Q4K/Q6K/Q80/F16: GGUF rows [E, K]
+  const uint8_t* w;
+  const float* bias;       // [E] fp32, selection only (nullable)
+  const uint16_t* x;       // bf16 [M, K]
+  int M, K, E, topk;
+  float scale;             // renormalisation scale (the reference uses 2.5)
+  uint16_t* gate;          // bf16 [M, E] sigmoid gates (scratch and output)
+  uint16_t* logits;        // bf16 [M, E] (nullable)
+  int32_t* sel;            // [M, topk] selected experts, slot order
+  uint16_t* sel_w;         // bf16 [M, topk] routing weights
+  int32_t* union_ids;      // [<= M*topk] sorted union of selected experts (nullable)
+  int32_t* n_union;        // [1]
+  int32_t* slot_map;       // [M, topk] index of sel[m, s] in union_ids
+  int* counters;           // [M + 1] arrival counters, zero between launches
+};
+
+struct CombineParams {
+  int M, H, topk;
+  const int32_t* slot_map;  // [M, topk]
+  const uint16_t* sel_w;    // bf16 [M, topk]
+  const uint16_t* y_union;  // bf16 [U, M, H]
+  const uint16_t* y_shared; // bf16 [M, H] (nullable)
+  uint16_t* out;            // bf16 [M, H]
+};
+
+int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, int out_bf16, cudaStream_t s);
+int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,
+                       cudaStream_t s);
+int router_launch(const RouterParams& p, cudaStream_t s, bool pdl);
+int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl);
+int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl);
+int gemv_partials_floats(int num_sms);
+int act_launch(int kind, const void* x, int64_t n, void* out, cudaStream_t s);
+
+}  // namespace aipu

@@ -1,0 +1,23 @@
+// Host-side helpers shared by the launchers: thread-local error text and kernel launch with
+// optional programmatic dependent launch (PDL).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace aipu {
+
+// status codes returned by every C entry point (mirrored in include/aipu_q4k.h)
+enum : int { OK = 0, EINVAL_ = -1, ECUDA_ = -2, ETIMEOUT_ = -3, ENCCL_ = -4, ENOMEM_ = -5 };
+
+int set_error(int code, const char* msg);
+int set_cuda_error(cudaError_t e, const char* where);
+const char* last_error();
+
+// Launch `kern` with the given configuration. When `pdl` is true the launch carries
+// cudaLaunchAttributeProgrammaticStreamSerialization, so it may start while the previous kernel on
+// the stream drains; kernels call griddepcontrol.wait before touching inputs that the previous
+// kernel produces.
+int launch_kernel(const void* kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, bool pdl, void* arg0);
+
+int num_sms_of_current_device();
+
+}  // namespace aipu

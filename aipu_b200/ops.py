@@ -1,0 +1,209 @@
+"""Torch-tensor front end of the C ABI. Tensors are only the boundary: every call goes straight to
+``libaipu_q4k.so`` on the current CUDA stream. There is no CPU path; CPU tensors are rejected.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+from ._lib import check, lib
+
+_DTYPE = {torch.float32: L.DT_F32, torch.bfloat16: L.DT_BF16}
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("aipu_b200 runs on CUDA tensors only (no CPU fallback)")
+        if t is not None and not t.is_contiguous():
+            raise ValueError("aipu_b200 needs contiguous tensors")
+
+
+def row_bytes(wtype: int, K: int) -> int:
+    n = lib().aipu_row_bytes(wtype, K)
+    if n <= 0:
+        raise ValueError(f"K={K} is not a whole number of blocks of type {wtype}")
+    return n
+
+
+class Context:
+    """Per-device workspace (stream-K partials, MoE scratch, side stream) owned by the library."""
+
+    _default: dict = {}
+
+    def __init__(self, device: int | torch.device | None = None):
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("Context needs a CUDA device")
+        self.device = dev
+        h = ctypes.c_void_p()
+        check(lib().aipu_ctx_create(ctypes.byref(h), dev.index if dev.index is not None else 0))
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().aipu_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_flags(self, pdl: bool = False) -> "Context":
+        """pdl=True: fast GEMMs start streaming weights while the previous kernel drains (only when no
+        kernel right before a GEMM writes its weights)."""
+        check(lib().aipu_ctx_set_flags(self.handle, L.FLAG_PDL if pdl else 0))
+        return self
+
+    def status(self) -> int:
+        v = ctypes.c_int()
+        check(lib().aipu_ctx_status(self.handle, ctypes.byref(v)))
+        return v.value
+
+    @classmethod
+    def default(cls, device: torch.device) -> "Context":
+        key = device.index if device.index is not None else torch.cuda.current_device()
+        if key not in cls._default:
+            cls._default[key] = Context(torch.device("cuda", key))
+        return cls._default[key]
+
+
+def dequant(wtype: int, w: torch.Tensor, nrows: int, K: int, out_dtype=torch.float32) -> torch.Tensor:
+    """Exact dequantisation of ``nrows`` GGUF rows of K weights -> [nrows, K] fp32 (or bf16 RNE)."""
+    _need_cuda(w)
+    if w.numel() * w.element_size() < nrows * row_bytes(wtype, K):
+        raise ValueError("weight buffer smaller than nrows * row_bytes")
+    out = torch.empty((nrows, K), dtype=out_dtype, device=w.device)
+    check(lib().aipu_q4k_dequant(wtype, _ptr(w), nrows, K, _ptr(out), _DTYPE[out_dtype], _stream(w.device)))
+    return out
+
+
+def act(kind: str, x: torch.Tensor) -> torch.Tensor:
+    """bf16 glm sigmoid (kind "sigmoid") or SiLU (kind "silu") of a bf16 tensor."""
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("act needs bf16 input")
+    out = torch.empty_like(x)
+    check(lib().aipu_act_eval({"sigmoid": 0, "silu": 1}[kind], _ptr(x), x.numel(), _ptr(out), _stream(x.device)))
+    return out
+
+
+def gemm(wtype: int, w: torch.Tensor, N: int, K: int, x: torch.Tensor, mode: str = "fast",
+         ctx: Optional[Context] = None, out: Optional[torch.Tensor] = None,
+         out_f32: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[M, N] bf16 = x[M, K] (fp32 or bf16) x W^T, W = N GGUF rows of K weights."""
+    _need_cuda(w, x, out, out_f32)
+    if x.dim() != 2 or x.shape[1] != K:
+        raise ValueError("x must be [M, K]")
+    if w.numel() * w.element_size() < N * row_bytes(wtype, K):
+        raise ValueError("weight buffer smaller than N * row_bytes")
+    ctx = ctx or Context.default(w.device)
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=w.device)
+    m = L.MODE_STRICT if mode == "strict" else L.MODE_FAST
+    check(lib().aipu_q4k_gemm(ctx.handle, wtype, _ptr(w), N, K, _ptr(x), _DTYPE[x.dtype], M, _ptr(out),
+                              _ptr(out_f32), m, _stream(w.device)))
+    return out
+
+
+def moe_router(router_wtype: int, w: torch.Tensor, x: torch.Tensor, n_experts: int, topk: int,
+               bias: Optional[torch.Tensor] = None, scale: float = 2.5, ctx: Optional[Context] = None,
+               want_logits: bool = False):
+    """Strict router: returns (sel int32 [M, topk], sel_w bf16 [M, topk], gate bf16 [M, E][, logits])."""
+    _need_cuda(w, x, bias)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("router activations must be bf16")
+    M, K = x.shape
+    ctx = ctx or Context.default(x.device)
+    sel = torch.empty((M, topk), dtype=torch.int32, device=x.device)
+    sw = torch.empty((M, topk), dtype=torch.bfloat16, device=x.device)
+    gate = torch.empty((M, n_experts), dtype=torch.bfloat16, device=x.device)
+    logits = torch.empty((M, n_experts), dtype=torch.bfloat16, device=x.device) if want_logits else None
+    check(lib().aipu_moe_router(ctx.handle, router_wtype, _ptr(w), _ptr(bias), _ptr(x), M, K, n_experts, topk,
+                                scale, _ptr(sel), _ptr(sw), _ptr(gate), _ptr(logits), _stream(x.device)))
+    return (sel, sw, gate, logits) if want_logits else (sel, sw, gate)
+
+
+@dataclass
+class MoeLayerWeights:
+    """Device weights of one MoE layer (experts back to back in one uint8 tensor per projection)."""
+
+    hidden: int
+    ffn: int
+    n_experts: int
+    topk: int
+    router_wtype: int
+    router_w: torch.Tensor
+    gate_w: torch.Tensor
+    up_w: torch.Tensor
+    down_w: torch.Tensor
+    gate_wtype: int = L.Q4_K
+    down_wtype: int = L.Q6_K
+    router_bias: Optional[torch.Tensor] = None
+    shared_gate_w: Optional[torch.Tensor] = None
+    shared_up_w: Optional[torch.Tensor] = None
+    shared_down_w: Optional[torch.Tensor] = None
+    scale: float = 2.5
+
+    def cstruct(self) -> L.MoeWeights:
+        s = L.MoeWeights()
+        s.hidden, s.ffn, s.n_experts, s.topk, s.scale = self.hidden, self.ffn, self.n_experts, self.topk, self.scale
+        s.router_wtype = self.router_wtype
+        s.router_w = self.router_w.data_ptr()
+        s.router_bias = self.router_bias.data_ptr() if self.router_bias is not None else None
+        s.gate_wtype = s.up_wtype = self.gate_wtype
+        s.down_wtype = self.down_wtype
+        s.gate_w, s.up_w, s.down_w = self.gate_w.data_ptr(), self.up_w.data_ptr(), self.down_w.data_ptr()
+        if self.shared_gate_w is not None:
+            s.shared_gate_w = self.shared_gate_w.data_ptr()
+            s.shared_up_w = self.shared_up_w.data_ptr()
+            s.shared_down_w = self.shared_down_w.data_ptr()
+        return s
+
+
+def moe_layer(W: MoeLayerWeights, x: torch.Tensor, ctx: Optional[Context] = None, out: Optional[torch.Tensor] = None,
+              return_routing: bool = False):
+    """MoE branch on bf16 rows x[M, H] -> bf16 [M, H] (router, union of experts, SwiGLU, combine)."""
+    _need_cuda(x, out)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("MoE activations must be bf16")
+    M = x.shape[0]
+    ctx = ctx or Context.default(x.device)
+    if out is None:
+        out = torch.empty((M, W.hidden), dtype=torch.bfloat16, device=x.device)
+    sel = sw = None
+    if return_routing:
+        sel = torch.empty((M, W.topk), dtype=torch.int32, device=x.device)
+        sw = torch.empty((M, W.topk), dtype=torch.bfloat16, device=x.device)
+    cs = W.cstruct()
+    check(lib().aipu_moe_layer(ctx.handle, ctypes.byref(cs), _ptr(x), M, _ptr(out), _ptr(sel), _ptr(sw),
+                               _stream(x.device)))
+    return (out, sel, sw) if return_routing else out
+
+
+def swiglu_expert(gate_wtype: int, gate_w: torch.Tensor, up_w: torch.Tensor, down_wtype: int, down_w: torch.Tensor,
+                  H: int, F: int, x: torch.Tensor, ctx: Optional[Context] = None, return_hidden: bool = False):
+    """One SwiGLU expert on bf16 rows x[M, H] -> y bf16 [M, H] (and h bf16 [M, F])."""
+    _need_cuda(gate_w, up_w, down_w, x)
+    M = x.shape[0]
+    ctx = ctx or Context.default(x.device)
+    h = torch.empty((M, F), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    check(lib().aipu_swiglu_expert(ctx.handle, gate_wtype, _ptr(gate_w), gate_wtype, _ptr(up_w), down_wtype,
+                                   _ptr(down_w), H, F, _ptr(x), M, _ptr(h), _ptr(y), _stream(x.device)))
+    return (y, h) if return_hidden else y

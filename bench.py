@@ -1,0 +1,368 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 k-quant decode path. Prints ONE JSON line (rank 0).
+
+Headline metric: Q4_K GEMV HBM GB/s on the BASELINE config-2 shape (2048 rows x 6144, bf16 x,
+M = 1). A step is one pass over a batch of `--matrices` distinct weight matrices (1.8 GB by default,
+far larger than the 126 MB L2, so no L2 flush is needed), one GEMV launch per matrix, replayed as a
+CUDA graph with programmatic dependent launch. value = algorithmic bytes (weights + x + y) of all
+GEMVs of all ranks / device time (max over ranks).
+
+Also reported: roofline of the GEMV kernel against MEASURED_PEAKS.json, the CPU baseline (the C
+restatement of the reference's contract on the host cores), the end-to-end number through the public
+API with host buffers, SM clocks sampled through NVML during the timed region, and the MoE-layer
+decode throughput of BASELINE config 3 (1 GPU).
+
+--impl reference times the reference's CPU implementation of the path (its C restatement, all host
+threads) on the same config and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_ROWS, K_COLS = 2048, 6144
+GEMV_W_BYTES = N_ROWS * (K_COLS // 256) * 144            # 7,077,888
+GEMV_BYTES = GEMV_W_BYTES + K_COLS * 2 + N_ROWS * 2       # + x bf16 + y bf16 = 7,094,272
+METRIC = "Q4_K GEMV HBM GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="aipu", choices=["aipu", "reference"])
+    ap.add_argument("--matrices", type=int, default=256, help="distinct weight matrices per step")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def traffic_from_profile():
+    """dram bytes per launch of the GEMV kernel from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "gemv_q4k_2048x6144.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":")[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.reasons = set()
+        self._stop = threading.Event()
+        self.ok = False
+        self.max_mhz = None
+
+    def __enter__(self):
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.ok = True
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception:
+            self.ok = False
+        return self
+
+    def _run(self):
+        nv = self.nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in names.items():
+                    if r & bit:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.ok:
+            self.t.join(timeout=1)
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def cpu_baseline_gemv(seconds=10.0, w=None, x=None):
+    """The C restatement on all host cores: full 2048 x 6144 Q4_K GEMVs for ~`seconds`."""
+    import numpy as np
+
+    from aipu_b200 import formats as F
+    from oracle import cpu
+
+    if w is None:
+        w = F.random_rows_np(F.Q4_K, N_ROWS, K_COLS, seed=0)
+        x = np.random.default_rng(0).standard_normal((1, K_COLS)).astype(np.float32)
+    cores = os.cpu_count() or 1
+    cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return {"value": round(GEMV_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{n} full Q4_K GEMVs 2048x6144 (M=1) by oracle/q4k_oracle.c, {cores} threads, {dt:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation of the path (C restatement), rank 0 only."""
+    import numpy as np
+
+    from aipu_b200 import formats as F
+    from oracle import cpu
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cores = os.cpu_count() or 1
+    w = F.random_rows_np(F.Q4_K, N_ROWS, K_COLS, seed=0)
+    x = np.random.default_rng(0).standard_normal((1, K_COLS)).astype(np.float32)
+    for _ in range(max(args.warmup, 1)):
+        cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+    dt = time.perf_counter() - t0
+    v = GEMV_BYTES * args.steps / dt / 1e9
+    line = {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "Q4_K GEMV 2048x6144, x bf16-valued fp32 [1,6144], y bf16 (BASELINE config 2, "
+                                   "Q4_K, M=1)", "step": "one GEMV"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} GEMVs, oracle/q4k_oracle.c (restatement of tools/q4k_ref.py)"},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def moe_decode(M_list=(1, 4), reps=200):
+    """BASELINE config 3 on one GPU: tokens/s of the MoE layer (CUDA graph replays)."""
+    import numpy as np
+    import torch
+
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    H, Fd, E, T = 6144, 2048, 256, 8
+    W = ops.MoeLayerWeights(
+        hidden=H, ffn=Fd, n_experts=E, topk=T, router_wtype=F.F32,
+        router_w=torch.randn((H, E), device=d, generator=torch.Generator(device=d).manual_seed(1)) * 0.02,
+        router_bias=torch.randn((E,), device=d, generator=torch.Generator(device=d).manual_seed(2)) * 0.01,
+        gate_w=F.random_rows_dev(F.Q4_K, E * Fd, H, seed=11, device=d),
+        up_w=F.random_rows_dev(F.Q4_K, E * Fd, H, seed=12, device=d),
+        down_w=F.random_rows_dev(F.Q6_K, E * H, Fd, seed=13, device=d),
+        shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=14, device=d),
+        shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=15, device=d),
+        shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
+    ctx = ops.Context(d)
+    out = {}
+    expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
+    for M in M_list:
+        x = (torch.randn((M, H), device=d, generator=torch.Generator(device=d).manual_seed(100 + M))).to(torch.bfloat16)
+        y = torch.empty((M, H), dtype=torch.bfloat16, device=d)
+        _, sel, _ = ops.moe_layer(W, x, ctx=ctx, out=y, return_routing=True)
+        torch.cuda.synchronize()
+        union = len(set(sel.cpu().numpy().reshape(-1).tolist()))
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            ops.moe_layer(W, x, ctx=ctx, out=y)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                ops.moe_layer(W, x, ctx=ctx, out=y)
+        for _ in range(10):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / reps / 1e3
+        byts = H * E * 4 + (union + 1) * expert_bytes
+        out[f"M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(M / t, 1), "union_experts": union,
+                        "hbm_bytes": byts, "hbm_gbs": round(byts / t / 1e9, 1)}
+    del W
+    torch.cuda.empty_cache()
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import numpy as np
+    import torch
+
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    world, rank, local = dist_setup(args.gpus)
+    d = torch.device("cuda", torch.cuda.current_device())
+    L = args.matrices
+    Wt = F.random_rows_dev(F.Q4_K, L * N_ROWS, K_COLS, seed=1234 + rank, device=d)
+    rb = F.row_bytes(F.Q4_K, K_COLS)
+    mats = [Wt[l * N_ROWS:(l + 1) * N_ROWS] for l in range(L)]
+    x = torch.randn((1, K_COLS), device=d, generator=torch.Generator(device=d).manual_seed(7)).to(torch.bfloat16)
+    y = torch.empty((L, 1, N_ROWS), dtype=torch.bfloat16, device=d)
+    ctx = ops.Context(d).set_flags(pdl=True)
+
+    def issue():
+        for l in range(L):
+            ops.gemm(F.Q4_K, mats[l], N_ROWS, K_COLS, x, ctx=ctx, out=y[l])
+
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        issue()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            issue()
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(d.index) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        tt = torch.tensor([t], device=d, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+        dist.barrier()
+    step = t / args.steps
+    value = world * L * GEMV_BYTES / step / 1e9
+    per_launch = step / L
+    hbm_peak, _, peak_kind = peaks()
+    achieved = GEMV_BYTES / per_launch / 1e9
+
+    # ---- end to end through the public API with host buffers (x in, all y out, every step)
+    x_host = torch.empty((1, K_COLS), dtype=torch.bfloat16, pin_memory=True).copy_(x.cpu())
+    y_host = torch.empty((L, 1, N_ROWS), dtype=torch.bfloat16, pin_memory=True)
+    e2e_steps = max(10, args.steps // 4)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            x.copy_(x_host, non_blocking=True)
+            g.replay()
+            y_host.copy_(y, non_blocking=True)
+        s.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            g.replay()
+            y_host.copy_(y, non_blocking=True)
+        s.synchronize()
+        te = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([te], device=d, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        te = float(tt.item())
+    e2e = {"value": round(world * L * GEMV_BYTES / te / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": K_COLS * 2, "d2h_bytes_per_step": L * N_ROWS * 2,
+           "path": "ops.gemm -> aipu_q4k_gemm (C ABI), replayed as a CUDA graph; pinned host x in, y out"}
+
+    del Wt, mats
+    torch.cuda.empty_cache()
+    moe = None
+    if rank == 0 and world == 1 and not args.no_moe:
+        moe = moe_decode()
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu_base = cpu_baseline_gemv()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "Q4_K GEMV 2048x6144, x bf16 [1,6144] ~N(0,1), y bf16 (BASELINE config 2, Q4_K, "
+                                   "M=1)", "matrices_per_step": L, "bytes_per_gemv": GEMV_BYTES,
+                       "l2": f"inputs larger than L2: {L * GEMV_W_BYTES / 1e9:.2f} GB of distinct weights per step",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic_from_profile(),
+                         "peak_source": peak_kind, "kernel": "gemv_kernel<Q4_K,bf16,store>",
+                         "us_per_launch": round(per_launch * 1e6, 3)},
+            "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": L * args.steps,
+            "clocks": clk.summary(), "moe_decode": moe,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,148 @@
+/* aipu_q4k.h -- C ABI of the B200 (sm_100a) k-quant dequant-GEMM and MoE library.
+ *
+ * Every function returns an int status (AIPU_OK = 0, negative on error) and never throws; the
+ * text of the last error on the calling thread is available from aipu_last_error(). All device
+ * pointers are caller-owned CUDA device memory; `stream` is a cudaStream_t (NULL = legacy default
+ * stream). Calls are asynchronous on `stream` and do not synchronise.
+ *
+ * Weight layout: GGUF/ggml blocks, one weight row (= one output column of the contraction) is a
+ * contiguous run of blocks along K, rows stored back to back:
+ *   Q4_K 144 B / 256 weights, Q6_K 210 B / 256, Q8_0 34 B / 32, F16 2 B, F32 4 B.
+ * Weight buffers must start on a 16-byte boundary and stay readable up to the next 16-byte boundary
+ * after their last byte (the bulk copies move whole 16-byte chunks).
+ *
+ * Numeric contract (Wick-Lim/AIPU tools/q4k_ref.py:67-92): weights dequantised exactly as ggml,
+ * products accumulated in fp32, output rounded to bf16 (round to nearest even).
+ *   AIPU_MODE_FAST   tensor-core dot products, within 1 bf16 ulp of the sequential reference
+ *   AIPU_MODE_STRICT sequential fp32 chain in K order, bit-identical to the reference
+ */
+#ifndef AIPU_Q4K_H
+#define AIPU_Q4K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AIPU_OK 0
+#define AIPU_EINVAL (-1)   /* bad shape, type or pointer */
+#define AIPU_ECUDA (-2)    /* a CUDA runtime call failed */
+#define AIPU_ETIMEOUT (-3) /* a bounded device-side wait gave up (device status word set) */
+#define AIPU_ENCCL (-4)    /* an NCCL call failed */
+#define AIPU_ENOMEM (-5)   /* workspace allocation failed */
+
+/* weight types; values match the reference's w_type selector (src/glm_matmul_q4k.v:76-92) */
+#define AIPU_Q4_K 0
+#define AIPU_Q6_K 1
+#define AIPU_Q8_0 2
+#define AIPU_F16 3
+#define AIPU_F32 4
+
+/* activation / output dtypes */
+#define AIPU_DT_F32 0
+#define AIPU_DT_BF16 1
+
+#define AIPU_MODE_FAST 0
+#define AIPU_MODE_STRICT 1
+
+typedef struct aipu_ctx aipu_ctx;
+
+/* library version (major*10000 + minor*100 + patch) */
+int aipu_version(void);
+/* text of the last error raised on this thread ("" if none) */
+const char* aipu_last_error(void);
+/* bytes of one weight row of K weights of type `wtype` (0 if K is not a multiple of the block) */
+int64_t aipu_row_bytes(int wtype, int64_t K);
+
+/* A context owns the per-device workspace (stream-K partials and counters, MoE scratch) and a side
+ * stream. One context per (device, concurrently used stream). The first MoE call sizes its scratch
+ * (cudaMalloc), so make it once before capturing a CUDA graph. */
+int aipu_ctx_create(aipu_ctx** ctx, int device);
+int aipu_ctx_destroy(aipu_ctx* ctx);
+/* Context flags.
+ * AIPU_FLAG_PDL: launch the fast GEMM with programmatic dependent launch, so its weight stream
+ * starts while the previous kernel on the stream is still running (activations are read only after
+ * that kernel completes). Set it only when no kernel just before the GEMM writes the weights. */
+#define AIPU_FLAG_PDL 1
+int aipu_ctx_set_flags(aipu_ctx* ctx, int flags);
+/* device status word of the context (0 = no bounded wait ever gave up); resets it to 0 */
+int aipu_ctx_status(aipu_ctx* ctx, int* status);
+
+/* Exact dequantisation of `nrows` rows of K weights to fp32 (out_dtype AIPU_DT_F32) or bf16
+ * (AIPU_DT_BF16, RNE of the exact fp32). Bit-identical to the reference.
+ * Replaces: tools/q4k_ref.py:39-65 dequantize_block_q4_K / dequantize_row_q4_K,
+ *           tools/q4k_ref.py:105-124 dequantize_block_q6_K, tools/q4k_ref.py:126-129
+ *           dequantize_block_q8_0, and the ggml dequant CLI tools/dequant_dump.c:11-33. */
+int aipu_q4k_dequant(int wtype, const void* w, int64_t nrows, int64_t K, void* out, int out_dtype, void* stream);
+
+/* Elementwise glm activation on bf16 values: kind 0 = sigmoid, 1 = SiLU (x * sigmoid(x)), bf16 out.
+ * Degree-5 Horner exp, Quake-rsqrt^2 reciprocal, +-16 clamp; bit-identical to the reference.
+ * Replaces: tools/glm_model_q4k_ref.py:293-299 glm_sigmoid / glm_silu (src/glm_act.v). */
+int aipu_act_eval(int kind, const void* x, int64_t n, void* out, void* stream);
+
+/* y[M, N] (bf16) = x[M, K] (fp32 or bf16, row-major) x W[N rows, K]^T.
+ * FAST mode: K a multiple of 256, any M (internally blocks of 8 bf16 / 4 fp32 tokens), any N.
+ * STRICT mode: any K that is a whole number of blocks; y_f32 (nullable) also receives the fp32
+ * accumulator before rounding.
+ * Replaces: tools/q4k_ref.py:86-92 matmul_q4k_col, tools/glm_model_q4k_ref.py:470-472
+ *           matmul_q4k, and the GEMM core src/glm_matmul_q4k.v:50-288 (PE_M token rows). */
+int aipu_q4k_gemm(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype,
+                  int64_t M, void* y, float* y_f32, int mode, void* stream);
+
+/* MoE router on M bf16 token rows x[M, K]:
+ *   logits = bf16(sequential fp32 x . w_e) for every expert e  (strict, bit-exact)
+ *   gate   = bf16 glm sigmoid(logits)
+ *   select top-`topk` by gate (+ bias[e] in fp32 when bias != NULL; selection only), lower expert
+ *   index wins ties; weights = bf16(gate_i * rsqrt(s)^2 * scale), s = balanced sum of the winners.
+ * router_wtype AIPU_F32: w is fp32 [K, E] (x @ W); otherwise GGUF rows [E, K].
+ * Outputs: sel int32 [M, topk] (slot 0 = largest), sel_w bf16 [M, topk], gate bf16 [M, E]
+ * (nullable), logits bf16 [M, E] (nullable).
+ * Replaces: tools/glm_model_q4k_ref.py:663-681 moe_router (src/moe_router_q4k.v,
+ *           src/topk_select.v). The bias is an extension (absent in the reference). */
+int aipu_moe_router(aipu_ctx* ctx, int router_wtype, const void* w, const float* bias, const void* x, int64_t M,
+                    int64_t K, int64_t E, int topk, float scale, int32_t* sel, void* sel_w, void* gate, void* logits,
+                    void* stream);
+
+/* Weights of one MoE layer. Routed experts: gate/up [E][F rows][row bytes of H] and
+ * down [E][H rows][row bytes of F], experts back to back (stride = rows * row bytes). */
+typedef struct aipu_moe_weights {
+  int64_t hidden;        /* H */
+  int64_t ffn;           /* F */
+  int64_t n_experts;     /* E */
+  int32_t topk;
+  float scale;           /* routing-weight scale (2.5 in the reference) */
+  int32_t router_wtype;  /* AIPU_F32 ([H, E]) or a GGUF type ([E, H]) */
+  const void* router_w;
+  const float* router_bias; /* nullable */
+  int32_t gate_wtype, up_wtype, down_wtype;
+  const void* gate_w;
+  const void* up_w;
+  const void* down_w;
+  const void* shared_gate_w; /* nullable: no shared expert */
+  const void* shared_up_w;
+  const void* shared_down_w;
+} aipu_moe_weights;
+
+/* y[M, H] (bf16) = MoE branch of the decoder block on bf16 token rows x[M, H]:
+ * router (strict) -> per selected expert SwiGLU y_e = (silu(x Wg) * (x Wu)) Wd with bf16 rounding
+ * at each stage -> facc = sum over slots (slot order) of w_slot * y_e, + y_shared -> bf16.
+ * Each expert in the union of the M tokens' selections is streamed once for all M rows.
+ * Optional outputs (nullable): sel [M, topk], sel_w bf16 [M, topk].
+ * Replaces: tools/glm_model_q4k_ref.py:797-809 (decoder_block MoE branch) with
+ *           swiglu_expert :702-708 (src/glm_decoder_block_q4k.v, src/swiglu_expert_q4k.v). */
+int aipu_moe_layer(aipu_ctx* ctx, const aipu_moe_weights* wts, const void* x, int64_t M, void* y, int32_t* sel,
+                   void* sel_w, void* stream);
+
+/* One SwiGLU expert on bf16 rows x[M, H]: y[M, H] = bf16 rows of (silu(x Wg) * (x Wu)) Wd.
+ * h (nullable, bf16 [M, F]) receives the hidden activation.
+ * Replaces: tools/glm_model_q4k_ref.py:702-708 swiglu_expert (src/swiglu_expert_q4k.v). */
+int aipu_swiglu_expert(aipu_ctx* ctx, int gate_wtype, const void* gate_w, int up_wtype, const void* up_w,
+                       int down_wtype, const void* down_w, int64_t H, int64_t F, const void* x, int64_t M, void* h,
+                       void* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AIPU_Q4K_H */

@@ -1,0 +1,291 @@
+"""GPU parity of the CUDA path against the oracle and the reference fixtures.
+
+Bars (written here, checked below):
+  * dequant, activations, strict GEMM, router logits/gates/top-k indices/weights: bit-exact;
+  * fast GEMM, SwiGLU, MoE layer: >= 99.9 % of outputs within 1 bf16 ulp of the oracle and
+    max relative error <= 1e-2 with the denominator floored at 2^-8 * rms(reference row).
+"""
+import numpy as np
+import pytest
+import torch
+
+from aipu_b200 import formats as F
+from aipu_b200 import ops
+from oracle import moe_oracle as mo
+from oracle import q4k_oracle as qo
+
+pytestmark = pytest.mark.gpu
+
+F32 = np.float32
+TOL_FRAC_1ULP = 0.999
+TOL_MAX_REL = 1e-2
+
+
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def to_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev())
+
+
+def bf16_np(t: torch.Tensor) -> np.ndarray:
+    return (t.view(torch.int16).cpu().numpy().astype(np.uint16).astype(np.uint32) << 16).view(F32)
+
+
+def np_to_bf16_dev(x: np.ndarray) -> torch.Tensor:
+    bits = (np.asarray(x, F32).view(np.uint32) >> 16).astype(np.uint16)
+    return to_dev(bits.view(np.int16)).view(torch.bfloat16)
+
+
+def assert_close_bf16(got, ref, what=""):
+    st = qo.parity_stats(got, ref)
+    assert st["frac_within_1ulp"] >= TOL_FRAC_1ULP and st["max_rel"] <= TOL_MAX_REL, f"{what}: {st}"
+    return st
+
+
+# ------------------------------------------------------------------ dequant / activations
+@pytest.mark.parametrize("name,wt,bw", [("q4k", F.Q4_K, 256), ("q6k", F.Q6_K, 256), ("q80", F.Q8_0, 32)])
+def test_dequant_fixture_bitexact(golden, name, wt, bw):
+    g = golden("dequant_golden")
+    blocks = g[f"{name}_blocks"]
+    out = ops.dequant(wt, to_dev(blocks), blocks.shape[0], bw)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32).reshape(-1), g[f"{name}_y"].reshape(-1))
+
+
+def test_dequant_f16_all_patterns(golden):
+    g = golden("dequant_golden")
+    pats = g["f16_bits"]
+    n = pats.size - pats.size % 1
+    out = ops.dequant(F.F16, to_dev(pats.view(np.uint8)), 1, n)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32).reshape(-1), g["f16_y"])
+
+
+@pytest.mark.parametrize("wt", [F.Q4_K, F.Q6_K, F.Q8_0, F.F16])
+def test_dequant_random_rows_and_bf16_out(wt):
+    N, K = 37, 1024
+    w = F.random_rows_np(wt, N, K, seed=5 + wt)
+    ref = qo.dequant_rows(wt, w, N, K)
+    out = ops.dequant(wt, to_dev(w), N, K)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    outb = ops.dequant(wt, to_dev(w), N, K, out_dtype=torch.bfloat16)
+    assert np.array_equal(bf16_np(outb).view(np.uint32), qo.bf16_round(ref).view(np.uint32))
+
+
+def test_activations_all_bf16_patterns(golden):
+    g = golden("act_golden")
+    x = to_dev(np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.int16)).view(torch.bfloat16)
+    sig = ops.act("sigmoid", x).view(torch.int16).cpu().numpy().view(np.uint16)
+    silu = ops.act("silu", x).view(torch.int16).cpu().numpy().view(np.uint16)
+    assert np.array_equal(sig, g["sigmoid"])
+    assert np.array_equal(silu, g["silu"])
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("ci", range(10))
+def test_gemm_fixture_strict_bitexact_and_fast_close(golden, ci):
+    g = golden("gemm_golden")
+    wt, N, K, M = (int(v) for v in g[f"c{ci}_meta"])
+    x = g[f"c{ci}_x"].view(F32)
+    w = to_dev(g[f"c{ci}_w"])
+    xd = np_to_bf16_dev(x)
+    ys = ops.gemm(wt, w, N, K, xd, mode="strict")
+    assert np.array_equal(bf16_np(ys).view(np.uint32), g[f"c{ci}_y"])
+    if K % 256 == 0:
+        yf = ops.gemm(wt, w, N, K, xd, mode="fast")
+        assert_close_bf16(bf16_np(yf), g[f"c{ci}_y"].view(F32), f"case {ci}")
+
+
+def test_gemm_fp32_activations_fixture(golden):
+    g = golden("gemm_golden")
+    wt, N, K, M = (int(v) for v in g["f32x_meta"])
+    x = to_dev(g["f32x_x"].view(F32))
+    w = to_dev(g["f32x_w"])
+    ys = ops.gemm(wt, w, N, K, x, mode="strict")
+    assert np.array_equal(bf16_np(ys).view(np.uint32), g["f32x_y"])
+    yf = ops.gemm(wt, w, N, K, x, mode="fast")
+    assert_close_bf16(bf16_np(yf), g["f32x_y"].view(F32))
+
+
+def test_reference_generator_vectors(golden):
+    """tools/q4k_matmul_gen.py and tools/q4k_mixed_gen.py vectors: strict bit-exact, fast close."""
+    g = golden("refvec_golden")
+    for i in range(int(g["n_mm"])):
+        wt, N, K, M, _ = (int(v) for v in g[f"mm{i}_meta"])
+        xd = to_dev(g[f"mm{i}_a"].view(np.int16)).view(torch.bfloat16)
+        ys = ops.gemm(0, to_dev(g[f"mm{i}_w"]), N, K, xd, mode="strict")
+        assert np.array_equal(ys.view(torch.int16).cpu().numpy().view(np.uint16), g[f"mm{i}_c"]), i
+        yf = ops.gemm(0, to_dev(g[f"mm{i}_w"]), N, K, xd, mode="fast")
+        ud = qo.ulp_diff_bf16(bf16_np(yf), qo.bf16_from_bits(g[f"mm{i}_c"]))
+        assert ud.max() <= 1, (i, ud)
+    for t in range(int(g["n_mx"])):
+        K, PE_M, PE_N = (int(v) for v in g[f"mx{t}_meta"])
+        xd = to_dev(g[f"mx{t}_a"].view(np.int16)).view(torch.bfloat16)
+        for pj, wt in enumerate(g[f"mx{t}_types"]):
+            ys = ops.gemm(int(wt), to_dev(g[f"mx{t}_w{pj}"]), 1, K, xd, mode="strict")
+            assert np.array_equal(ys.view(torch.int16).cpu().numpy().view(np.uint16)[:, 0], g[f"mx{t}_c"][:, pj])
+            yf = ops.gemm(int(wt), to_dev(g[f"mx{t}_w{pj}"]), 1, K, xd, mode="fast")
+            ud = qo.ulp_diff_bf16(bf16_np(yf)[:, 0], qo.bf16_from_bits(g[f"mx{t}_c"][:, pj]))
+            assert ud.max() <= 1, (t, pj, ud)
+
+
+@pytest.mark.parametrize("wt", [F.Q4_K, F.Q6_K, F.Q8_0, F.F16])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+def test_gemm_fast_config2_shapes(wt, M):
+    """BASELINE config 2 (2048 x 6144, small M) and the speculative-verify M up to 8."""
+    N, K = 2048, 6144
+    w = F.random_rows_np(wt, N, K, seed=100 + wt)
+    rng = np.random.default_rng(7 + M)
+    x = qo.bf16_round(rng.standard_normal((M, K)).astype(F32))
+    ref = qo.gemm(wt, w, N, K, x)
+    y = ops.gemm(wt, to_dev(w), N, K, np_to_bf16_dev(x))
+    assert_close_bf16(bf16_np(y), ref, f"wt={wt} M={M}")
+
+
+def test_gemm_fast_config1_fp32_x():
+    """Q4_K 4096 x 4096, fp32 activations ~ N(0,1)."""
+    N = K = 4096
+    w = F.random_rows_np(F.Q4_K, N, K, seed=0)
+    x = np.random.default_rng(0).standard_normal((1, K)).astype(F32)
+    ref = qo.gemm(F.Q4_K, w, N, K, x)
+    y = ops.gemm(F.Q4_K, to_dev(w), N, K, to_dev(x))
+    assert_close_bf16(bf16_np(y), ref)
+
+
+@pytest.mark.parametrize("N,K", [(1, 256), (5, 256), (17, 512), (40, 2048), (300, 768), (16, 6144)])
+def test_gemm_fast_ragged_and_streamk_splits(N, K):
+    """Ragged N (partial tiles), tiny problems where one tile is cut across many CTAs."""
+    for wt in (F.Q4_K, F.Q6_K, F.Q8_0, F.F16):
+        w = F.random_rows_np(wt, N, K, seed=N + K + wt)
+        x = qo.bf16_round(np.random.default_rng(N).standard_normal((3, K)).astype(F32))
+        ref = qo.gemm(wt, w, N, K, x)
+        for _ in range(2):  # twice: arrival counters must be left at zero
+            y = ops.gemm(wt, to_dev(w), N, K, np_to_bf16_dev(x))
+            ud = qo.ulp_diff_bf16(bf16_np(y), ref)
+            assert ud.max() <= 2 and np.mean(ud <= 1) >= 0.99, (wt, N, K, ud.max())
+
+
+def test_gemm_edge_values():
+    """Zero activations give exact zeros; a zero-scale block contributes nothing; large |x|."""
+    N, K = 32, 512
+    w = F.random_rows_np(F.Q4_K, N, K, seed=3)
+    y0 = ops.gemm(F.Q4_K, to_dev(w), N, K, torch.zeros((2, K), dtype=torch.bfloat16, device=dev()))
+    assert torch.count_nonzero(y0.float()) == 0
+    w2 = w.copy().reshape(N, -1, 144)
+    w2[:, 0, 0:4] = 0  # d = dmin = 0 for the first super-block
+    w2 = w2.reshape(N, -1)
+    x = qo.bf16_round(np.random.default_rng(1).standard_normal((2, K)).astype(F32) * 1000.0)
+    ref = qo.gemm(F.Q4_K, w2, N, K, x)
+    y = ops.gemm(F.Q4_K, to_dev(w2), N, K, np_to_bf16_dev(x))
+    assert_close_bf16(bf16_np(y), ref)
+
+
+# ------------------------------------------------------------------ router / experts / layer
+@pytest.mark.parametrize("name", ["r8", "r256"])
+def test_router_reference_fixture_bitexact(golden, name):
+    g = golden("moe_golden")
+    E, T, D = (int(v) for v in g[f"{name}_meta"])
+    x = g[f"{name}_x"].view(F32)
+    xp = np.zeros((x.shape[0], 256), F32)
+    xp[:, :D] = x
+    sel, sw, gate = ops.moe_router(F.Q4_K, to_dev(g[f"{name}_w"]), np_to_bf16_dev(xp), E, T)
+    assert np.array_equal(sel.cpu().numpy(), g[f"{name}_sel"])
+    assert np.array_equal(bf16_np(sw).view(np.uint32), g[f"{name}_sw"])
+    assert np.array_equal(bf16_np(gate).view(np.uint32), g[f"{name}_gate"])
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_router_fp32_bias_config3_bitexact(M):
+    """BASELINE config 3 router: fp32 6144 x 256 ~ N(0, 0.02), bias ~ N(0, 0.01), top-8, x2.5."""
+    H, E, T = 6144, 256, 8
+    rng = np.random.default_rng(11 + M)
+    wr = rng.normal(0, 0.02, (H, E)).astype(F32)
+    bias = rng.normal(0, 0.01, E).astype(F32)
+    x = qo.bf16_round(rng.standard_normal((M, H)).astype(F32))
+    sel_r, sw_r, gate_r = mo.moe_router(x, wr.T.copy(), T, bias=bias)
+    sel, sw, gate, logits = ops.moe_router(F.F32, to_dev(wr), np_to_bf16_dev(x), E, T, bias=to_dev(bias),
+                                           want_logits=True)
+    assert np.array_equal(bf16_np(logits).view(np.uint32), mo.router_logits(x, wr.T.copy()).view(np.uint32))
+    assert np.array_equal(sel.cpu().numpy(), sel_r)
+    assert np.array_equal(bf16_np(sw).view(np.uint32), sw_r.view(np.uint32))
+    assert np.array_equal(bf16_np(gate).view(np.uint32), gate_r.view(np.uint32))
+
+
+def test_swiglu_expert_full_dims():
+    H, Fd, M = 6144, 2048, 2
+    wg = F.random_rows_np(F.Q4_K, Fd, H, seed=21)
+    wu = F.random_rows_np(F.Q4_K, Fd, H, seed=22)
+    wd = F.random_rows_np(F.Q6_K, H, Fd, seed=23)
+    x = qo.bf16_round(np.random.default_rng(3).standard_normal((M, H)).astype(F32))
+    g_ = qo.dequant_rows(F.Q4_K, wg, Fd, H)
+    u_ = qo.dequant_rows(F.Q4_K, wu, Fd, H)
+    d_ = qo.dequant_rows(F.Q6_K, wd, H, Fd)
+    h_ref = mo.swiglu_hidden(x, g_, u_)
+    y_ref = qo.matmul_seq(h_ref, d_)
+    y, h = ops.swiglu_expert(F.Q4_K, to_dev(wg), to_dev(wu), F.Q6_K, to_dev(wd), H, Fd, np_to_bf16_dev(x),
+                             return_hidden=True)
+    assert_close_bf16(bf16_np(h), h_ref, "h")
+    assert_close_bf16(bf16_np(y), y_ref, "y")
+
+
+def test_moe_layer_reference_fixture(golden):
+    """Reference decoder-block MoE branch (16 experts, top-4, shared expert) at H=256, F=128
+    (F padded to 256 with zero gate/up rows, which leave h and y unchanged)."""
+    g = golden("moe_golden")
+    E, T, D, Fd = (int(v) for v in g["moe_meta"])
+    Fp = 256
+    gate = np.zeros((E + 1, Fp, 144), np.uint8)
+    up = np.zeros((E + 1, Fp, 144), np.uint8)
+    gate[:, :Fd] = g["moe_gate_w"]
+    up[:, :Fd] = g["moe_up_w"]
+    down = g["moe_down_w"]  # [E+1, 256 rows, 144]: K=256 with codes beyond 128 padded
+    W = ops.MoeLayerWeights(hidden=D, ffn=Fp, n_experts=E, topk=T, router_wtype=F.Q4_K,
+                            router_w=to_dev(g["moe_router_w"]), gate_w=to_dev(gate[:E]), up_w=to_dev(up[:E]),
+                            down_w=to_dev(down[:E]), gate_wtype=F.Q4_K, down_wtype=F.Q4_K,
+                            shared_gate_w=to_dev(gate[E]), shared_up_w=to_dev(up[E]), shared_down_w=to_dev(down[E]))
+    x = g["moe_x"].view(F32)
+    y, sel, sw = ops.moe_layer(W, np_to_bf16_dev(x), return_routing=True)
+    assert np.array_equal(sel.cpu().numpy(), g["moe_sel"])
+    assert np.array_equal(bf16_np(sw).view(np.uint32), g["moe_sw"])
+    assert_close_bf16(bf16_np(y), g["moe_y"].view(F32), "moe layer")
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_moe_layer_config3(M):
+    """BASELINE config 3 at full size: H=6144, 256 experts + shared, F=2048, gate/up Q4_K, down Q6_K,
+    fp32 router + bias, top-8. Weights drawn on the device; the oracle dequantises only the
+    experts the router selected."""
+    d = dev()
+    H, Fd, E, T = 6144, 2048, 256, 8
+    gate = F.random_rows_dev(F.Q4_K, E * Fd, H, seed=1, device=d)
+    up = F.random_rows_dev(F.Q4_K, E * Fd, H, seed=2, device=d)
+    down = F.random_rows_dev(F.Q6_K, E * H, Fd, seed=3, device=d)
+    sg = F.random_rows_dev(F.Q4_K, Fd, H, seed=4, device=d)
+    su = F.random_rows_dev(F.Q4_K, Fd, H, seed=5, device=d)
+    sd = F.random_rows_dev(F.Q6_K, H, Fd, seed=6, device=d)
+    rng = np.random.default_rng(9 + M)
+    wr = rng.normal(0, 0.02, (H, E)).astype(F32)
+    bias = rng.normal(0, 0.01, E).astype(F32)
+    x = qo.bf16_round(rng.standard_normal((M, H)).astype(F32))
+    W = ops.MoeLayerWeights(hidden=H, ffn=Fd, n_experts=E, topk=T, router_wtype=F.F32, router_w=to_dev(wr),
+                            router_bias=to_dev(bias), gate_w=gate, up_w=up, down_w=down,
+                            shared_gate_w=sg, shared_up_w=su, shared_down_w=sd)
+    y, sel, sw = ops.moe_layer(W, np_to_bf16_dev(x), return_routing=True)
+    torch.cuda.synchronize()
+    gate_v = gate.view(E, Fd, -1)
+    up_v = up.view(E, Fd, -1)
+    down_v = down.view(E, H, -1)
+
+    def deq(e):
+        return (qo.dequant_rows(F.Q4_K, gate_v[e].cpu().numpy(), Fd, H),
+                qo.dequant_rows(F.Q4_K, up_v[e].cpu().numpy(), Fd, H),
+                qo.dequant_rows(F.Q6_K, down_v[e].cpu().numpy(), H, Fd))
+
+    shared = (qo.dequant_rows(F.Q4_K, sg.cpu().numpy(), Fd, H), qo.dequant_rows(F.Q4_K, su.cpu().numpy(), Fd, H),
+              qo.dequant_rows(F.Q6_K, sd.cpu().numpy(), H, Fd))
+    y_ref, sel_ref, sw_ref = mo.moe_layer(x, wr.T.copy(), deq, shared, T, bias=bias)
+    assert np.array_equal(sel.cpu().numpy(), sel_ref)
+    assert np.array_equal(bf16_np(sw).view(np.uint32), sw_ref.view(np.uint32))
+    assert_close_bf16(bf16_np(y), y_ref, f"moe M={M}")

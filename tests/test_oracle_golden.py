@@ -130,3 +130,30 @@ def test_moe_layer_reference(golden):
     assert np.array_equal(sel, g["moe_sel"])
     assert np.array_equal(bits(sw), g["moe_sw"])
     assert np.array_equal(bits(out), g["moe_y"])
+
+
+@pytest.mark.parametrize("ci", range(10))
+def test_c_oracle_matches_reference_fixtures(golden, ci):
+    """The C restatement (CPU baseline) is bit-exact to the reference too, for any thread count."""
+    from oracle import cpu
+
+    g = golden("gemm_golden")
+    wt, N, K, M = (int(v) for v in g[f"c{ci}_meta"])
+    x = g[f"c{ci}_x"].view(F32)
+    for nt in (1, 3):
+        y = cpu.gemm(wt, g[f"c{ci}_w"], N, K, x, nthreads=nt)
+        assert np.array_equal(bits(y), g[f"c{ci}_y"])
+    row = cpu.dequant_row(wt, g[f"c{ci}_w"][0], K)
+    assert np.array_equal(bits(row), g[f"c{ci}_wdeq"][0])
+
+
+def test_c_oracle_dequant_edge_blocks(golden):
+    from oracle import cpu
+
+    g = golden("dequant_golden")
+    for name, wt, bw in (("q4k", 0, 256), ("q6k", 1, 256), ("q80", 2, 32)):
+        blocks = g[f"{name}_blocks"]
+        y = np.stack([cpu.dequant_row(wt, b, bw) for b in blocks])
+        assert np.array_equal(bits(y), g[f"{name}_y"])
+    y = cpu.dequant_row(3, g["f16_bits"].view(np.uint8), g["f16_bits"].size)
+    assert np.array_equal(bits(y), g["f16_y"])
