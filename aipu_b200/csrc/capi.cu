@@ -261,6 +261,7 @@ extern "C" int aipu_moe_router(aipu_ctx* c, int wt, const void* w, const float* 
   p.sel = sel;
   p.sel_w = static_cast<uint16_t*>(sel_w);
   p.counters = c->router_counters;
+  p.status = c->status;
   int rc = router_launch(p, s, false);
   if (tmp) cudaFreeAsync(tmp, s);
   return rc;
@@ -399,6 +400,7 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
   rp.n_union = sc.n_union;
   rp.slot_map = sc.slot_map;
   rp.counters = c->router_counters;
+  rp.status = c->status;
   if ((rc = router_launch(rp, s, false))) return rc;
   const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
   rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F, sc.union_ids,

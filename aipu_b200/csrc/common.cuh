@@ -49,21 +49,26 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
-// Bounded wait: gives up after `limit` try_wait rounds (each suspends up to ~1 ms), sets the
-// status bit and returns false. No wait in this library can spin forever.
+// Bounded wait: gives up after `limit_cycles` SM clock cycles (~2 s by default), sets the status
+// bit and returns false. No wait in this library can spin forever.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int bit,
-                                                  uint32_t limit = 4000u) {
-  for (uint32_t i = 0; i < limit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  if (status) atomicOr(status, bit);
-  return false;
+                                                  long long limit_cycles = 4000000000LL) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > limit_cycles) {
+      if (status) atomicOr(status, bit);
+      return false;
+    }
+  }
+  return true;
 }
 
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (the untiled TMA path).

@@ -281,11 +281,35 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
   const int64_t xo = static_cast<int64_t>(grp) * p.x_group_stride;
   const float* xf = reinterpret_cast<const float*>(p.x) + xo;
   const uint16_t* xh = reinterpret_cast<const uint16_t*>(p.x) + xo;
-  auto ldx = [&](int64_t i) -> float { return XT == XT_F32 ? xf[i] : bf16_bits_to_f32(xh[i]); };
-  // 1. per-token max |x| -> power-of-two prescale so that max * 2^-s lies in [2^9, 2^10)
+  (void)xf;
+  (void)xh;
+  // 1. per-token max |x| -> power-of-two prescale so that max * 2^-s lies in [2^9, 2^10).
+  //    16-byte loads, several in flight per thread (x is read from L2 by every CTA).
+  constexpr int VEC = (XT == XT_F32) ? 4 : 8;  // elements per 16-byte vector
+  const int nv = K / VEC;
+  const uint4* xv = reinterpret_cast<const uint4*>(XT == XT_F32 ? static_cast<const void*>(xf)
+                                                                : static_cast<const void*>(xh));
+  auto vmax = [&](const uint4 q, float mx) -> float {
+    if (XT == XT_F32) {
+      mx = fmaxf(mx, fabsf(__uint_as_float(q.x)));
+      mx = fmaxf(mx, fabsf(__uint_as_float(q.y)));
+      mx = fmaxf(mx, fabsf(__uint_as_float(q.z)));
+      mx = fmaxf(mx, fabsf(__uint_as_float(q.w)));
+    } else {
+      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        mx = fmaxf(mx, fabsf(__uint_as_float(w4[i] << 16)));
+        mx = fmaxf(mx, fabsf(__uint_as_float(w4[i] & 0xFFFF0000u)));
+      }
+    }
+    return mx;
+  };
   for (int m = 0; m < M; ++m) {
     float mx = 0.f;
-    for (int k = tid; k < K; k += NT) mx = fmaxf(mx, fabsf(ldx(static_cast<int64_t>(m) * K + k)));
+    const uint4* row = xv + static_cast<int64_t>(m) * nv;
+#pragma unroll 4
+    for (int v = tid; v < nv; v += NT) mx = vmax(__ldg(row + v), mx);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = mx;
@@ -305,20 +329,55 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
     }
   }
   named_bar_sync(1, NT);
-  // 2. convert to fp16 columns (bf16: exact; fp32: hi + lo), with the per-type k order
+  // 2. convert to fp16 columns (bf16: exact; fp32: hi + lo), in the per-type k order. A 16-byte
+  //    vector covers whole aligned groups of four, so the reordering stays inside it.
   constexpr bool swz = (WT != WT_F16);
   uint8_t* xs = smem + L.off_xs;
-  for (int64_t i = tid; i < static_cast<int64_t>(M) * K; i += NT) {
-    const int m = static_cast<int>(i / K), k = static_cast<int>(i - static_cast<int64_t>(m) * K);
-    const float v = __fmul_rn(ldx(i), exp2i(-misc[XT == XT_F32 ? 2 * m : m]));
-    const __half hi = __float2half_rn(v);
-    const int kk = xswz(k, swz);
-    if (XT == XT_F32) {
-      const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-      reinterpret_cast<__half*>(xs + (2 * m) * p.xpitch)[kk] = hi;
-      reinterpret_cast<__half*>(xs + (2 * m + 1) * p.xpitch)[kk] = lo;
-    } else {
-      reinterpret_cast<__half*>(xs + m * p.xpitch)[kk] = hi;
+  for (int m = 0; m < M; ++m) {
+    const uint4* row = xv + static_cast<int64_t>(m) * nv;
+    const float sc = exp2i(-misc[XT == XT_F32 ? 2 * m : m]);
+#pragma unroll 4
+    for (int v = tid; v < nv; v += NT) {
+      const uint4 q = __ldg(row + v);
+      if (XT == XT_F32) {
+        const float f[4] = {__fmul_rn(__uint_as_float(q.x), sc), __fmul_rn(__uint_as_float(q.y), sc),
+                            __fmul_rn(__uint_as_float(q.z), sc), __fmul_rn(__uint_as_float(q.w), sc)};
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          hi[i] = __float2half_rn(f[i]);
+          lo[i] = __float2half_rn(__fsub_rn(f[i], __half2float(hi[i])));
+        }
+        const int o = swz ? 1 : 0;  // positions (0,2,1,3) within the group when swizzled
+        uint2 H, Lw;
+        H.x = static_cast<uint32_t>(__half_as_ushort(hi[0])) | (static_cast<uint32_t>(__half_as_ushort(hi[o ? 2 : 1])) << 16);
+        H.y = static_cast<uint32_t>(__half_as_ushort(hi[o ? 1 : 2])) | (static_cast<uint32_t>(__half_as_ushort(hi[3])) << 16);
+        Lw.x = static_cast<uint32_t>(__half_as_ushort(lo[0])) | (static_cast<uint32_t>(__half_as_ushort(lo[o ? 2 : 1])) << 16);
+        Lw.y = static_cast<uint32_t>(__half_as_ushort(lo[o ? 1 : 2])) | (static_cast<uint32_t>(__half_as_ushort(lo[3])) << 16);
+        *reinterpret_cast<uint2*>(xs + (2 * m) * p.xpitch + 8 * v) = H;
+        *reinterpret_cast<uint2*>(xs + (2 * m + 1) * p.xpitch + 8 * v) = Lw;
+      } else {
+        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+        uint16_t h[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          h[2 * i] = __half_as_ushort(__float2half_rn(__fmul_rn(__uint_as_float(w4[i] << 16), sc)));
+          h[2 * i + 1] = __half_as_ushort(__float2half_rn(__fmul_rn(__uint_as_float(w4[i] & 0xFFFF0000u), sc)));
+        }
+        uint4 o4;
+        if (swz) {
+          o4.x = h[0] | (static_cast<uint32_t>(h[2]) << 16);
+          o4.y = h[1] | (static_cast<uint32_t>(h[3]) << 16);
+          o4.z = h[4] | (static_cast<uint32_t>(h[6]) << 16);
+          o4.w = h[5] | (static_cast<uint32_t>(h[7]) << 16);
+        } else {
+          o4.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
+          o4.y = h[2] | (static_cast<uint32_t>(h[3]) << 16);
+          o4.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
+          o4.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
+        }
+        *reinterpret_cast<uint4*>(xs + m * p.xpitch + 16 * v) = o4;
+      }
     }
   }
   if (WT == WT_Q4K) {
@@ -381,7 +440,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams 
     int i = 0;
     for (int64_t u = u0; u < u1; ++i) {
       const int tile = static_cast<int>(u / nsb), sb0 = static_cast<int>(u - static_cast<int64_t>(tile) * nsb);
-      const int len = static_cast<int>(min(static_cast<int64_t>(min(GEMV_KC, nsb - sb0)), u1 - u));
+      const int len = static_cast<int>(min(static_cast<int64_t>(min(p.kc, nsb - sb0)), u1 - u));
       const int slot = i % NST;
       if (i >= NST) {
         bool ok = true;
@@ -408,7 +467,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams 
     }
     // never leave with copies in flight: wait for the last issued phase of every slot
     if (lane == 0) {
-      for (int j = max(0, i - NST); j < i; ++j) mbar_wait_bounded(&full[j % NST], (j / NST) & 1, p.status, ST_TIMEOUT_FULL, 200u);
+      for (int j = max(0, i - NST); j < i; ++j)
+        mbar_wait_bounded(&full[j % NST], (j / NST) & 1, p.status, ST_TIMEOUT_FULL, 200000000LL);
     }
     return;
   }
@@ -426,7 +486,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams 
   int i = 0;
   for (int64_t u = u0; u < u1; ++i) {
     const int tile = static_cast<int>(u / nsb), sb0 = static_cast<int>(u - static_cast<int64_t>(tile) * nsb);
-    const int len = static_cast<int>(min(static_cast<int64_t>(min(GEMV_KC, nsb - sb0)), u1 - u));
+    const int len = static_cast<int>(min(static_cast<int64_t>(min(p.kc, nsb - sb0)), u1 - u));
     const int grp = tile / tpg, lt = tile - grp * tpg;
     if (grp != staged) {
       named_bar_sync(1, GEMV_NCW * 32);
@@ -533,12 +593,15 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   const int ncols = (xt == XT_F32) ? 2 * p.M : p.M;
   if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ncols > 8) return set_error(-1, "gemv: bad shape");
   if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
-  p.pitch = gemv_stage_pitch(wt);
   const int xb = p.K * 2;
   p.xpitch = ((xb + 127) & ~127) + 64;
-  GemvLayout L0 = gemv_layout(wt, ncols, p.K, 0, p.pitch, p.xpitch);
-  const int per_stage = 16 * p.pitch;
-  int nst = (232448 - L0.off_ring) / per_stage;
+  int nst = 0;
+  for (p.kc = GEMV_KC; p.kc >= 1; p.kc >>= 1) {
+    p.pitch = gemv_stage_pitch(wt, p.kc);
+    GemvLayout L0 = gemv_layout(wt, ncols, p.K, 0, p.pitch, p.xpitch);
+    nst = (232448 - L0.off_ring) / (16 * p.pitch);
+    if (nst >= 2) break;
+  }
   if (nst > GEMV_MAXST) nst = GEMV_MAXST;
   if (nst < 2) return set_error(-1, "gemv: activation block too large for shared memory");
   p.nstages = nst;

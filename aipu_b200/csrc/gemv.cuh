@@ -4,7 +4,7 @@
 //
 // Contract followed: tools/q4k_ref.py:67-92 (exact ggml dequant, fp32 MAC, bf16 RNE out). The MAC
 // order differs from the reference's sequential K order (this kernel is within 1 bf16 ulp; the
-// strict kernel in strict.cu is the bit-exact one).
+// strict kernel in kernels.cu is the bit-exact one).
 //
 // Design (HBM-bound: ~0.56 B/weight for Q4_K, so the budget is ~3 thread-ops per weight):
 //   * Persistent grid, one CTA per SM: 8 consumer warps + 1 producer warp.
@@ -55,13 +55,14 @@ struct GemvParams {
   float* partials;           // stream-K workspace [grid][2][32][4]
   int* counters;             // stream-K arrival counters, one per tile, zero between launches
   int* status;               // device status word
+  int kc;                    // units (256-weight columns) per stage, <= GEMV_KC
   int pitch;                 // shared-memory row pitch of a stage
   int nstages;               // ring depth
   int xpitch;                // shared-memory bytes per activation column
 };
 
-__host__ __device__ inline int gemv_stage_pitch(int wt) {
-  int p0 = ((GEMV_KC * unit_bytes(wt) + 16) + 15) & ~15;
+__host__ __device__ inline int gemv_stage_pitch(int wt, int kc) {
+  int p0 = ((kc * unit_bytes(wt) + 16) + 15) & ~15;
   return p0 + (((32 - p0 % 128) % 128) + 128) % 128;  // pitch = 32 mod 128 (bank spread)
 }
 

@@ -182,62 +182,138 @@ __device__ void router_union(const RouterParams& p) {
   }
 }
 
-__global__ void __launch_bounds__(32) router_strict_kernel(const RouterParams p) {
-  pdl_wait();
-  const int lane = threadIdx.x;
-  const int e = blockIdx.x * 32 + lane;
-  const int m = blockIdx.y;
+// One CTA = 32 experts x a block of up to 8 tokens; one consumer warp per token (lane = expert),
+// each lane running the sequential fp32 chain of its (token, expert) logit. For the dense fp32
+// router ([K, E]) a producer warp streams 128-row x 32-expert chunks of W (and the matching
+// activation slices) into a shared-memory ring with 1-D bulk copies, so the chains never wait on
+// DRAM latency. GGUF-row routers dequantise each weight exactly in the chain.
+constexpr int RT_CHUNK = 128;   // k rows per stage
+constexpr int RT_NST = 6;       // ring depth
+constexpr int RT_MB = 8;        // tokens per CTA
+constexpr int RT_WBYTES = RT_CHUNK * 32 * 4;
+constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
+
+__global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const RouterParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + RT_NST;
+  uint8_t* ring = smem + 128;
+  __shared__ int last_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * 32, e = e0 + lane;
+  const int m0 = blockIdx.y * RT_MB;
+  const int mb = min(RT_MB, p.M - m0);
   const int K = p.K, E = p.E;
-  float acc = 0.f;
-  if (e < E) {
-    const int64_t xo = static_cast<int64_t>(m) * K;
-    if (p.wt == WT_F32) {
-      // dense fp32 router stored [K, E] (x @ W): coalesced across the warp at every k
-      const float* W = reinterpret_cast<const float*>(p.w);
-#pragma unroll 4
-      for (int k = 0; k < K; ++k) {
-        const float xv = bf16_bits_to_f32(__ldg(p.x + xo + k));
-        acc = __fadd_rn(acc, __fmul_rn(xv, __ldg(W + static_cast<int64_t>(k) * E + e)));
-      }
-    } else {
-      const uint8_t* row = p.w + static_cast<int64_t>(e) * row_bytes_of(p.wt, K);
-      for (int k = 0; k < K; ++k) {
-        const float xv = bf16_bits_to_f32(__ldg(p.x + xo + k));
-        acc = __fadd_rn(acc, __fmul_rn(xv, deq_one(p.wt, row, k)));
-      }
+  const bool dense = (p.wt == WT_F32);
+  const int nchunk = (K + RT_CHUNK - 1) / RT_CHUNK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RT_NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], mb);
     }
-    const float logit = bf16_round_f(acc);
-    p.gate[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(glm_sigmoid_bf(logit));
-    if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
+    fence_mbar_init();
   }
-  // last warp of this token does the selection; the last token does the union
+  __syncthreads();
+  pdl_wait();
+  if (warp == RT_MB) {
+    // producer: W[k0:k0+128, e0:e0+32] rows and x[m0+m, k0:k0+128] slices
+    if (!dense) return;
+    const int ne = min(32, E - e0);
+    const uint32_t wrow = static_cast<uint32_t>((ne * 4 + 15) & ~15);
+    for (int c = 0; c < nchunk; ++c) {
+      const int slot = c % RT_NST;
+      if (c >= RT_NST) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((c / RT_NST) - 1) & 1, p.status, ST_TIMEOUT_EMPTY);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
+      }
+      const int k0 = c * RT_CHUNK, kl = min(RT_CHUNK, K - k0);
+      const uint32_t xrow = static_cast<uint32_t>((kl * 2 + 15) & ~15);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], wrow * kl + xrow * mb);
+      __syncwarp();
+      uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
+      const float* W = reinterpret_cast<const float*>(p.w);
+      for (int r = lane; r < kl; r += 32)
+        bulk_g2s(st + r * 128, W + static_cast<int64_t>(k0 + r) * E + e0, wrow, &full[slot]);
+      if (lane < mb)
+        bulk_g2s(st + RT_WBYTES + lane * RT_CHUNK * 2, p.x + static_cast<int64_t>(m0 + lane) * K + k0, xrow,
+                 &full[slot]);
+    }
+    return;
+  }
+  // consumer warp `warp` = token m0 + warp
+  const int m = m0 + warp;
+  if (warp < mb) {
+    float acc = 0.f;
+    if (dense) {
+      bool ok = true;
+      for (int c = 0; c < nchunk; ++c) {
+        const int slot = c % RT_NST;
+        const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
+        if (ok) ok = mbar_wait_bounded(&full[slot], (c / RT_NST) & 1, p.status, ST_TIMEOUT_FULL);
+        if (ok) {
+          const uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
+          const float* ws = reinterpret_cast<const float*>(st);
+          const uint16_t* xs = reinterpret_cast<const uint16_t*>(st + RT_WBYTES + warp * RT_CHUNK * 2);
+#pragma unroll 8
+          for (int k = 0; k < kl; ++k) acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(xs[k]), ws[k * 32 + lane]));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+    } else if (e < E) {
+      const uint8_t* row = p.w + static_cast<int64_t>(e) * row_bytes_of(p.wt, K);
+      const int64_t xo = static_cast<int64_t>(m) * K;
+      for (int k = 0; k < K; ++k)
+        acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(__ldg(p.x + xo + k)), deq_one(p.wt, row, k)));
+    }
+    if (e < E) {
+      const float logit = bf16_round_f(acc);
+      p.gate[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(glm_sigmoid_bf(logit));
+      if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
+    }
+  }
+  // the last CTA of this token block selects top-K for its tokens; the last block builds the union
+  named_bar_sync(1, 32 * RT_MB);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last_flag = (atomicAdd(&p.counters[blockIdx.y], 1) == static_cast<int>(gridDim.x) - 1);
+  }
+  named_bar_sync(1, 32 * RT_MB);
+  if (!last_flag) return;
   __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) last = (atomicAdd(&p.counters[m], 1) == static_cast<int>(gridDim.x) - 1);
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
+  if (warp < mb) router_topk_token(p, m);
+  named_bar_sync(1, 32 * RT_MB);
+  if (threadIdx.x == 0) {
+    p.counters[blockIdx.y] = 0;
+    __threadfence();
+    last_flag = (atomicAdd(&p.counters[gridDim.y], 1) == static_cast<int>(gridDim.y) - 1);
+  }
+  named_bar_sync(1, 32 * RT_MB);
+  if (!last_flag) return;
   __threadfence();
-  if (lane == 0) p.counters[m] = 0;
-  router_topk_token(p, m);
-  __threadfence();
-  __syncwarp();
-  int lastm = 0;
-  if (lane == 0) lastm = (atomicAdd(&p.counters[p.M], 1) == p.M - 1);
-  lastm = __shfl_sync(0xffffffffu, lastm, 0);
-  if (!lastm) return;
-  __threadfence();
-  if (lane == 0) p.counters[p.M] = 0;
-  if (p.union_ids) router_union(p);
-  pdl_launch_dependents();
+  if (warp == 0) {
+    if (lane == 0) p.counters[gridDim.y] = 0;
+    if (p.union_ids) router_union(p);
+  }
 }
 
 int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
   if (p.E <= 0 || p.E > 1024 || p.topk <= 0 || p.topk > 16 || p.topk > p.E || p.M <= 0)
     return set_error(EINVAL_, "router: need 1 <= topk <= min(16, E), E <= 1024");
+  if (p.wt == WT_F32 && (p.E % 4 != 0 || (reinterpret_cast<uintptr_t>(p.w) & 15u) ||
+                         (reinterpret_cast<uintptr_t>(p.x) & 15u) || (p.K % 8)))
+    return set_error(EINVAL_, "router: fp32 router needs E % 4 == 0, K % 8 == 0 and 16-byte aligned w, x");
+  static bool attr = false;
+  const int smem = 128 + RT_NST * (RT_WBYTES + RT_XBYTES);
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(router_strict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(router)");
+    attr = true;
+  }
   RouterParams q = p;
-  return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel), dim3((p.E + 31) / 32, p.M), dim3(32), 0,
-                       s, pdl, &q);
+  return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel), dim3((p.E + 31) / 32, (p.M + RT_MB - 1) / RT_MB),
+                       dim3(32 * (RT_MB + 1)), smem, s, pdl, &q);
 }
 
 // ------------------------------------------------------------------ combine

@@ -21,7 +21,8 @@ struct RouterParams {
   int32_t* union_ids;      // [<= M*topk] sorted union of selected experts (nullable)
   int32_t* n_union;        // [1]
   int32_t* slot_map;       // [M, topk] index of sel[m, s] in union_ids
-  int* counters;           // [M + 1] arrival counters, zero between launches
+  int* counters;           // [token blocks + 1] arrival counters, zero between launches
+  int* status;             // device status word
 };
 
 struct CombineParams {
