@@ -231,6 +231,41 @@ extern "C" int aipu_q4k_gemm(aipu_ctx* c, int wtype, const void* w, int64_t N, i
   return gemm_fast(c, c->ws[0], wtype, w, N, K, x, x_dtype, M, y, s, (c->flags & AIPU_FLAG_PDL) != 0);
 }
 
+extern "C" int aipu_q4k_gemm_grouped(aipu_ctx* c, int wtype, const void* w, int64_t n_mats, int64_t mat_stride,
+                                     int64_t N, int64_t K, const void* x, int x_dtype, int64_t M, void* y,
+                                     void* stream) {
+  if (!c || !w || !x || !y || n_mats <= 0 || N <= 0 || M <= 0 || K % 256 || aipu_row_bytes(wtype, K) == 0 ||
+      wtype == AIPU_F32 || (x_dtype != AIPU_DT_F32 && x_dtype != AIPU_DT_BF16) || N > INT32_MAX || K > INT32_MAX ||
+      mat_stride < N * aipu_row_bytes(wtype, K) || (mat_stride & 15) || (reinterpret_cast<uintptr_t>(w) & 15u))
+    return set_error(EINVAL_, "gemm_grouped: bad arguments");
+  if (n_mats * ((N + 15) / 16) > c->ws[0].max_tiles) return set_error(EINVAL_, "gemm_grouped: too many tiles");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int mb = (x_dtype == AIPU_DT_F32) ? 4 : 8;
+  const int esz = (x_dtype == AIPU_DT_F32) ? 4 : 2;
+  for (int64_t m0 = 0; m0 < M; m0 += mb) {
+    GemvParams p = {};
+    p.w0 = static_cast<const uint8_t*>(w);
+    p.row_bytes = row_bytes_of(wtype, K);
+    p.expert_stride = mat_stride;
+    p.n_groups = static_cast<int>(n_mats);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.x = static_cast<const uint8_t*>(x) + m0 * K * esz;
+    p.x_group_stride = 0;
+    p.M = static_cast<int>(std::min<int64_t>(mb, M - m0));
+    p.y = static_cast<uint16_t*>(y) + m0 * N;
+    p.y_group_stride = M * N;
+    p.partials = c->ws[0].partials;
+    p.counters = c->ws[0].counters;
+    p.status = c->status;
+    int rc = gemv_launch(wtype, x_dtype == AIPU_DT_F32 ? XT_F32 : XT_BF16, EPI_STORE, p, c->num_sms, s,
+                         (c->flags & AIPU_FLAG_PDL) != 0);
+    if (rc) return rc;
+  }
+  return OK;
+}
+
 extern "C" int aipu_moe_router(aipu_ctx* c, int wt, const void* w, const float* bias, const void* x, int64_t M,
                                int64_t K, int64_t E, int topk, float scale, int32_t* sel, void* sel_w, void* gate,
                                void* logits, void* stream) {

@@ -16,7 +16,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int 
   GemvLayout L;
   L.off_misc = 2 * GEMV_MAXST * 8;                 // mbarriers first
   L.off_red = L.off_misc + 256;
-  L.off_xs = L.off_red + GEMV_NCW * 32 * 16;       // 4096 B of reduction space
+  L.off_xs = L.off_red + GEMV_NCW * 32 * 16;       // per-warp reduction space
   L.off_sxs = L.off_xs + ncols * xpitch;
   int sx = (wt == WT_Q4K) ? ncols * (K / 256) * 32 : 0;
   L.off_ring = (L.off_sxs + sx + 127) & ~127;
@@ -61,10 +61,12 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
   const uint32_t sc478 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
   const uint32_t m478 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
 
-  float P[4] = {0.f, 0.f, 0.f, 0.f};
+  float P4[4][4];  // one accumulator chain per 64-weight group (independent MMA chains)
   const uint8_t* xb = xcol + 2 * (sb * 256 + 8 * t);
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
+    float (&P)[4] = P4[p];
+    P[0] = P[1] = P[2] = P[3] = 0.f;
     const uint32_t wg = (p < 2) ? sc03g : sc47g;
     const uint32_t w8 = (p < 2) ? sc038 : sc478;
     const int il = (2 * p) & 3, ih = (2 * p + 1) & 3;
@@ -100,6 +102,9 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
       mma_f16_16816(P, a, j ? xh.z : xh.x, j ? xh.w : xh.y);
     }
   }
+  float P[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) P[i] = __fadd_rn(__fadd_rn(P4[0][i], P4[1][i]), __fadd_rn(P4[2][i], P4[3][i]));
   // min term: Cm[row, col] = sum_j m_j * (Sx_hi + Sx_lo)[col, j]
   float Cm[4] = {0.f, 0.f, 0.f, 0.f};
   {
@@ -201,6 +206,7 @@ __device__ __forceinline__ void unit_q80(const uint8_t* rg, const uint8_t* rg8, 
 __device__ __forceinline__ void unit_f16(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol, bool colok,
                                          int sb, int t, float (&acc)[4]) {
   const uint8_t* xb = xcol + 2 * (sb * 256 + 4 * t);
+  float P4[4][4] = {};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint2 wg = *reinterpret_cast<const uint2*>(rg + 2 * (16 * i + 4 * t));
@@ -208,8 +214,11 @@ __device__ __forceinline__ void unit_f16(const uint8_t* rg, const uint8_t* rg8, 
     uint32_t a[4] = {wg.x, w8.x, wg.y, w8.y};
     uint2 xv = make_uint2(0, 0);
     if (colok) xv = *reinterpret_cast<const uint2*>(xb + 2 * (16 * i));
-    mma_f16_16816(acc, a, xv.x, xv.y);
+    mma_f16_16816(P4[i & 3], a, xv.x, xv.y);
   }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    acc[j] = __fadd_rn(acc[j], __fadd_rn(__fadd_rn(P4[0][j], P4[1][j]), __fadd_rn(P4[2][j], P4[3][j])));
 }
 
 // ------------------------------------------------------------------ kernel
@@ -271,132 +280,174 @@ __device__ void gemv_epilogue(const GemvParams& p, const int* misc, int grp, int
   }
 }
 
+// fp32 or bf16 16-byte vector -> fp16 values scaled by `sc` (hi, and lo for fp32 input), written to
+// the activation columns in the per-type k order; returns the sum(s) of the written fp16 values.
+template <int XT, bool SWZ>
+__device__ __forceinline__ void stage_vec(const uint4 q, float sc, uint8_t* colhi, uint8_t* collo, int v,
+                                          float& sum_hi, float& sum_lo) {
+  if (XT == XT_F32) {
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+    uint32_t hb[4], lb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float f = __fmul_rn(__uint_as_float(w4[i]), sc);
+      const __half hi = __float2half_rn(f);
+      const float hf = __half2float(hi);
+      const __half lo = __float2half_rn(__fsub_rn(f, hf));
+      hb[i] = __half_as_ushort(hi);
+      lb[i] = __half_as_ushort(lo);
+      sum_hi = __fadd_rn(sum_hi, hf);
+      sum_lo = __fadd_rn(sum_lo, __half2float(lo));
+    }
+    const int a1 = SWZ ? 2 : 1, a2 = SWZ ? 1 : 2;
+    *reinterpret_cast<uint2*>(colhi + 8 * v) = make_uint2(hb[0] | (hb[a1] << 16), hb[a2] | (hb[3] << 16));
+    *reinterpret_cast<uint2*>(collo + 8 * v) = make_uint2(lb[0] | (lb[a1] << 16), lb[a2] | (lb[3] << 16));
+  } else {
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half a = __float2half_rn(__fmul_rn(__uint_as_float(w4[i] << 16), sc));
+      const __half b = __float2half_rn(__fmul_rn(__uint_as_float(w4[i] & 0xFFFF0000u), sc));
+      h[2 * i] = __half_as_ushort(a);
+      h[2 * i + 1] = __half_as_ushort(b);
+      sum_hi = __fadd_rn(sum_hi, __fadd_rn(__half2float(a), __half2float(b)));
+    }
+    uint4 o;
+    if (SWZ) {
+      o = make_uint4(h[0] | (h[2] << 16), h[1] | (h[3] << 16), h[4] | (h[6] << 16), h[5] | (h[7] << 16));
+    } else {
+      o = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+    }
+    *reinterpret_cast<uint4*>(colhi + 16 * v) = o;
+  }
+}
+
+__device__ __forceinline__ float vec_absmax(const uint4 q, bool f32, float mx) {
+  const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (f32) {
+      mx = fmaxf(mx, fabsf(__uint_as_float(w4[i])));
+    } else {
+      mx = fmaxf(mx, fabsf(__uint_as_float(w4[i] << 16)));
+      mx = fmaxf(mx, fabsf(__uint_as_float(w4[i] & 0xFFFF0000u)));
+    }
+  }
+  return mx;
+}
+
+__device__ __forceinline__ int prescale_shift(float mx) {
+  // max * 2^-s in [2^9, 2^10): sub-block sums of 32 values stay below 2^15 (fp16-safe)
+  const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
+  int s = (mx == 0.f) ? 0 : (e - 127 - 9);
+  return s < -100 ? -100 : (s > 100 ? 100 : s);
+}
+
+// Stage the activations of group `grp` into shared memory as fp16 columns (see gemv.cuh). Tokens
+// are handled two at a time: 16-byte vectors are loaded once into registers (up to 4 per thread per
+// token), reduced for the per-token power-of-two prescale, converted and stored; for Q4_K the
+// 32-weight sub-block sums are reduced across the 4 (bf16) or 8 (fp32) lanes holding a sub-block.
 template <int WT, int XT, int EPI>
 __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int ncols) {
-  const int tid = threadIdx.x;  // consumer threads 0..255
+  const int tid = threadIdx.x;
   constexpr int NT = GEMV_NCW * 32;
+  constexpr int VEC = (XT == XT_F32) ? 4 : 8;
+  constexpr int VPT = 4;
+  constexpr bool SWZ = (WT != WT_F16);
+  constexpr int LPS = 32 / VEC;  // lanes holding one 32-weight sub-block
   int* misc = reinterpret_cast<int*>(smem + L.off_misc);
   float* red = reinterpret_cast<float*>(smem + L.off_red);
-  const int K = p.K, M = p.M;
-  const int64_t xo = static_cast<int64_t>(grp) * p.x_group_stride;
-  const float* xf = reinterpret_cast<const float*>(p.x) + xo;
-  const uint16_t* xh = reinterpret_cast<const uint16_t*>(p.x) + xo;
-  (void)xf;
-  (void)xh;
-  // 1. per-token max |x| -> power-of-two prescale so that max * 2^-s lies in [2^9, 2^10).
-  //    16-byte loads, several in flight per thread (x is read from L2 by every CTA).
-  constexpr int VEC = (XT == XT_F32) ? 4 : 8;  // elements per 16-byte vector
-  const int nv = K / VEC;
-  const uint4* xv = reinterpret_cast<const uint4*>(XT == XT_F32 ? static_cast<const void*>(xf)
-                                                                : static_cast<const void*>(xh));
-  auto vmax = [&](const uint4 q, float mx) -> float {
-    if (XT == XT_F32) {
-      mx = fmaxf(mx, fabsf(__uint_as_float(q.x)));
-      mx = fmaxf(mx, fabsf(__uint_as_float(q.y)));
-      mx = fmaxf(mx, fabsf(__uint_as_float(q.z)));
-      mx = fmaxf(mx, fabsf(__uint_as_float(q.w)));
-    } else {
-      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        mx = fmaxf(mx, fabsf(__uint_as_float(w4[i] << 16)));
-        mx = fmaxf(mx, fabsf(__uint_as_float(w4[i] & 0xFFFF0000u)));
-      }
-    }
-    return mx;
-  };
-  for (int m = 0; m < M; ++m) {
-    float mx = 0.f;
-    const uint4* row = xv + static_cast<int64_t>(m) * nv;
-#pragma unroll 4
-    for (int v = tid; v < nv; v += NT) mx = vmax(__ldg(row + v), mx);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = mx;
-  }
-  named_bar_sync(1, NT);
-  if (tid < M) {
-    float mx = 0.f;
-    for (int w = 0; w < GEMV_NCW; ++w) mx = fmaxf(mx, red[w * 8 + tid]);
-    int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
-    int s = (mx == 0.f) ? 0 : (e - 127 - 9);
-    s = s < -100 ? -100 : (s > 100 ? 100 : s);
-    if (XT == XT_F32) {
-      misc[2 * tid] = s;
-      misc[2 * tid + 1] = s;
-    } else {
-      misc[tid] = s;
-    }
-  }
-  named_bar_sync(1, NT);
-  // 2. convert to fp16 columns (bf16: exact; fp32: hi + lo), in the per-type k order. A 16-byte
-  //    vector covers whole aligned groups of four, so the reordering stays inside it.
-  constexpr bool swz = (WT != WT_F16);
   uint8_t* xs = smem + L.off_xs;
-  for (int m = 0; m < M; ++m) {
-    const uint4* row = xv + static_cast<int64_t>(m) * nv;
-    const float sc = exp2i(-misc[XT == XT_F32 ? 2 * m : m]);
-#pragma unroll 4
-    for (int v = tid; v < nv; v += NT) {
-      const uint4 q = __ldg(row + v);
-      if (XT == XT_F32) {
-        const float f[4] = {__fmul_rn(__uint_as_float(q.x), sc), __fmul_rn(__uint_as_float(q.y), sc),
-                            __fmul_rn(__uint_as_float(q.z), sc), __fmul_rn(__uint_as_float(q.w), sc)};
-        __half hi[4], lo[4];
+  uint8_t* sxs = smem + L.off_sxs;
+  const int K = p.K, M = p.M, nv = K / VEC, nsb = K / 256;
+  const uint4* xv = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
+                                                   static_cast<int64_t>(grp) * p.x_group_stride * (XT == XT_F32 ? 4 : 2));
+  const bool one_pass = nv <= VPT * NT;
+  for (int m0 = 0; m0 < M; m0 += 2) {
+    const int mt = min(2, M - m0);
+    uint4 q[2][VPT];
+    float mx[2] = {0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          hi[i] = __float2half_rn(f[i]);
-          lo[i] = __float2half_rn(__fsub_rn(f[i], __half2float(hi[i])));
-        }
-        const int o = swz ? 1 : 0;  // positions (0,2,1,3) within the group when swizzled
-        uint2 H, Lw;
-        H.x = static_cast<uint32_t>(__half_as_ushort(hi[0])) | (static_cast<uint32_t>(__half_as_ushort(hi[o ? 2 : 1])) << 16);
-        H.y = static_cast<uint32_t>(__half_as_ushort(hi[o ? 1 : 2])) | (static_cast<uint32_t>(__half_as_ushort(hi[3])) << 16);
-        Lw.x = static_cast<uint32_t>(__half_as_ushort(lo[0])) | (static_cast<uint32_t>(__half_as_ushort(lo[o ? 2 : 1])) << 16);
-        Lw.y = static_cast<uint32_t>(__half_as_ushort(lo[o ? 1 : 2])) | (static_cast<uint32_t>(__half_as_ushort(lo[3])) << 16);
-        *reinterpret_cast<uint2*>(xs + (2 * m) * p.xpitch + 8 * v) = H;
-        *reinterpret_cast<uint2*>(xs + (2 * m + 1) * p.xpitch + 8 * v) = Lw;
-      } else {
-        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-        uint16_t h[8];
+    for (int t2 = 0; t2 < 2; ++t2) {
+      if (t2 < mt) {
+        const uint4* row = xv + static_cast<int64_t>(m0 + t2) * nv;
+        if (one_pass) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          h[2 * i] = __half_as_ushort(__float2half_rn(__fmul_rn(__uint_as_float(w4[i] << 16), sc)));
-          h[2 * i + 1] = __half_as_ushort(__float2half_rn(__fmul_rn(__uint_as_float(w4[i] & 0xFFFF0000u), sc)));
-        }
-        uint4 o4;
-        if (swz) {
-          o4.x = h[0] | (static_cast<uint32_t>(h[2]) << 16);
-          o4.y = h[1] | (static_cast<uint32_t>(h[3]) << 16);
-          o4.z = h[4] | (static_cast<uint32_t>(h[6]) << 16);
-          o4.w = h[5] | (static_cast<uint32_t>(h[7]) << 16);
+          for (int j = 0; j < VPT; ++j) {
+            const int v = tid + j * NT;
+            q[t2][j] = (v < nv) ? __ldg(row + v) : make_uint4(0, 0, 0, 0);
+            mx[t2] = vec_absmax(q[t2][j], XT == XT_F32, mx[t2]);
+          }
         } else {
-          o4.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
-          o4.y = h[2] | (static_cast<uint32_t>(h[3]) << 16);
-          o4.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
-          o4.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
+          for (int v = tid; v < nv; v += NT) mx[t2] = vec_absmax(__ldg(row + v), XT == XT_F32, mx[t2]);
         }
-        *reinterpret_cast<uint4*>(xs + m * p.xpitch + 16 * v) = o4;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx[t2] = fmaxf(mx[t2], __shfl_xor_sync(0xffffffffu, mx[t2], o));
+        if ((tid & 31) == 0) red[(tid >> 5) * 2 + t2] = mx[t2];
       }
     }
-  }
-  if (WT == WT_Q4K) {
     named_bar_sync(1, NT);
-    // 3. per-(column, 32-weight sub-block) activation sums, split hi/lo fp16
-    const int nsub = K / 32;
-    uint8_t* sxs = smem + L.off_sxs;
-    for (int it = tid; it < ncols * nsub; it += NT) {
-      const int c = it / nsub, sub = it - c * nsub;
-      const __half* col = reinterpret_cast<const __half*>(xs + c * p.xpitch) + sub * 32;
-      float s = 0.f;
-#pragma unroll 8
-      for (int i = 0; i < 32; ++i) s = __fadd_rn(s, __half2float(col[i]));
-      const __half hi = __float2half_rn(s);
-      const __half lo = __float2half_rn(__fsub_rn(s, __half2float(hi)));
-      __half* dst = reinterpret_cast<__half*>(sxs + (c * (K / 256) + sub / 8) * 32);
-      dst[sub & 7] = hi;
-      dst[8 + (sub & 7)] = lo;
+    int sh[2];
+#pragma unroll
+    for (int t2 = 0; t2 < 2; ++t2) {
+      float m = 0.f;
+      for (int w = 0; w < GEMV_NCW; ++w) m = fmaxf(m, red[w * 2 + t2]);
+      sh[t2] = prescale_shift(m);
     }
+    if (tid == 0) {
+      for (int t2 = 0; t2 < mt; ++t2) {
+        if (XT == XT_F32) {
+          misc[2 * (m0 + t2)] = sh[t2];
+          misc[2 * (m0 + t2) + 1] = sh[t2];
+        } else {
+          misc[m0 + t2] = sh[t2];
+        }
+      }
+    }
+#pragma unroll
+    for (int t2 = 0; t2 < 2; ++t2) {
+      if (t2 >= mt) continue;
+      const int m = m0 + t2;
+      const float sc = exp2i(-sh[t2]);
+      const int chi = (XT == XT_F32) ? 2 * m : m;
+      uint8_t* colhi = xs + chi * p.xpitch;
+      uint8_t* collo = (XT == XT_F32) ? xs + (chi + 1) * p.xpitch : colhi;
+      const uint4* row = xv + static_cast<int64_t>(m) * nv;
+      const int nrounds = one_pass ? 1 : (nv + VPT * NT - 1) / (VPT * NT);
+      for (int rd = 0; rd < nrounds; ++rd) {
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const int v = tid + (rd * VPT + j) * NT;
+          if (!one_pass && v < nv) q[t2][j] = __ldg(row + v);
+          float shi = 0.f, slo = 0.f;
+          if (v < nv) stage_vec<XT, SWZ>(q[t2][j], sc, colhi, collo, v, shi, slo);
+          if (WT == WT_Q4K) {
+#pragma unroll
+            for (int o = 1; o < LPS; o <<= 1) {
+              shi = __fadd_rn(shi, __shfl_xor_sync(0xffffffffu, shi, o));
+              if (XT == XT_F32) slo = __fadd_rn(slo, __shfl_xor_sync(0xffffffffu, slo, o));
+            }
+            if (v < nv && (v % LPS) == 0) {
+              const int sub = v / LPS;
+              const __half hh = __float2half_rn(shi);
+              const __half hl = __float2half_rn(__fsub_rn(shi, __half2float(hh)));
+              __half* dst = reinterpret_cast<__half*>(sxs + (chi * nsb + sub / 8) * 32);
+              dst[sub & 7] = hh;
+              dst[8 + (sub & 7)] = hl;
+              if (XT == XT_F32) {
+                const __half lh = __float2half_rn(slo);
+                const __half ll = __float2half_rn(__fsub_rn(slo, __half2float(lh)));
+                __half* d2 = reinterpret_cast<__half*>(sxs + ((chi + 1) * nsb + sub / 8) * 32);
+                d2[sub & 7] = lh;
+                d2[8 + (sub & 7)] = ll;
+              }
+            }
+          }
+        }
+      }
+    }
+    named_bar_sync(1, NT);
   }
 }
 
@@ -425,6 +476,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams 
     fence_mbar_init();
   }
   __syncthreads();
+  // the next kernel may be scheduled now; it reads our outputs only after its griddepcontrol.wait
+  pdl_launch_dependents();
 
   const bool dyn = (p.group_ids != nullptr) || (p.n_groups_dev != nullptr);
   const int nsb = p.K >> 8;
@@ -465,8 +518,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams 
       if (lane < 16) bulk_g2s(ring + slot * stage_bytes + lane * p.pitch, lo, bytes, &full[slot]);
       u += len;
     }
-    // never leave with copies in flight: wait for the last issued phase of every slot
-    if (lane == 0) {
+    // after an abort, never leave with copies in flight: wait for the last issued phase of every slot
+    if (lane == 0 && *abort_flag) {
       for (int j = max(0, i - NST); j < i; ++j)
         mbar_wait_bounded(&full[j % NST], (j / NST) & 1, p.status, ST_TIMEOUT_FULL, 200000000LL);
     }
@@ -571,7 +624,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams 
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
     }
   }
-  pdl_launch_dependents();
 }
 
 // ------------------------------------------------------------------ host launch

@@ -7,11 +7,11 @@
 // strict kernel in kernels.cu is the bit-exact one).
 //
 // Design (HBM-bound: ~0.56 B/weight for Q4_K, so the budget is ~3 thread-ops per weight):
-//   * Persistent grid, one CTA per SM: 8 consumer warps + 1 producer warp.
+//   * Persistent grid, one CTA per SM: 16 consumer warps + 1 producer warp.
 //   * Work unit = 16 weight rows x 256 weights (one super-block column). The units of all tiles are
 //     laid end to end and split evenly over the CTAs ("stream-K"); a tile cut between CTAs is
 //     finished by the last CTA to arrive, which sums the partials in CTA order (deterministic).
-//   * The producer streams each chunk (16 rows x up to 8 units) with 1-D bulk copies
+//   * The producer streams each chunk (16 rows x up to 16 units) with 1-D bulk copies
 //     (cp.async.bulk, the untiled TMA path; no multicast) into a multi-stage shared-memory ring,
 //     completion tracked by mbarriers. Weights do not depend on the previous kernel, so with
 //     programmatic dependent launch the ring fills before griddepcontrol.wait.
@@ -30,7 +30,7 @@
 
 namespace aipu {
 
-constexpr int GEMV_NCW = 8;                       // consumer warps
+constexpr int GEMV_NCW = 16;                      // consumer warps
 constexpr int GEMV_THREADS = (GEMV_NCW + 1) * 32;
 constexpr int GEMV_KC = GEMV_NCW;                 // units per stage (one per consumer warp)
 constexpr int GEMV_MAXST = 16;

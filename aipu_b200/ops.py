@@ -121,6 +121,23 @@ def gemm(wtype: int, w: torch.Tensor, N: int, K: int, x: torch.Tensor, mode: str
     return out
 
 
+def gemm_grouped(wtype: int, w: torch.Tensor, n_mats: int, N: int, K: int, x: torch.Tensor,
+                 mat_stride: Optional[int] = None, ctx: Optional[Context] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[g, M, N] bf16 = x[M, K] x W_g^T for n_mats matrices stored back to back (stride in bytes)."""
+    _need_cuda(w, x, out)
+    stride = mat_stride or N * row_bytes(wtype, K)
+    if w.numel() * w.element_size() < (n_mats - 1) * stride + N * row_bytes(wtype, K):
+        raise ValueError("weight buffer too small for n_mats matrices")
+    ctx = ctx or Context.default(w.device)
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((n_mats, M, N), dtype=torch.bfloat16, device=w.device)
+    check(lib().aipu_q4k_gemm_grouped(ctx.handle, wtype, _ptr(w), n_mats, stride, N, K, _ptr(x), _DTYPE[x.dtype],
+                                      M, _ptr(out), _stream(w.device)))
+    return out
+
+
 def moe_router(router_wtype: int, w: torch.Tensor, x: torch.Tensor, n_experts: int, topk: int,
                bias: Optional[torch.Tensor] = None, scale: float = 2.5, ctx: Optional[Context] = None,
                want_logits: bool = False):

@@ -3,9 +3,11 @@
 
 Headline metric: Q4_K GEMV HBM GB/s on the BASELINE config-2 shape (2048 rows x 6144, bf16 x,
 M = 1). A step is one pass over a batch of `--matrices` distinct weight matrices (1.8 GB by default,
-far larger than the 126 MB L2, so no L2 flush is needed), one GEMV launch per matrix, replayed as a
-CUDA graph with programmatic dependent launch. value = algorithmic bytes (weights + x + y) of all
-GEMVs of all ranks / device time (max over ranks).
+far larger than the 126 MB L2, so no L2 flush is needed) applied to the same activation row, as ONE
+grouped launch (aipu_q4k_gemm_grouped), replayed as a CUDA graph. value = algorithmic bytes
+(weights + x + y) of all GEMVs of all ranks / device time (max over ranks). The same GEMVs as one
+launch per matrix (decode-style stream, programmatic dependent launch) are reported as
+"single_launch".
 
 Also reported: roofline of the GEMV kernel against MEASURED_PEAKS.json, the CPU baseline (the C
 restatement of the reference's contract on the host cores), the end-to-end number through the public
@@ -66,6 +68,14 @@ def traffic_from_profile():
             except ValueError:
                 return None
     return None
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
 
 
 class ClockSampler:
@@ -270,44 +280,60 @@ def main():
     y = torch.empty((L, 1, N_ROWS), dtype=torch.bfloat16, device=d)
     ctx = ops.Context(d).set_flags(pdl=True)
 
-    def issue():
+    def issue_grouped():
+        ops.gemm_grouped(F.Q4_K, Wt, L, N_ROWS, K_COLS, x, ctx=ctx, out=y)
+
+    def issue_single():
         for l in range(L):
             ops.gemm(F.Q4_K, mats[l], N_ROWS, K_COLS, x, ctx=ctx, out=y[l])
 
-    s = torch.cuda.Stream()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        issue()
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            fn()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                fn()
         torch.cuda.synchronize()
-        with torch.cuda.graph(g, stream=s):
-            issue()
-    torch.cuda.synchronize()
-    for _ in range(max(args.warmup, 3)):
-        g.replay()
-    torch.cuda.synchronize()
+        return g
+
+    def timed(g, steps, warmup, sampler=None):
+        for _ in range(max(warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with (sampler if sampler is not None else _Null()):
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(steps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            tt = torch.tensor([t], device=d, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t / steps
+
+    s = torch.cuda.Stream()
     if world > 1:
         import torch.distributed as dist
-
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(d.index) as clk:
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(args.steps):
-            g.replay()
-        e1.record()
-        torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / 1e3
-    if world > 1:
-        tt = torch.tensor([t], device=d, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt.item())
-        dist.barrier()
-    step = t / args.steps
+    g = capture(issue_grouped)
+    clk = ClockSampler(d.index)
+    step = timed(g, args.steps, args.warmup, clk)
     value = world * L * GEMV_BYTES / step / 1e9
-    per_launch = step / L
     hbm_peak, _, peak_kind = peaks()
-    achieved = GEMV_BYTES / per_launch / 1e9
+    achieved = L * GEMV_BYTES / step / 1e9
+    # the same GEMVs as one launch per matrix (decode-style stream), back to back with PDL
+    gs = capture(issue_single)
+    step_single = timed(gs, max(10, args.steps // 4), args.warmup)
+    single = {"us_per_launch": round(step_single / L * 1e6, 3),
+              "gbs": round(L * GEMV_BYTES / step_single / 1e9, 1),
+              "note": "one kernel launch per 2048x6144 matrix, CUDA graph, programmatic dependent launch"}
+    del gs
 
     # ---- end to end through the public API with host buffers (x in, all y out, every step)
     x_host = torch.empty((1, K_COLS), dtype=torch.bfloat16, pin_memory=True).copy_(x.cpu())
@@ -333,7 +359,8 @@ def main():
         te = float(tt.item())
     e2e = {"value": round(world * L * GEMV_BYTES / te / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": K_COLS * 2, "d2h_bytes_per_step": L * N_ROWS * 2,
-           "path": "ops.gemm -> aipu_q4k_gemm (C ABI), replayed as a CUDA graph; pinned host x in, y out"}
+           "path": "ops.gemm_grouped -> aipu_q4k_gemm_grouped (C ABI), replayed as a CUDA graph; pinned host x in, "
+                   "all y out, every step"}
 
     del Wt, mats
     torch.cuda.empty_cache()
@@ -349,14 +376,16 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(step * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "Q4_K GEMV 2048x6144, x bf16 [1,6144] ~N(0,1), y bf16 (BASELINE config 2, Q4_K, "
-                                   "M=1)", "matrices_per_step": L, "bytes_per_gemv": GEMV_BYTES,
+                                   "M=1); a step = one grouped launch over the batch of matrices",
+                       "matrices_per_step": L, "bytes_per_gemv": GEMV_BYTES,
                        "l2": f"inputs larger than L2: {L * GEMV_W_BYTES / 1e9:.2f} GB of distinct weights per step",
                        "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic_from_profile(),
-                         "peak_source": peak_kind, "kernel": "gemv_kernel<Q4_K,bf16,store>",
-                         "us_per_launch": round(per_launch * 1e6, 3)},
-            "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": L * args.steps,
+                         "peak_source": peak_kind, "kernel": "gemv_kernel<Q4_K,bf16,store> (grouped launch)",
+                         "us_per_launch": round(step * 1e6, 3)},
+            "single_launch": single,
+            "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,
             "clocks": clk.summary(), "moe_decode": moe,
         }
         print(json.dumps(line), flush=True)

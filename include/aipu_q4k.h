@@ -91,6 +91,15 @@ int aipu_act_eval(int kind, const void* x, int64_t n, void* out, void* stream);
 int aipu_q4k_gemm(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype,
                   int64_t M, void* y, float* y_f32, int mode, void* stream);
 
+/* Grouped fast GEMM: n_mats independent matrices of N rows x K (matrix g at w + g * mat_stride
+ * bytes) applied to the same activations x[M, K] in ONE launch; y[g, M, N] (bf16). This is the
+ * decode pattern of several projections or experts fed by the same token rows (e.g. all experts of
+ * a layer on one token, or fused Q/K/V-style projections), and amortises the launch and the
+ * activation staging over all matrices. Same numerics as AIPU_MODE_FAST.
+ * Replaces: a loop of tools/q4k_ref.py:86-92 matmul_q4k_col over several weight matrices. */
+int aipu_q4k_gemm_grouped(aipu_ctx* ctx, int wtype, const void* w, int64_t n_mats, int64_t mat_stride, int64_t N,
+                          int64_t K, const void* x, int x_dtype, int64_t M, void* y, void* stream);
+
 /* MoE router on M bf16 token rows x[M, K]:
  *   logits = bf16(sequential fp32 x . w_e) for every expert e  (strict, bit-exact)
  *   gate   = bf16 glm sigmoid(logits)
