@@ -8,19 +8,21 @@
 namespace aipu {
 
 // ------------------------------------------------------------------ shared-memory layout
+// [mbarriers: NW x S][misc: prescale shifts per (group slot, column)][activations: XG x ncols fp16
+// columns][Q4_K sub-block sums][per-warp rings: NW x S slots x 16 rows x pitch]
 struct GemvLayout {
-  int off_misc, off_red, off_xs, off_sxs, off_ring, total;
+  int off_misc, off_xs, off_sxs, off_ring, total;
 };
 
-__host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int nstages, int pitch, int xpitch) {
+__host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int xg, int nw, int nslots, int pitch,
+                                                  int xpitch) {
   GemvLayout L;
-  L.off_misc = 2 * GEMV_MAXST * 8;                 // mbarriers first
-  L.off_red = L.off_misc + 256;
-  L.off_xs = L.off_red + GEMV_NCW * 32 * 16;       // per-warp reduction space
-  L.off_sxs = L.off_xs + ncols * xpitch;
-  int sx = (wt == WT_Q4K) ? ncols * (K / 256) * 32 : 0;
+  L.off_misc = GEMV_MAXW * GEMV_MAXS * 8;
+  L.off_xs = L.off_misc + 256;
+  L.off_sxs = L.off_xs + xg * ncols * xpitch;
+  const int sx = (wt == WT_Q4K) ? xg * ncols * (K / 256) * 32 : 0;
   L.off_ring = (L.off_sxs + sx + 127) & ~127;
-  L.total = L.off_ring + nstages * 16 * pitch;
+  L.total = L.off_ring + nw * nslots * 16 * pitch;
   return L;
 }
 
@@ -348,19 +350,24 @@ __device__ __forceinline__ int prescale_shift(float mx) {
 // are handled two at a time: 16-byte vectors are loaded once into registers (up to 4 per thread per
 // token), reduced for the per-token power-of-two prescale, converted and stored; for Q4_K the
 // 32-weight sub-block sums are reduced across the 4 (bf16) or 8 (fp32) lanes holding a sub-block.
+// Stage the activations of group `grp` into group slot `xs_slot` as fp16 columns (all threads of
+// the CTA). Tokens two at a time: 16-byte vectors are loaded once into registers (up to 4 per
+// thread per token), reduced for the per-token power-of-two prescale, converted and stored; for
+// Q4_K the 32-weight sub-block sums are reduced across the 4 (bf16) or 8 (fp32) lanes holding a
+// sub-block. Leaves with a __syncthreads.
 template <int WT, int XT, int EPI>
-__device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int ncols) {
+__device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int xs_slot,
+                             int ncols, float* red) {
   const int tid = threadIdx.x;
-  constexpr int NT = GEMV_NCW * 32;
+  const int NT = blockDim.x, NW = NT >> 5;
   constexpr int VEC = (XT == XT_F32) ? 4 : 8;
   constexpr int VPT = 4;
   constexpr bool SWZ = (WT != WT_F16);
   constexpr int LPS = 32 / VEC;  // lanes holding one 32-weight sub-block
-  int* misc = reinterpret_cast<int*>(smem + L.off_misc);
-  float* red = reinterpret_cast<float*>(smem + L.off_red);
-  uint8_t* xs = smem + L.off_xs;
-  uint8_t* sxs = smem + L.off_sxs;
+  int* misc = reinterpret_cast<int*>(smem + L.off_misc) + xs_slot * 8;
+  uint8_t* xs = smem + L.off_xs + xs_slot * ncols * p.xpitch;
   const int K = p.K, M = p.M, nv = K / VEC, nsb = K / 256;
+  uint8_t* sxs = smem + L.off_sxs + xs_slot * ncols * nsb * 32;
   const uint4* xv = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
                                                    static_cast<int64_t>(grp) * p.x_group_stride * (XT == XT_F32 ? 4 : 2));
   const bool one_pass = nv <= VPT * NT;
@@ -387,12 +394,12 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
         if ((tid & 31) == 0) red[(tid >> 5) * 2 + t2] = mx[t2];
       }
     }
-    named_bar_sync(1, NT);
+    __syncthreads();
     int sh[2];
 #pragma unroll
     for (int t2 = 0; t2 < 2; ++t2) {
       float m = 0.f;
-      for (int w = 0; w < GEMV_NCW; ++w) m = fmaxf(m, red[w * 2 + t2]);
+      for (int w = 0; w < NW; ++w) m = fmaxf(m, red[w * 2 + t2]);
       sh[t2] = prescale_shift(m);
     }
     if (tid == 0) {
@@ -447,223 +454,246 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
         }
       }
     }
-    named_bar_sync(1, NT);
+    __syncthreads();
   }
 }
 
+__device__ __forceinline__ int worker_of_unit(int64_t u, int64_t U, int W) {
+  return static_cast<int>(((u + 1) * W - 1) / U);
+}
+
+// A warp's chunk: up to `upc` consecutive units of one tile inside the warp's unit range.
+struct Chunk {
+  int tile, sb, n;
+};
+__device__ __forceinline__ Chunk next_chunk(int64_t u, int64_t b, int nsb, int upc) {
+  Chunk c;
+  c.tile = static_cast<int>(u / nsb);
+  c.sb = static_cast<int>(u - static_cast<int64_t>(c.tile) * nsb);
+  c.n = static_cast<int>(min(static_cast<int64_t>(min(upc, nsb - c.sb)), b - u));
+  return c;
+}
+
 template <int WT, int XT, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const GemvParams p) {
+__device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch, int tpg, uint8_t* slot,
+                                            uint64_t* bar, int lane) {
+  constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
+  uint32_t bytes = 0;
+  const uint8_t* lo = nullptr;
+  if (lane < 16) {
+    const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
+    const uint8_t* src = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, lane) + static_cast<int64_t>(ch.sb) * UB;
+    lo = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15));
+    bytes = (static_cast<uint32_t>(src - lo) + ch.n * UB + 15u) & ~15u;
+  }
+  uint32_t total = bytes;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+  total = __shfl_sync(0xffffffffu, total, 0);
+  if (lane == 0) mbar_arrive_expect_tx(bar, total);
+  __syncwarp();
+  if (lane < 16) bulk_g2s(slot + lane * p.pitch, lo, bytes, bar);
+}
+
+template <int WT, int XT, int EPI>
+__global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
   constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NW = blockDim.x >> 5, S = p.nslots;
   const int ncols = (XT == XT_F32) ? 2 * p.M : p.M;
-  const GemvLayout L = gemv_layout(WT, ncols, p.K, p.nstages, p.pitch, p.xpitch);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + GEMV_MAXST;
-  int* misc = reinterpret_cast<int*>(smem + L.off_misc);
-  volatile int* abort_flag = misc + 32;
-  uint8_t* ring = smem + L.off_ring;
-  const int NST = p.nstages;
-  const int stage_bytes = 16 * p.pitch;
+  const GemvLayout L = gemv_layout(WT, ncols, p.K, p.xg, NW, S, p.pitch, p.xpitch);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * GEMV_MAXS;
+  uint8_t* ring = smem + L.off_ring + warp * S * 16 * p.pitch;
+  __shared__ float red[2 * GEMV_MAXW];
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], GEMV_NCW);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
+  if (lane < S) mbar_init(&bars[lane], 1);
+  fence_mbar_init();
+  __syncwarp();
   // the next kernel may be scheduled now; it reads our outputs only after its griddepcontrol.wait
   pdl_launch_dependents();
 
   const bool dyn = (p.group_ids != nullptr) || (p.n_groups_dev != nullptr);
   const int nsb = p.K >> 8;
   const int tpg = (p.N + RPT - 1) / RPT;
-  const int G = gridDim.x, c = blockIdx.x;
+  const int G = gridDim.x, W = G * NW, wid = blockIdx.x * NW + warp;
+  const int stride_slot = 16 * p.pitch;
 
-  if (warp == GEMV_NCW) {
-    // ---------------------------------------------------------------- producer warp
-    if (dyn) pdl_wait();
-    const int ngroups = p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups;
-    const int64_t U = static_cast<int64_t>(ngroups) * tpg * nsb;
-    const int64_t u0 = U * c / G, u1 = U * (c + 1) / G;
-    int i = 0;
-    for (int64_t u = u0; u < u1; ++i) {
-      const int tile = static_cast<int>(u / nsb), sb0 = static_cast<int>(u - static_cast<int64_t>(tile) * nsb);
-      const int len = static_cast<int>(min(static_cast<int64_t>(min(p.kc, nsb - sb0)), u1 - u));
-      const int slot = i % NST;
-      if (i >= NST) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((i / NST) - 1) & 1, p.status, ST_TIMEOUT_EMPTY);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok || *abort_flag) break;
-      }
-      uint32_t bytes = 0;
-      const uint8_t* lo = nullptr;
-      if (lane < 16) {
-        const int grp = tile / tpg, lt = tile - grp * tpg;
-        const uint8_t* src = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, lane) + static_cast<int64_t>(sb0) * UB;
-        lo = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15));
-        const uint32_t head = static_cast<uint32_t>(src - lo);
-        bytes = (head + len * UB + 15u) & ~15u;
-      }
-      uint32_t total = bytes;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], total);
-      __syncwarp();
-      if (lane < 16) bulk_g2s(ring + slot * stage_bytes + lane * p.pitch, lo, bytes, &full[slot]);
-      u += len;
+  // weights are static: without a data-dependent group list, prefetch before waiting on the
+  // previous kernel
+  int64_t U = 0, a = 0, b = 0, ui = 0;
+  int issued = 0;
+  auto setup_range = [&](int ngroups) {
+    U = static_cast<int64_t>(ngroups) * tpg * nsb;
+    a = U * wid / W;
+    b = U * (wid + 1) / W;
+    ui = a;
+  };
+  auto prefetch = [&]() {
+    while (ui < b && issued < S) {
+      const Chunk ch = next_chunk(ui, b, nsb, p.upc);
+      issue_chunk<WT, XT, EPI>(p, ch, tpg, ring + (issued % S) * stride_slot, &bars[issued % S], lane);
+      ui += ch.n;
+      ++issued;
     }
-    // after an abort, never leave with copies in flight: wait for the last issued phase of every slot
-    if (lane == 0 && *abort_flag) {
-      for (int j = max(0, i - NST); j < i; ++j)
-        mbar_wait_bounded(&full[j % NST], (j / NST) & 1, p.status, ST_TIMEOUT_FULL, 200000000LL);
-    }
-    return;
+  };
+  if (!dyn) {
+    setup_range(p.n_groups);
+    prefetch();
+  }
+  pdl_wait();
+  if (dyn) {
+    setup_range(p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
+    prefetch();
+  }
+  // stage the activations of every group this CTA touches (one group when x is shared)
+  const int64_t c0 = U * (static_cast<int64_t>(blockIdx.x) * NW) / W;
+  const int64_t c1 = U * (static_cast<int64_t>(blockIdx.x + 1) * NW) / W;
+  const int gfirst = (c1 > c0) ? static_cast<int>((c0 / nsb) / tpg) : 0;
+  const int glast = (c1 > c0) ? static_cast<int>(((c1 - 1) / nsb) / tpg) : 0;
+  if (p.x_group_stride == 0) {
+    gemv_stage_x<WT, XT, EPI>(p, smem, L, 0, 0, ncols, red);
+  } else {
+    for (int g = gfirst; g <= glast && g - gfirst < p.xg; ++g) gemv_stage_x<WT, XT, EPI>(p, smem, L, g, g - gfirst, ncols, red);
   }
 
-  // ------------------------------------------------------------------ consumer warps
-  pdl_wait();
-  const int ngroups = p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups;
-  const int64_t U = static_cast<int64_t>(ngroups) * tpg * nsb;
-  const int64_t u0 = U * c / G, u1 = U * (c + 1) / G;
+  // ------------------------------------------------------------------ per-warp main loop
   const int g = lane >> 2, t = lane & 3;
   const bool colok = g < ncols;
-  float* red = reinterpret_cast<float*>(smem + L.off_red);
+  const int* misc0 = reinterpret_cast<const int*>(smem + L.off_misc);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int staged = -1;
-  int i = 0;
-  for (int64_t u = u0; u < u1; ++i) {
-    const int tile = static_cast<int>(u / nsb), sb0 = static_cast<int>(u - static_cast<int64_t>(tile) * nsb);
-    const int len = static_cast<int>(min(static_cast<int64_t>(min(p.kc, nsb - sb0)), u1 - u));
-    const int grp = tile / tpg, lt = tile - grp * tpg;
-    if (grp != staged) {
-      named_bar_sync(1, GEMV_NCW * 32);
-      gemv_stage_x<WT, XT, EPI>(p, smem, L, grp, ncols);
-      named_bar_sync(1, GEMV_NCW * 32);
-      staged = grp;
-    }
-    const int slot = i % NST;
-    bool ok = !*abort_flag;
-    if (ok) {
-      ok = mbar_wait_bounded(&full[slot], (i / NST) & 1, p.status, ST_TIMEOUT_FULL);
-      if (!ok) *abort_flag = 1;
-    }
-    if (ok && warp < len) {
-      const int sb = sb0 + warp;
-      const uint8_t* st = ring + slot * stage_bytes;
-      const uint8_t* sg = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g) + static_cast<int64_t>(sb0) * UB;
-      const uint8_t* s8 = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g + 8) + static_cast<int64_t>(sb0) * UB;
-      const uint8_t* rg = st + g * p.pitch + (reinterpret_cast<uintptr_t>(sg) & 15u) + warp * UB;
-      const uint8_t* r8 = st + (g + 8) * p.pitch + (reinterpret_cast<uintptr_t>(s8) & 15u) + warp * UB;
-      const uint8_t* xcol = smem + L.off_xs + g * p.xpitch;
+  int consumed = 0;
+  bool ok = true;
+  for (int64_t uc = a; uc < b;) {
+    const Chunk ch = next_chunk(uc, b, nsb, p.upc);
+    const int slot = consumed % S;
+    ok = mbar_wait_bounded(&bars[slot], (consumed / S) & 1, p.status, ST_TIMEOUT_FULL);
+    if (!ok) break;
+    const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
+    const int xsl = (p.x_group_stride == 0) ? 0 : grp - gfirst;
+    const uint8_t* st = ring + slot * stride_slot;
+    const uint8_t* sg = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g) + static_cast<int64_t>(ch.sb) * UB;
+    const uint8_t* s8 = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g + 8) + static_cast<int64_t>(ch.sb) * UB;
+    const uint8_t* rg = st + g * p.pitch + (reinterpret_cast<uintptr_t>(sg) & 15u);
+    const uint8_t* r8 = st + (g + 8) * p.pitch + (reinterpret_cast<uintptr_t>(s8) & 15u);
+    const uint8_t* xcol = smem + L.off_xs + (xsl * ncols + g) * p.xpitch;
+    for (int i = 0; i < ch.n; ++i) {
+      const int sb = ch.sb + i;
       if (WT == WT_Q4K) {
-        const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + g * nsb * 32);
-        unit_q4k(rg, r8, xcol, sxcol, colok, sb, t, acc);
+        const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + (xsl * ncols + g) * nsb * 32);
+        unit_q4k(rg + i * UB, r8 + i * UB, xcol, sxcol, colok, sb, t, acc);
       } else if (WT == WT_Q6K) {
-        unit_q6k(rg, r8, xcol, colok, sb, t, acc);
+        unit_q6k(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
       } else if (WT == WT_Q80) {
-        unit_q80(rg, r8, xcol, colok, sb, t, acc);
+        unit_q80(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
       } else {
-        unit_f16(rg, r8, xcol, colok, sb, t, acc);
+        unit_f16(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-    u += len;
-    if (sb0 + len == nsb || u == u1) {
-      // ---------------- this CTA's segment of `tile` is done: reduce the warps in order
-      const int64_t seg0 = max(u0, static_cast<int64_t>(tile) * nsb);
-      const bool whole = (seg0 == static_cast<int64_t>(tile) * nsb) && (u == static_cast<int64_t>(tile + 1) * nsb);
-      *reinterpret_cast<float4*>(red + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      named_bar_sync(1, GEMV_NCW * 32);
-      if (warp == 0) {
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int w = 0; w < GEMV_NCW; ++w) {
-          const float4 r = *reinterpret_cast<const float4*>(red + (w * 32 + lane) * 4);
-          v[0] = __fadd_rn(v[0], r.x);
-          v[1] = __fadd_rn(v[1], r.y);
-          v[2] = __fadd_rn(v[2], r.z);
-          v[3] = __fadd_rn(v[3], r.w);
-        }
-        if (whole) {
-          gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, v, lane);
-        } else {
-          const int slot2 = (tile == static_cast<int>(u0 / nsb)) ? 0 : 1;
-          *reinterpret_cast<float4*>(p.partials + ((static_cast<int64_t>(c) * 2 + slot2) * 32 + lane) * 4) =
-              make_float4(v[0], v[1], v[2], v[3]);
+    ++consumed;
+    uc += ch.n;
+    prefetch();  // refill the slot just freed
+    if (ch.sb + ch.n == nsb || uc == b) {
+      // ---------------- this worker's piece of `tile` is done
+      const int64_t seg0 = max(a, static_cast<int64_t>(ch.tile) * nsb);
+      const bool whole = (seg0 == static_cast<int64_t>(ch.tile) * nsb) && (uc == static_cast<int64_t>(ch.tile + 1) * nsb);
+      const int* misc = misc0 + xsl * 8;
+      if (whole) {
+        gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, acc, lane);
+      } else {
+        const int slot2 = (ch.tile == static_cast<int>(a / nsb)) ? 0 : 1;
+        *reinterpret_cast<float4*>(p.partials + ((static_cast<int64_t>(wid) * 2 + slot2) * 32 + lane) * 4) =
+            make_float4(acc[0], acc[1], acc[2], acc[3]);
+        __threadfence();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&p.counters[ch.tile], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        const int wf = worker_of_unit(static_cast<int64_t>(ch.tile) * nsb, U, W);
+        const int wl = worker_of_unit(static_cast<int64_t>(ch.tile + 1) * nsb - 1, U, W);
+        if (old == wl - wf) {
           __threadfence();
-          __syncwarp();
-          int old = 0;
-          if (lane == 0) old = atomicAdd(&p.counters[tile], 1);
-          old = __shfl_sync(0xffffffffu, old, 0);
-          const int cf = cta_of_unit(static_cast<int64_t>(tile) * nsb, U, G);
-          const int cl = cta_of_unit(static_cast<int64_t>(tile + 1) * nsb - 1, U, G);
-          if (old == cl - cf) {
-            __threadfence();
-            float w4[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int cc = cf; cc <= cl; ++cc) {
-              const int s2 = (tile == static_cast<int>((U * cc / G) / nsb)) ? 0 : 1;
-              const float4 r = __ldcg(reinterpret_cast<const float4*>(
-                  p.partials + ((static_cast<int64_t>(cc) * 2 + s2) * 32 + lane) * 4));
-              w4[0] = __fadd_rn(w4[0], r.x);
-              w4[1] = __fadd_rn(w4[1], r.y);
-              w4[2] = __fadd_rn(w4[2], r.z);
-              w4[3] = __fadd_rn(w4[3], r.w);
-            }
-            gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, w4, lane);
-            if (lane == 0) p.counters[tile] = 0;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int w2 = wf; w2 <= wl; ++w2) {
+            const int s2 = (ch.tile == static_cast<int>((U * w2 / W) / nsb)) ? 0 : 1;
+            const float4 r = __ldcg(reinterpret_cast<const float4*>(
+                p.partials + ((static_cast<int64_t>(w2) * 2 + s2) * 32 + lane) * 4));
+            v[0] = __fadd_rn(v[0], r.x);
+            v[1] = __fadd_rn(v[1], r.y);
+            v[2] = __fadd_rn(v[2], r.z);
+            v[3] = __fadd_rn(v[3], r.w);
           }
+          gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, v, lane);
+          if (lane == 0) p.counters[ch.tile] = 0;
         }
       }
-      named_bar_sync(1, GEMV_NCW * 32);
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
     }
+  }
+  if (!ok) {
+    // a bounded wait gave up: never leave with this warp's copies in flight
+    for (int j = consumed; j < issued; ++j)
+      mbar_wait_bounded(&bars[j % S], (j / S) & 1, p.status, ST_TIMEOUT_FULL, 200000000LL);
   }
 }
 
 // ------------------------------------------------------------------ host launch
 template <int WT, int XT, int EPI>
-static int launch_one(GemvParams p, int grid, int smem, cudaStream_t stream, bool pdl) {
+static int launch_one(GemvParams p, int grid, int nw, int smem, cudaStream_t stream, bool pdl) {
   auto kern = gemv_kernel<WT, XT, EPI>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024);
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(gemv)");
     attr_set[dev & 63] = true;
   }
-  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(GEMV_THREADS), smem, stream, pdl, &p);
+  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(nw * 32), smem, stream, pdl, &p);
 }
+
+// units per slot: rows of at least ~288 bytes per bulk copy keep the copy engine efficient
+static int gemv_upc(int wt) { return wt == WT_Q4K ? 2 : wt == WT_Q6K ? 2 : wt == WT_Q80 ? 2 : 1; }
 
 int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl) {
   const int ncols = (xt == XT_F32) ? 2 * p.M : p.M;
   if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ncols > 8) return set_error(-1, "gemv: bad shape");
   if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
-  const int xb = p.K * 2;
-  p.xpitch = ((xb + 127) & ~127) + 64;
-  int nst = 0;
-  for (p.kc = GEMV_KC; p.kc >= 1; p.kc >>= 1) {
-    p.pitch = gemv_stage_pitch(wt, p.kc);
-    GemvLayout L0 = gemv_layout(wt, ncols, p.K, 0, p.pitch, p.xpitch);
-    nst = (232448 - L0.off_ring) / (16 * p.pitch);
-    if (nst >= 2) break;
-  }
-  if (nst > GEMV_MAXST) nst = GEMV_MAXST;
-  if (nst < 2) return set_error(-1, "gemv: activation block too large for shared memory");
-  p.nstages = nst;
-  const int smem = gemv_layout(wt, ncols, p.K, nst, p.pitch, p.xpitch).total;
+  if ((reinterpret_cast<uintptr_t>(p.x) & 15u) != 0) return set_error(-1, "gemv: activations must be 16-byte aligned");
   const int rpt = (epi == EPI_SWIGLU) ? 8 : 16;
-  const int64_t U = static_cast<int64_t>(p.n_groups) * ((p.N + rpt - 1) / rpt) * (p.K / 256);
-  int grid = static_cast<int>(std::min<int64_t>(num_sms, U));
+  const int64_t upg = static_cast<int64_t>((p.N + rpt - 1) / rpt) * (p.K / 256);
+  const int64_t U = static_cast<int64_t>(p.n_groups) * upg;
+  int grid = static_cast<int>(std::min<int64_t>(num_sms, (U + 1) / 2));
   if (grid < 1) grid = 1;
+  p.upc = gemv_upc(wt);
+  p.pitch = gemv_slot_pitch(wt, p.upc);
+  p.xpitch = ((p.K * 2 + 127) & ~127) + 64;
+  if (p.x_group_stride == 0) {
+    p.xg = 1;
+  } else {
+    const int64_t per_cta = (U + grid - 1) / grid;
+    p.xg = static_cast<int>(std::min<int64_t>(p.n_groups, (per_cta + upg - 1) / upg + 1));
+    if (p.xg > GEMV_MAXXG) return set_error(-1, "gemv: too many activation groups per CTA");
+  }
+  const int limit = 232448 - 1024 - 2 * GEMV_MAXW * 4;  // dynamic smem limit minus static
+  int nw = 0, ns = 0;
+  for (int cand_w : {16, 12, 8, 4}) {
+    for (int cand_s = GEMV_MAXS; cand_s >= 2; --cand_s) {
+      if (gemv_layout(wt, ncols, p.K, p.xg, cand_w, cand_s, p.pitch, p.xpitch).total <= limit) {
+        nw = cand_w;
+        ns = cand_s;
+        break;
+      }
+    }
+    if (nw) break;
+  }
+  if (!nw) return set_error(-1, "gemv: activation block too large for shared memory");
+  p.nslots = ns;
+  const int smem = gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch).total;
 #define AIPU_GEMV_CASE(W, X, E)                                              \
-  if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, smem, stream, pdl);
+  if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, nw, smem, stream, pdl);
   AIPU_GEMV_CASE(WT_Q4K, XT_BF16, EPI_STORE)
   AIPU_GEMV_CASE(WT_Q4K, XT_F32, EPI_STORE)
   AIPU_GEMV_CASE(WT_Q6K, XT_BF16, EPI_STORE)
@@ -678,6 +708,7 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   return set_error(-1, "gemv: unsupported weight/activation type combination");
 }
 
-int gemv_partials_floats(int num_sms) { return num_sms * 2 * 128; }
+// stream-K workspace: one partial tile (32 lanes x 4 floats) per (worker, first/last tile)
+int gemv_partials_floats(int num_sms) { return num_sms * GEMV_MAXW * 2 * 128; }
 
 }  // namespace aipu

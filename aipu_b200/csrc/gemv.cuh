@@ -7,20 +7,23 @@
 // strict kernel in kernels.cu is the bit-exact one).
 //
 // Design (HBM-bound: ~0.56 B/weight for Q4_K, so the budget is ~3 thread-ops per weight):
-//   * Persistent grid, one CTA per SM: 16 consumer warps + 1 producer warp.
+//   * Persistent grid, one CTA per SM, NW (8..16) fully decoupled warps. There is no producer warp
+//     and no CTA-wide barrier in the main loop: every warp is its own "worker".
 //   * Work unit = 16 weight rows x 256 weights (one super-block column). The units of all tiles are
-//     laid end to end and split evenly over the CTAs ("stream-K"); a tile cut between CTAs is
-//     finished by the last CTA to arrive, which sums the partials in CTA order (deterministic).
-//   * The producer streams each chunk (16 rows x up to 16 units) with 1-D bulk copies
-//     (cp.async.bulk, the untiled TMA path; no multicast) into a multi-stage shared-memory ring,
-//     completion tracked by mbarriers. Weights do not depend on the previous kernel, so with
-//     programmatic dependent launch the ring fills before griddepcontrol.wait.
+//     laid end to end and split evenly over all workers of the grid ("stream-K" at warp level); a
+//     tile cut between workers is finished by the last worker to arrive, which sums the partials in
+//     worker order (deterministic).
+//   * Each warp streams its own chunks (16 rows x up to UPC units) into a private S-slot ring with
+//     1-D bulk copies (cp.async.bulk, the untiled TMA path; no multicast): lanes 0..15 each copy one
+//     row, completion on a per-slot mbarrier. Weights do not depend on the previous kernel, so with
+//     programmatic dependent launch the first slots fill before griddepcontrol.wait.
 //   * Consumers turn packed codes into exact fp16 operands with LOP3/PRMT magic-number tricks and
 //     use mma.sync m16n8k16 (fp16 in, fp32 accumulate) as an exact-product dot engine: weight rows
 //     are the 16 MMA rows, activation columns (tokens, or hi/lo halves of fp32 tokens) the 8 MMA
 //     columns.
-//   * Activations are staged once per CTA as fp16 with a per-token power-of-two prescale (exact
-//     for bf16 input; fp32 input is split into hi + lo fp16 columns).
+//   * Activations are staged once per CTA (per group the CTA touches, when groups have their own
+//     activations) as fp16 with a per-token power-of-two prescale (exact for bf16 input; fp32
+//     input is split into hi + lo fp16 columns).
 //   * Q4_K: A = sc*q (exact in fp16, <= 945), so one fp32 accumulator per super-block, then
 //     acc += d*P - dmin*Cm, where Cm = sum_j m_j * sum_{k in j} x_k comes from one more MMA with
 //     A = m (6-bit mins) and B = per-sub-block activation sums (hi/lo fp16).
@@ -30,10 +33,9 @@
 
 namespace aipu {
 
-constexpr int GEMV_NCW = 16;                      // consumer warps
-constexpr int GEMV_THREADS = (GEMV_NCW + 1) * 32;
-constexpr int GEMV_KC = GEMV_NCW;                 // units per stage (one per consumer warp)
-constexpr int GEMV_MAXST = 16;
+constexpr int GEMV_MAXW = 16;   // warps per CTA (each an independent worker)
+constexpr int GEMV_MAXS = 4;    // ring slots per warp
+constexpr int GEMV_MAXXG = 4;   // activation groups staged per CTA
 
 enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1 };
 
@@ -55,15 +57,19 @@ struct GemvParams {
   float* partials;           // stream-K workspace [grid][2][32][4]
   int* counters;             // stream-K arrival counters, one per tile, zero between launches
   int* status;               // device status word
-  int kc;                    // units (256-weight columns) per stage, <= GEMV_KC
-  int pitch;                 // shared-memory row pitch of a stage
-  int nstages;               // ring depth
+  int upc;                   // units (256-weight columns) per ring slot
+  int pitch;                 // shared-memory row pitch of a slot
+  int nslots;                // ring slots per warp
   int xpitch;                // shared-memory bytes per activation column
+  int xg;                    // activation groups staged per CTA (1 when x is shared by all groups)
 };
 
-__host__ __device__ inline int gemv_stage_pitch(int wt, int kc) {
-  int p0 = ((kc * unit_bytes(wt) + 16) + 15) & ~15;
-  return p0 + (((32 - p0 % 128) % 128) + 128) % 128;  // pitch = 32 mod 128 (bank spread)
+__host__ __device__ inline int gemv_slot_pitch(int wt, int upc) {
+  // room for the unit bytes plus a possible 16-byte-alignment head, rounded so that rows start
+  // 32 or 96 bytes mod 128 (rows g = 0..3 of a half-warp then hit distinct banks)
+  int p = (upc * unit_bytes(wt) + ((wt == WT_Q6K) ? 15 : 0) + 15) & ~15;
+  while (p % 128 != 32 && p % 128 != 96) p += 16;
+  return p;
 }
 
 // ---------------------------------------------------------------------------------- x staging

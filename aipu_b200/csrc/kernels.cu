@@ -2,6 +2,8 @@
 // top-K, and the MoE weighted combine. Each follows the reference golden op for op.
 #include <cstdio>
 
+#include <cudaTypedefs.h>
+
 #include "act.cuh"
 #include "deq.cuh"
 #include "kernels.h"
@@ -193,7 +195,7 @@ constexpr int RT_MB = 8;        // tokens per CTA
 constexpr int RT_WBYTES = RT_CHUNK * 32 * 4;
 constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
 
-__global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const RouterParams p) {
+__global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const __grid_constant__ RouterParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + RT_NST;
@@ -218,8 +220,6 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const R
   if (warp == RT_MB) {
     // producer: W[k0:k0+128, e0:e0+32] rows and x[m0+m, k0:k0+128] slices
     if (!dense) return;
-    const int ne = min(32, E - e0);
-    const uint32_t wrow = static_cast<uint32_t>((ne * 4 + 15) & ~15);
     for (int c = 0; c < nchunk; ++c) {
       const int slot = c % RT_NST;
       if (c >= RT_NST) {
@@ -229,12 +229,17 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const R
       }
       const int k0 = c * RT_CHUNK, kl = min(RT_CHUNK, K - k0);
       const uint32_t xrow = static_cast<uint32_t>((kl * 2 + 15) & ~15);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], wrow * kl + xrow * mb);
-      __syncwarp();
       uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
-      const float* W = reinterpret_cast<const float*>(p.w);
-      for (int r = lane; r < kl; r += 32)
-        bulk_g2s(st + r * 128, W + static_cast<int64_t>(k0 + r) * E + e0, wrow, &full[slot]);
+      if (lane == 0) {
+        // one tiled TMA request for the whole 128-row x 32-expert box (out-of-range parts read 0)
+        mbar_arrive_expect_tx(&full[slot], RT_WBYTES + xrow * mb);
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+                "r"(smem_u32(st)),
+            "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(e0), "r"(k0), "r"(smem_u32(&full[slot]))
+            : "memory");
+      }
+      __syncwarp();
       if (lane < mb)
         bulk_g2s(st + RT_WBYTES + lane * RT_CHUNK * 2, p.x + static_cast<int64_t>(m0 + lane) * K + k0, xrow,
                  &full[slot]);
@@ -312,6 +317,24 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
     attr = true;
   }
   RouterParams q = p;
+  if (p.wt == WT_F32) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+      cudaDriverEntryPointQueryResult qr;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault,
+                                  &qr) != cudaSuccess ||
+          qr != cudaDriverEntryPointSuccess || !encode)
+        return set_error(ECUDA_, "router: cuTensorMapEncodeTiled unavailable");
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.K)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.E) * 4};
+    const cuuint32_t box[2] = {32, RT_CHUNK};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&q.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<uint8_t*>(p.w), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(ECUDA_, "router: tensor map encoding failed");
+  }
   return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel), dim3((p.E + 31) / 32, (p.M + RT_MB - 1) / RT_MB),
                        dim3(32 * (RT_MB + 1)), smem, s, pdl, &q);
 }

@@ -1,6 +1,7 @@
 // Launch prototypes and parameter blocks of the exact kernels and the decode GEMV.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace aipu {
@@ -23,6 +24,7 @@ struct RouterParams {
   int32_t* slot_map;       // [M, topk] index of sel[m, s] in union_ids
   int* counters;           // [token blocks + 1] arrival counters, zero between launches
   int* status;             // device status word
+  alignas(64) CUtensorMap wmap;  // fp32 router: 2-D tiled map over W [K rows, E cols], box 128 x 32
 };
 
 struct CombineParams {
