@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParam
   // weights are static: without a data-dependent group list, prefetch before waiting on the
   // previous kernel
   int64_t U = 0, a = 0, b = 0, ui = 0;
-  int issued = 0;
+  int issued = 0, consumed = 0;
   auto setup_range = [&](int ngroups) {
     U = static_cast<int64_t>(ngroups) * tpg * nsb;
     a = U * wid / W;
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParam
     ui = a;
   };
   auto prefetch = [&]() {
-    while (ui < b && issued < S) {
+    while (ui < b && issued - consumed < S) {
       const Chunk ch = next_chunk(ui, b, nsb, p.upc);
       issue_chunk<WT, XT, EPI>(p, ch, tpg, ring + (issued % S) * stride_slot, &bars[issued % S], lane);
       ui += ch.n;
@@ -563,7 +563,6 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParam
   const bool colok = g < ncols;
   const int* misc0 = reinterpret_cast<const int*>(smem + L.off_misc);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int consumed = 0;
   bool ok = true;
   for (int64_t uc = a; uc < b;) {
     const Chunk ch = next_chunk(uc, b, nsb, p.upc);
@@ -613,10 +612,14 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParam
         old = __shfl_sync(0xffffffffu, old, 0);
         const int wf = worker_of_unit(static_cast<int64_t>(ch.tile) * nsb, U, W);
         const int wl = worker_of_unit(static_cast<int64_t>(ch.tile + 1) * nsb - 1, U, W);
-        if (old == wl - wf) {
+        // workers with an empty range (more workers than units) hold no piece
+        int npieces = 0;
+        for (int w2 = wf; w2 <= wl; ++w2) npieces += (U * w2 / W < U * (w2 + 1) / W) ? 1 : 0;
+        if (old == npieces - 1) {
           __threadfence();
           float v[4] = {0.f, 0.f, 0.f, 0.f};
           for (int w2 = wf; w2 <= wl; ++w2) {
+            if (U * w2 / W == U * (w2 + 1) / W) continue;
             const int s2 = (ch.tile == static_cast<int>((U * w2 / W) / nsb)) ? 0 : 1;
             const float4 r = __ldcg(reinterpret_cast<const float4*>(
                 p.partials + ((static_cast<int64_t>(w2) * 2 + s2) * 32 + lane) * 4));
@@ -665,7 +668,8 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   const int rpt = (epi == EPI_SWIGLU) ? 8 : 16;
   const int64_t upg = static_cast<int64_t>((p.N + rpt - 1) / rpt) * (p.K / 256);
   const int64_t U = static_cast<int64_t>(p.n_groups) * upg;
-  int grid = static_cast<int>(std::min<int64_t>(num_sms, (U + 1) / 2));
+  // at least one unit per worker of a full CTA, so small problems do not spread into empty workers
+  int grid = static_cast<int>(std::min<int64_t>(num_sms, (U + GEMV_MAXW - 1) / GEMV_MAXW));
   if (grid < 1) grid = 1;
   p.upc = gemv_upc(wt);
   p.pitch = gemv_slot_pitch(wt, p.upc);
