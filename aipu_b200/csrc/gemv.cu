@@ -2,6 +2,7 @@
 #include <algorithm>
 #include <cstdio>
 
+#include "deq.cuh"
 #include "gemv.cuh"
 #include "launch.h"
 
@@ -711,6 +712,76 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
 #undef AIPU_GEMV_CASE
   return set_error(-1, "gemv: unsupported weight/activation type combination");
 }
+
+// ------------------------------------------------------------------ allocation-free variant
+// Scratch for aipu_q4k_gemm_noalloc, owned by the library for the lifetime of the process on every
+// device that loads it: stream-K partials for up to kNoAllocSms CTAs of GEMV_MAXW workers, then one
+// arrival counter per 16-row tile for up to kNoAllocTiles tiles (N <= 65536 rows).
+constexpr int kNoAllocSms = 160;
+constexpr int kNoAllocTiles = 4096;
+constexpr size_t kNoAllocPartialBytes = sizeof(float) * kNoAllocSms * GEMV_MAXW * 2 * 128;  // 2.5 MiB
+constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + sizeof(int) * kNoAllocTiles;        // + 16 KiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+}  // namespace aipu
+
+extern "C" int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype,
+                                     int64_t M, void* y, void* stream) {
+  using namespace aipu;
+  if (!w || !x || !y || N <= 0 || M <= 0 || K <= 0 || K % 256 || K > INT32_MAX ||
+      (wtype != WT_Q4K && wtype != WT_Q6K && wtype != WT_Q80 && wtype != WT_F16) ||
+      (x_dtype != XT_F32 && x_dtype != XT_BF16))
+    return set_error(EINVAL_, "gemm_noalloc: bad arguments");
+  if ((N + 15) / 16 > kNoAllocTiles)
+    return set_error(EINVAL_, "gemm_noalloc: N exceeds the static scratch limit of 65536 rows");
+  if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0) return set_error(EINVAL_, "gemm_noalloc: weights must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaGetDevice");
+  // device address of the scratch array, resolved once per device with that device current (in
+  // host code the array's name is only a host-side stand-in, never a device address)
+  static unsigned char* scratch_ptr[64] = {nullptr};
+  static int sms[64] = {0};
+  if (dev < 0 || dev >= 64) return set_error(EINVAL_, "gemm_noalloc: device index out of range");
+  if (!scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaGetSymbolAddress");
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaDeviceGetAttribute");
+    sms[dev] = n < kNoAllocSms ? n : kNoAllocSms;
+    scratch_ptr[dev] = static_cast<unsigned char*>(ptr);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* partials = reinterpret_cast<float*>(scratch_ptr[dev]);
+  int* counters = reinterpret_cast<int*>(scratch_ptr[dev] + kNoAllocPartialBytes);
+  const int mb = (x_dtype == XT_F32) ? 4 : 8;
+  const int esz = (x_dtype == XT_F32) ? 4 : 2;
+  for (int64_t m0 = 0; m0 < M; m0 += mb) {
+    // the counters must start at zero; an earlier call that gave up a bounded wait may have left
+    // some set, so clear them before every launch (no allocation involved)
+    e = cudaMemsetAsync(counters, 0, sizeof(int) * ((N + 15) / 16), s);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaMemsetAsync");
+    GemvParams p = {};
+    p.w0 = static_cast<const uint8_t*>(w);
+    p.row_bytes = row_bytes_of(wtype, K);
+    p.n_groups = 1;
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.x = static_cast<const uint8_t*>(x) + m0 * K * esz;
+    p.M = static_cast<int>(M - m0 < mb ? M - m0 : mb);
+    p.y = static_cast<uint16_t*>(y) + m0 * N;
+    p.partials = partials;
+    p.counters = counters;
+    p.status = nullptr;
+    const int rc = gemv_launch(wtype, x_dtype, EPI_STORE, p, sms[dev], s, false);
+    if (rc) return rc;
+  }
+  return OK;
+}
+
+namespace aipu {
 
 // stream-K workspace: one partial tile (32 lanes x 4 floats) per (worker, first/last tile)
 int gemv_partials_floats(int num_sms) { return num_sms * GEMV_MAXW * 2 * 128; }

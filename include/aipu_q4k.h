@@ -91,6 +91,21 @@ int aipu_act_eval(int kind, const void* x, int64_t n, void* out, void* stream);
 int aipu_q4k_gemm(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype,
                   int64_t M, void* y, float* y_f32, int mode, void* stream);
 
+/* Allocation-free fast GEMM, for callers that cannot call cudaMalloc: hosts whose allocator has
+ * already reserved the device memory (a serving engine that owns all of HBM through its own pool),
+ * plug-ins that must not create or keep a context object, and latency-critical paths where the
+ * device-wide synchronisation of cudaMalloc/cudaFree is unacceptable. Same inputs, outputs and
+ * numerics as aipu_q4k_gemm in AIPU_MODE_FAST (x_dtype AIPU_DT_F32 or AIPU_DT_BF16; wtype Q4_K,
+ * Q6_K, Q8_0 or F16; K a multiple of 256), but its scratch (stream-K partial sums and arrival
+ * counters, about 2.5 MiB) is a static array inside the library, held by every GPU that loads the
+ * library until the process exits. Limit: N <= 65536 rows (larger N is rejected with
+ * AIPU_EINVAL). The first call on a device looks up the array's device address (make that first
+ * call before any stream capture). All calls share the one array: calls that overlap on the GPU
+ * (different streams, or other threads) race and corrupt each other; serialise them. No
+ * counterpart in the reference. */
+int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype, int64_t M,
+                          void* y, void* stream);
+
 /* Grouped fast GEMM: n_mats independent matrices of N rows x K (matrix g at w + g * mat_stride
  * bytes) applied to the same activations x[M, K] in ONE launch; y[g, M, N] (bf16). This is the
  * decode pattern of several projections or experts fed by the same token rows (e.g. all experts of
