@@ -5,6 +5,8 @@
 #include <mutex>
 #include <string>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/aipu_q4k.h"
 #include "common.cuh"
 #include "deq.cuh"
@@ -42,6 +44,24 @@ int launch_kernel(const void* kern, dim3 grid, dim3 block, int smem, cudaStream_
   }
   void* args[1] = {arg0};
   return set_cuda_error(cudaLaunchKernelExC(&cfg, kern, args), "cudaLaunchKernelExC");
+}
+
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides, const cuuint32_t* box) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &qr) !=
+            cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess || !encode)
+      return set_error(ECUDA_, "cuTensorMapEncodeTiled unavailable");
+  }
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ECUDA_, "tensor map encoding failed");
+  return OK;
 }
 
 int num_sms_of_current_device() {
@@ -248,6 +268,7 @@ extern "C" int aipu_q4k_gemm_grouped(aipu_ctx* c, int wtype, const void* w, int6
     p.w0 = static_cast<const uint8_t*>(w);
     p.row_bytes = row_bytes_of(wtype, K);
     p.expert_stride = mat_stride;
+    p.n_experts = static_cast<int>(n_mats);
     p.n_groups = static_cast<int>(n_mats);
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
@@ -352,7 +373,8 @@ static int moe_scratch(aipu_ctx* c, int64_t M, int64_t E, int T, int64_t H, int6
 
 // SwiGLU on groups of experts: h[g] = bf16(silu(x Wg_e) * (x Wu_e)), y[g] = h[g] Wd_e
 static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, const void* uw, int dwt, const void* dw,
-                         int64_t H, int64_t F, const int* group_ids, const int* n_groups_dev, int n_groups,
+                         int64_t H, int64_t F, int n_experts, const int* group_ids, const int* n_groups_dev,
+                         int n_groups,
                          const void* x, int64_t M, uint16_t* h, uint16_t* y, cudaStream_t s, bool pdl) {
   const int64_t gstride = F * row_bytes_of(gwt, H), dstride = H * row_bytes_of(dwt, F);
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
@@ -363,6 +385,7 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
     p.row_bytes = row_bytes_of(gwt, H);
     p.expert_stride = gstride;
     p.group_ids = group_ids;
+    p.n_experts = n_experts;
     p.n_groups_dev = n_groups_dev;
     p.n_groups = n_groups;
     p.N = static_cast<int>(F);
@@ -414,7 +437,7 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
     if ((rc = set_cuda_error(cudaEventRecord(c->ev_fork, s), "eventRecord"))) return rc;
     if ((rc = set_cuda_error(cudaStreamWaitEvent(c->side, c->ev_fork, 0), "streamWaitEvent"))) return rc;
     rc = swiglu_groups(c, c->ws[1], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
-                       H, F, nullptr, nullptr, 1, x, M, sc.h_sh, sc.y_sh, c->side, false);
+                       H, F, 1, nullptr, nullptr, 1, x, M, sc.h_sh, sc.y_sh, c->side, false);
     if (rc) return rc;
     if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
   }
@@ -438,7 +461,7 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
   rp.status = c->status;
   if ((rc = router_launch(rp, s, false))) return rc;
   const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
-  rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F, sc.union_ids,
+  rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F, static_cast<int>(E), sc.union_ids,
                      sc.n_union, Umax, x, M, sc.h, sc.y, s, true);
   if (rc) return rc;
   if (shared && (rc = set_cuda_error(cudaStreamWaitEvent(s, c->ev_join, 0), "streamWaitEvent"))) return rc;
@@ -475,7 +498,7 @@ extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt,
       return set_error(ENOMEM_, "swiglu: scratch");
     hb = tmp;
   }
-  int rc = swiglu_groups(c, c->ws[0], gwt, gw, uw, dwt, dw, H, F, nullptr, nullptr, 1, x, M, hb,
+  int rc = swiglu_groups(c, c->ws[0], gwt, gw, uw, dwt, dw, H, F, 1, nullptr, nullptr, 1, x, M, hb,
                          static_cast<uint16_t*>(y), s, false);
   if (tmp) cudaFreeAsync(tmp, s);
   return rc;

@@ -479,6 +479,20 @@ template <int WT, int XT, int EPI>
 __device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch, int tpg, uint8_t* slot,
                                             uint64_t* bar, int lane) {
   constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
+  constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
+  if (p.use_tmap) {
+    // one tiled request covers all 16 rows (two 8-row requests for gate/up), aligned down to 16 B
+    if (lane == 0) {
+      const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
+      const int e = p.group_ids ? p.group_ids[grp] : grp;
+      const int x = ((ch.sb * UB) & ~15) / p.tm_esz;
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(16 * p.tm_box * p.tm_esz));
+      tma_load_3d(slot, &p.tmap0, x, lt * RPT, e, bar);
+      if (EPI == EPI_SWIGLU) tma_load_3d(slot + 8 * p.pitch, &p.tmap1, x, lt * RPT, e, bar);
+    }
+    __syncwarp();
+    return;
+  }
   uint32_t bytes = 0;
   const uint8_t* lo = nullptr;
   if (lane < 16) {
@@ -497,7 +511,7 @@ __device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch
 }
 
 template <int WT, int XT, int EPI>
-__global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
   constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
@@ -573,10 +587,16 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const GemvParam
     const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
     const int xsl = (p.x_group_stride == 0) ? 0 : grp - gfirst;
     const uint8_t* st = ring + slot * stride_slot;
-    const uint8_t* sg = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g) + static_cast<int64_t>(ch.sb) * UB;
-    const uint8_t* s8 = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g + 8) + static_cast<int64_t>(ch.sb) * UB;
-    const uint8_t* rg = st + g * p.pitch + (reinterpret_cast<uintptr_t>(sg) & 15u);
-    const uint8_t* r8 = st + (g + 8) * p.pitch + (reinterpret_cast<uintptr_t>(s8) & 15u);
+    uint32_t hg, h8;
+    if (p.use_tmap) {
+      hg = h8 = static_cast<uint32_t>(ch.sb * UB) & 15u;  // rows are 16-byte multiples: same head for all
+    } else {
+      hg = reinterpret_cast<uintptr_t>(gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g) + static_cast<int64_t>(ch.sb) * UB) & 15u;
+      h8 = reinterpret_cast<uintptr_t>(gemv_row_ptr<WT, XT, EPI>(p, grp, lt, g + 8) + static_cast<int64_t>(ch.sb) * UB) &
+           15u;
+    }
+    const uint8_t* rg = st + g * p.pitch + hg;
+    const uint8_t* r8 = st + (g + 8) * p.pitch + h8;
     const uint8_t* xcol = smem + L.off_xs + (xsl * ncols + g) * p.xpitch;
     for (int i = 0; i < ch.n; ++i) {
       const int sb = ch.sb + i;
@@ -674,6 +694,27 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   if (grid < 1) grid = 1;
   p.upc = gemv_upc(wt);
   p.pitch = gemv_slot_pitch(wt, p.upc);
+  // tiled TMA path when rows (and experts) start on 16-byte boundaries
+  const int ne_map = p.n_experts > 0 ? p.n_experts : p.n_groups;
+  const bool aligned = (p.row_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(p.w0) % 16 == 0) &&
+                       (!p.w1 || reinterpret_cast<uintptr_t>(p.w1) % 16 == 0) &&
+                       (ne_map <= 1 || p.expert_stride % 16 == 0);
+  p.use_tmap = aligned ? 1 : 0;
+  if (p.use_tmap) {
+    p.tm_esz = (wt == WT_Q6K) ? 2 : 8;
+    p.tm_box = (wt == WT_Q4K) ? 36 : (wt == WT_Q6K) ? 240 : 68;
+    p.pitch = p.tm_box * p.tm_esz;
+    const int ne = ne_map;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.row_bytes / p.tm_esz), static_cast<cuuint64_t>(p.N),
+                                static_cast<cuuint64_t>(ne)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.row_bytes),
+                                   static_cast<cuuint64_t>(ne > 1 ? p.expert_stride : p.row_bytes * p.N)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(p.tm_box), static_cast<cuuint32_t>(rpt), 1};
+    const CUtensorMapDataType dt = (wt == WT_Q6K) ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64;
+    int rc = encode_tiled(&p.tmap0, dt, 3, p.w0, dims, strides, box);
+    if (!rc && epi == EPI_SWIGLU) rc = encode_tiled(&p.tmap1, dt, 3, p.w1, dims, strides, box);
+    if (rc) return rc;
+  }
   p.xpitch = ((p.K * 2 + 127) & ~127) + 64;
   if (p.x_group_stride == 0) {
     p.xg = 1;

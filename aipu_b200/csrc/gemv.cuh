@@ -28,6 +28,8 @@
 //     acc += d*P - dmin*Cm, where Cm = sum_j m_j * sum_{k in j} x_k comes from one more MMA with
 //     A = m (6-bit mins) and B = per-sub-block activation sums (hi/lo fp16).
 #pragma once
+#include <cuda.h>
+
 #include "act.cuh"
 #include "common.cuh"
 
@@ -62,6 +64,12 @@ struct GemvParams {
   int nslots;                // ring slots per warp
   int xpitch;                // shared-memory bytes per activation column
   int xg;                    // activation groups staged per CTA (1 when x is shared by all groups)
+  int n_experts;             // extent of the expert dimension of w0/w1 (tensor maps)
+  int use_tmap;              // 1: each slot is filled by one tiled TMA request (two for EPI_SWIGLU)
+  int tm_esz;                // tensor-map element size (bytes)
+  int tm_box;                // tensor-map box width (elements)
+  alignas(64) CUtensorMap tmap0;  // [expert][row][row bytes / esz] over w0
+  alignas(64) CUtensorMap tmap1;  // same over w1 (EPI_SWIGLU)
 };
 
 __host__ __device__ inline int gemv_slot_pitch(int wt, int upc) {

@@ -2,7 +2,6 @@
 // top-K, and the MoE weighted combine. Each follows the reference golden op for op.
 #include <cstdio>
 
-#include <cudaTypedefs.h>
 
 #include "act.cuh"
 #include "deq.cuh"
@@ -318,22 +317,11 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
   }
   RouterParams q = p;
   if (p.wt == WT_F32) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-      cudaDriverEntryPointQueryResult qr;
-      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault,
-                                  &qr) != cudaSuccess ||
-          qr != cudaDriverEntryPointSuccess || !encode)
-        return set_error(ECUDA_, "router: cuTensorMapEncodeTiled unavailable");
-    }
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.K)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.E) * 4};
     const cuuint32_t box[2] = {32, RT_CHUNK};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(&q.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<uint8_t*>(p.w), dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(ECUDA_, "router: tensor map encoding failed");
+    const int rc = encode_tiled(&q.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.w, dims, strides, box);
+    if (rc) return rc;
   }
   return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel), dim3((p.E + 31) / 32, (p.M + RT_MB - 1) / RT_MB),
                        dim3(32 * (RT_MB + 1)), smem, s, pdl, &q);

@@ -1,6 +1,7 @@
 // Host-side helpers shared by the launchers: thread-local error text and kernel launch with
 // optional programmatic dependent launch (PDL).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace aipu {
@@ -19,5 +20,11 @@ const char* last_error();
 int launch_kernel(const void* kern, dim3 grid, dim3 block, int smem, cudaStream_t stream, bool pdl, void* arg0);
 
 int num_sms_of_current_device();
+
+// Encode a tiled TMA tensor map (no swizzle, no interleave, OOB reads return 0). The driver entry
+// point is looked up through the runtime, so the library does not link libcuda.
+// dims/box in elements (innermost first); strides in bytes for dims 1..rank-1.
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides, const cuuint32_t* box);
 
 }  // namespace aipu
