@@ -35,11 +35,8 @@ __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* p) {
 }
 
 constexpr uint32_t H2_1024 = 0x64006400u;   // (1024, 1024)
-constexpr uint32_t H2_M1024 = 0xE400E400u;  // (-1024, -1024)
 constexpr uint32_t H2_1056 = 0x64206420u;   // (1056, 1056)
 constexpr uint32_t H2_1152 = 0x64806480u;   // (1152, 1152)
-constexpr uint32_t H2_16TH = 0x2C002C00u;   // (1/16, 1/16)
-constexpr uint32_t H2_M64 = 0xD400D400u;    // (-64, -64)
 
 __device__ __forceinline__ uint32_t byte_pair_sel(int idx) {
   return 0x4040u | static_cast<uint32_t>(idx) | (static_cast<uint32_t>(idx) << 8);
@@ -49,6 +46,19 @@ __device__ __forceinline__ uint32_t byte_pair_sel(int idx) {
 // A unit = 16 weight rows (g and g+8 of this thread) x 256 weights at super-block column `sb`.
 // xcol: this thread's activation column (fp16) in shared memory; colok: the column is a live
 // token column (others feed zeros).
+
+// Q4_K operand build: for a 32-bit word of packed nibbles, (w & 0x000F000F) holds two codes q in
+// separate 16-bit lanes; one integer multiply-add by the 6-bit scale sc and the magic 0x6400 gives,
+// in each lane, the fp16 bit pattern of 1024 + sc*q (sc*q <= 945 < 1024, so no carry between lanes
+// and the value is exact). High nibbles are used in place, (w & 0x00F000F0) = 16 q, and the magic
+// 0x7400 gives 16384 + 16*sc*q, exact because fp16 spacing at 2^14 is 16. The constant offsets
+// (1024 per weight, after dividing the high-nibble chain by 16) are removed with one extra MMA
+// that sums the activations of the super-block.
+__device__ __forceinline__ uint32_t imad_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
 __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol,
                                          const uint32_t* sxcol, bool colok, int sb, int t, float (&acc)[4]) {
@@ -64,23 +74,15 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
   const uint32_t sc478 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
   const uint32_t m478 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
 
-  float P4[4][4];  // one accumulator chain per 64-weight group (independent MMA chains)
+  float Plo[2][4] = {}, Phi[2][4] = {};  // two independent chains each for low / high nibbles
   const uint8_t* xb = xcol + 2 * (sb * 256 + 8 * t);
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    float (&P)[4] = P4[p];
-    P[0] = P[1] = P[2] = P[3] = 0.f;
     const uint32_t wg = (p < 2) ? sc03g : sc47g;
     const uint32_t w8 = (p < 2) ? sc038 : sc478;
-    const int il = (2 * p) & 3, ih = (2 * p + 1) & 3;
-    // (sc, sc) as fp16 pairs; low-nibble constants (sc, -1024 sc), high-nibble (sc/16, -64 sc)
-    const uint32_t slg = hsub2_u32(prmt(wg, 0x64u, byte_pair_sel(il)), H2_1024);
-    const uint32_t shg = hsub2_u32(prmt(wg, 0x64u, byte_pair_sel(ih)), H2_1024);
-    const uint32_t sl8 = hsub2_u32(prmt(w8, 0x64u, byte_pair_sel(il)), H2_1024);
-    const uint32_t sh8 = hsub2_u32(prmt(w8, 0x64u, byte_pair_sel(ih)), H2_1024);
-    const uint32_t alg = hmul2_u32(slg, H2_M1024), al8 = hmul2_u32(sl8, H2_M1024);
-    const uint32_t mhg = hmul2_u32(shg, H2_16TH), mh8 = hmul2_u32(sh8, H2_16TH);
-    const uint32_t ahg = hmul2_u32(shg, H2_M64), ah8 = hmul2_u32(sh8, H2_M64);
+    const int sl = 8 * ((2 * p) & 3), shh = 8 * ((2 * p + 1) & 3);
+    const uint32_t slg = (wg >> sl) & 0xFFu, shg = (wg >> shh) & 0xFFu;
+    const uint32_t sl8 = (w8 >> sl) & 0xFFu, sh8 = (w8 >> shh) & 0xFFu;
     const uint2 qg = *reinterpret_cast<const uint2*>(rg + 16 + 32 * p + 8 * t);
     const uint2 q8 = *reinterpret_cast<const uint2*>(rg8 + 16 + 32 * p + 8 * t);
     uint4 xl = make_uint4(0, 0, 0, 0), xh = make_uint4(0, 0, 0, 0);
@@ -93,23 +95,20 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
       const uint32_t w = j ? qg.y : qg.x, v = j ? q8.y : q8.x;
       const uint32_t ws = w >> 8, vs = v >> 8;
       uint32_t a[4];
-      a[0] = hfma2_u32(lop3_and_or(w, 0x000F000Fu, H2_1024), slg, alg);
-      a[1] = hfma2_u32(lop3_and_or(v, 0x000F000Fu, H2_1024), sl8, al8);
-      a[2] = hfma2_u32(lop3_and_or(ws, 0x000F000Fu, H2_1024), slg, alg);
-      a[3] = hfma2_u32(lop3_and_or(vs, 0x000F000Fu, H2_1024), sl8, al8);
-      mma_f16_16816(P, a, j ? xl.z : xl.x, j ? xl.w : xl.y);
-      a[0] = hfma2_u32(lop3_and_or(w, 0x00F000F0u, H2_1024), mhg, ahg);
-      a[1] = hfma2_u32(lop3_and_or(v, 0x00F000F0u, H2_1024), mh8, ah8);
-      a[2] = hfma2_u32(lop3_and_or(ws, 0x00F000F0u, H2_1024), mhg, ahg);
-      a[3] = hfma2_u32(lop3_and_or(vs, 0x00F000F0u, H2_1024), mh8, ah8);
-      mma_f16_16816(P, a, j ? xh.z : xh.x, j ? xh.w : xh.y);
+      a[0] = imad_u32(w & 0x000F000Fu, slg, 0x64006400u);
+      a[1] = imad_u32(v & 0x000F000Fu, sl8, 0x64006400u);
+      a[2] = imad_u32(ws & 0x000F000Fu, slg, 0x64006400u);
+      a[3] = imad_u32(vs & 0x000F000Fu, sl8, 0x64006400u);
+      mma_f16_16816(Plo[p & 1], a, j ? xl.z : xl.x, j ? xl.w : xl.y);
+      a[0] = imad_u32(w & 0x00F000F0u, shg, 0x74007400u);
+      a[1] = imad_u32(v & 0x00F000F0u, sh8, 0x74007400u);
+      a[2] = imad_u32(ws & 0x00F000F0u, shg, 0x74007400u);
+      a[3] = imad_u32(vs & 0x00F000F0u, sh8, 0x74007400u);
+      mma_f16_16816(Phi[p & 1], a, j ? xh.z : xh.x, j ? xh.w : xh.y);
     }
   }
-  float P[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) P[i] = __fadd_rn(__fadd_rn(P4[0][i], P4[1][i]), __fadd_rn(P4[2][i], P4[3][i]));
-  // min term: Cm[row, col] = sum_j m_j * (Sx_hi + Sx_lo)[col, j]
-  float Cm[4] = {0.f, 0.f, 0.f, 0.f};
+  // min term Cm[row, col] = sum_j m_j * S_j[col], and the super-block sum S[col] = sum_j S_j[col]
+  float Cm[4] = {0.f, 0.f, 0.f, 0.f}, Cs[4] = {0.f, 0.f, 0.f, 0.f};
   {
     const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
     const uint32_t mg = hsub2_u32(prmt((t < 2) ? m03g : m47g, 0x64u, sel), H2_1024);
@@ -121,11 +120,17 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
       b1 = sxcol[sb * 8 + 4 + t];
     }
     mma_f16_16816(Cm, a, b0, b1);
+    const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
+    mma_f16_16816(Cs, ones, b0, b1);
   }
-  acc[0] = fmaf(-dmg, Cm[0], fmaf(dg, P[0], acc[0]));
-  acc[1] = fmaf(-dmg, Cm[1], fmaf(dg, P[1], acc[1]));
-  acc[2] = fmaf(-dm8, Cm[2], fmaf(d8, P[2], acc[2]));
-  acc[3] = fmaf(-dm8, Cm[3], fmaf(d8, P[3], acc[3]));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __fadd_rn(Plo[0][i], Plo[1][i]);
+    const float hi = __fadd_rn(Phi[0][i], Phi[1][i]);
+    const float P = fmaf(-1024.f, Cs[i], fmaf(hi, 0.0625f, lo));  // sum_k x_k * sc * q
+    const float d = (i < 2) ? dg : d8, dm = (i < 2) ? dmg : dm8;
+    acc[i] = fmaf(-dm, Cm[i], fmaf(d, P, acc[i]));
+  }
 }
 
 __device__ __forceinline__ void unit_q6k(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol, bool colok,
@@ -463,16 +468,43 @@ __device__ __forceinline__ int worker_of_unit(int64_t u, int64_t U, int W) {
   return static_cast<int>(((u + 1) * W - 1) / U);
 }
 
-// A warp's chunk: up to `upc` consecutive units of one tile inside the warp's unit range.
-struct Chunk {
-  int tile, sb, n;
+// A warp walks its unit range with an incremental cursor (no divisions in the loop); a chunk is up
+// to `upc` consecutive units of one tile inside the range.
+struct Cursor {
+  int u, tile, sb, grp, lt;
 };
-__device__ __forceinline__ Chunk next_chunk(int64_t u, int64_t b, int nsb, int upc) {
-  Chunk c;
-  c.tile = static_cast<int>(u / nsb);
-  c.sb = static_cast<int>(u - static_cast<int64_t>(c.tile) * nsb);
-  c.n = static_cast<int>(min(static_cast<int64_t>(min(upc, nsb - c.sb)), b - u));
+struct Chunk {
+  int tile, sb, n, grp, lt;
+};
+__device__ __forceinline__ Cursor cursor_at(int u, int nsb, int tpg) {
+  Cursor c;
+  c.u = u;
+  c.tile = u / nsb;
+  c.sb = u - c.tile * nsb;
+  c.grp = c.tile / tpg;
+  c.lt = c.tile - c.grp * tpg;
   return c;
+}
+__device__ __forceinline__ Chunk chunk_at(const Cursor& c, int b, int nsb, int upc) {
+  Chunk ch;
+  ch.tile = c.tile;
+  ch.sb = c.sb;
+  ch.grp = c.grp;
+  ch.lt = c.lt;
+  ch.n = min(min(upc, nsb - c.sb), b - c.u);
+  return ch;
+}
+__device__ __forceinline__ void advance(Cursor& c, int n, int nsb, int tpg) {
+  c.u += n;
+  c.sb += n;
+  if (c.sb == nsb) {
+    c.sb = 0;
+    ++c.tile;
+    if (++c.lt == tpg) {
+      c.lt = 0;
+      ++c.grp;
+    }
+  }
 }
 
 template <int WT, int XT, int EPI>
@@ -483,7 +515,7 @@ __device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch
   if (p.use_tmap) {
     // one tiled request covers all 16 rows (two 8-row requests for gate/up), aligned down to 16 B
     if (lane == 0) {
-      const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
+      const int grp = ch.grp, lt = ch.lt;
       const int e = p.group_ids ? p.group_ids[grp] : grp;
       const int x = ((ch.sb * UB) & ~15) / p.tm_esz;
       mbar_arrive_expect_tx(bar, static_cast<uint32_t>(16 * p.tm_box * p.tm_esz));
@@ -496,7 +528,7 @@ __device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch
   uint32_t bytes = 0;
   const uint8_t* lo = nullptr;
   if (lane < 16) {
-    const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
+    const int grp = ch.grp, lt = ch.lt;
     const uint8_t* src = gemv_row_ptr<WT, XT, EPI>(p, grp, lt, lane) + static_cast<int64_t>(ch.sb) * UB;
     lo = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15));
     bytes = (static_cast<uint32_t>(src - lo) + ch.n * UB + 15u) & ~15u;
@@ -537,19 +569,20 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
 
   // weights are static: without a data-dependent group list, prefetch before waiting on the
   // previous kernel
-  int64_t U = 0, a = 0, b = 0, ui = 0;
+  int U = 0, a = 0, b = 0;  // unit counts fit in 32 bits (checked on the host)
+  Cursor ci;                // issue cursor
   int issued = 0, consumed = 0;
   auto setup_range = [&](int ngroups) {
-    U = static_cast<int64_t>(ngroups) * tpg * nsb;
-    a = U * wid / W;
-    b = U * (wid + 1) / W;
-    ui = a;
+    U = ngroups * tpg * nsb;
+    a = static_cast<int>(static_cast<int64_t>(U) * wid / W);
+    b = static_cast<int>(static_cast<int64_t>(U) * (wid + 1) / W);
+    ci = cursor_at(a, nsb, tpg);
   };
   auto prefetch = [&]() {
-    while (ui < b && issued - consumed < S) {
-      const Chunk ch = next_chunk(ui, b, nsb, p.upc);
+    while (ci.u < b && issued - consumed < S) {
+      const Chunk ch = chunk_at(ci, b, nsb, p.upc);
       issue_chunk<WT, XT, EPI>(p, ch, tpg, ring + (issued % S) * stride_slot, &bars[issued % S], lane);
-      ui += ch.n;
+      advance(ci, ch.n, nsb, tpg);
       ++issued;
     }
   };
@@ -563,8 +596,8 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     prefetch();
   }
   // stage the activations of every group this CTA touches (one group when x is shared)
-  const int64_t c0 = U * (static_cast<int64_t>(blockIdx.x) * NW) / W;
-  const int64_t c1 = U * (static_cast<int64_t>(blockIdx.x + 1) * NW) / W;
+  const int64_t c0 = static_cast<int64_t>(U) * (static_cast<int64_t>(blockIdx.x) * NW) / W;
+  const int64_t c1 = static_cast<int64_t>(U) * (static_cast<int64_t>(blockIdx.x + 1) * NW) / W;
   const int gfirst = (c1 > c0) ? static_cast<int>((c0 / nsb) / tpg) : 0;
   const int glast = (c1 > c0) ? static_cast<int>(((c1 - 1) / nsb) / tpg) : 0;
   if (p.x_group_stride == 0) {
@@ -579,12 +612,13 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
   const int* misc0 = reinterpret_cast<const int*>(smem + L.off_misc);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
-  for (int64_t uc = a; uc < b;) {
-    const Chunk ch = next_chunk(uc, b, nsb, p.upc);
-    const int slot = consumed % S;
-    ok = mbar_wait_bounded(&bars[slot], (consumed / S) & 1, p.status, ST_TIMEOUT_FULL);
+  Cursor cc = cursor_at(a, nsb, tpg);  // consume cursor
+  int slot = 0, phase = 0;
+  while (cc.u < b) {
+    const Chunk ch = chunk_at(cc, b, nsb, p.upc);
+    ok = mbar_wait_bounded(&bars[slot], phase, p.status, ST_TIMEOUT_FULL);
     if (!ok) break;
-    const int grp = ch.tile / tpg, lt = ch.tile - grp * tpg;
+    const int grp = ch.grp, lt = ch.lt;
     const int xsl = (p.x_group_stride == 0) ? 0 : grp - gfirst;
     const uint8_t* st = ring + slot * stride_slot;
     uint32_t hg, h8;
@@ -613,17 +647,21 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     }
     __syncwarp();
     ++consumed;
-    uc += ch.n;
+    if (++slot == S) {
+      slot = 0;
+      phase ^= 1;
+    }
+    advance(cc, ch.n, nsb, tpg);
     prefetch();  // refill the slot just freed
-    if (ch.sb + ch.n == nsb || uc == b) {
+    if (ch.sb + ch.n == nsb || cc.u == b) {
       // ---------------- this worker's piece of `tile` is done
-      const int64_t seg0 = max(a, static_cast<int64_t>(ch.tile) * nsb);
-      const bool whole = (seg0 == static_cast<int64_t>(ch.tile) * nsb) && (uc == static_cast<int64_t>(ch.tile + 1) * nsb);
+      const int seg0 = max(a, ch.tile * nsb);
+      const bool whole = (seg0 == ch.tile * nsb) && (cc.u == (ch.tile + 1) * nsb);
       const int* misc = misc0 + xsl * 8;
       if (whole) {
         gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, acc, lane);
       } else {
-        const int slot2 = (ch.tile == static_cast<int>(a / nsb)) ? 0 : 1;
+        const int slot2 = (ch.tile == a / nsb) ? 0 : 1;
         *reinterpret_cast<float4*>(p.partials + ((static_cast<int64_t>(wid) * 2 + slot2) * 32 + lane) * 4) =
             make_float4(acc[0], acc[1], acc[2], acc[3]);
         __threadfence();
@@ -635,13 +673,14 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
         const int wl = worker_of_unit(static_cast<int64_t>(ch.tile + 1) * nsb - 1, U, W);
         // workers with an empty range (more workers than units) hold no piece
         int npieces = 0;
-        for (int w2 = wf; w2 <= wl; ++w2) npieces += (U * w2 / W < U * (w2 + 1) / W) ? 1 : 0;
+        const int64_t U64 = U;
+        for (int w2 = wf; w2 <= wl; ++w2) npieces += (U64 * w2 / W < U64 * (w2 + 1) / W) ? 1 : 0;
         if (old == npieces - 1) {
           __threadfence();
           float v[4] = {0.f, 0.f, 0.f, 0.f};
           for (int w2 = wf; w2 <= wl; ++w2) {
-            if (U * w2 / W == U * (w2 + 1) / W) continue;
-            const int s2 = (ch.tile == static_cast<int>((U * w2 / W) / nsb)) ? 0 : 1;
+            if (U64 * w2 / W == U64 * (w2 + 1) / W) continue;
+            const int s2 = (ch.tile == static_cast<int>((U64 * w2 / W) / nsb)) ? 0 : 1;
             const float4 r = __ldcg(reinterpret_cast<const float4*>(
                 p.partials + ((static_cast<int64_t>(w2) * 2 + s2) * 32 + lane) * 4));
             v[0] = __fadd_rn(v[0], r.x);
@@ -689,6 +728,7 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   const int rpt = (epi == EPI_SWIGLU) ? 8 : 16;
   const int64_t upg = static_cast<int64_t>((p.N + rpt - 1) / rpt) * (p.K / 256);
   const int64_t U = static_cast<int64_t>(p.n_groups) * upg;
+  if (U > (1ll << 30)) return set_error(-1, "gemv: problem too large for one launch (units exceed 2^30)");
   // at least one unit per worker of a full CTA, so small problems do not spread into empty workers
   int grid = static_cast<int>(std::min<int64_t>(num_sms, (U + GEMV_MAXW - 1) / GEMV_MAXW));
   if (grid < 1) grid = 1;
