@@ -50,10 +50,9 @@ __device__ __forceinline__ uint32_t byte_pair_sel(int idx) {
 // Q4_K operand build: for a 32-bit word of packed nibbles, (w & 0x000F000F) holds two codes q in
 // separate 16-bit lanes; one integer multiply-add by the 6-bit scale sc and the magic 0x6400 gives,
 // in each lane, the fp16 bit pattern of 1024 + sc*q (sc*q <= 945 < 1024, so no carry between lanes
-// and the value is exact). High nibbles are used in place, (w & 0x00F000F0) = 16 q, and the magic
-// 0x7400 gives 16384 + 16*sc*q, exact because fp16 spacing at 2^14 is 16. The constant offsets
-// (1024 per weight, after dividing the high-nibble chain by 16) are removed with one extra MMA
-// that sums the activations of the super-block.
+// and the value is exact: the sum lands in the 10-bit mantissa field of 1024.0). High nibbles are
+// shifted down first and built the same way. The constant offset (1024 per weight) is removed with
+// one extra MMA that sums the activations of the super-block.
 __device__ __forceinline__ uint32_t imad_u32(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
   asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -100,10 +99,10 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
       a[2] = imad_u32(ws & 0x000F000Fu, slg, 0x64006400u);
       a[3] = imad_u32(vs & 0x000F000Fu, sl8, 0x64006400u);
       mma_f16_16816(Plo[p & 1], a, j ? xl.z : xl.x, j ? xl.w : xl.y);
-      a[0] = imad_u32(w & 0x00F000F0u, shg, 0x74007400u);
-      a[1] = imad_u32(v & 0x00F000F0u, sh8, 0x74007400u);
-      a[2] = imad_u32(ws & 0x00F000F0u, shg, 0x74007400u);
-      a[3] = imad_u32(vs & 0x00F000F0u, sh8, 0x74007400u);
+      a[0] = imad_u32((w >> 4) & 0x000F000Fu, shg, 0x64006400u);
+      a[1] = imad_u32((v >> 4) & 0x000F000Fu, sh8, 0x64006400u);
+      a[2] = imad_u32((w >> 12) & 0x000F000Fu, shg, 0x64006400u);
+      a[3] = imad_u32((v >> 12) & 0x000F000Fu, sh8, 0x64006400u);
       mma_f16_16816(Phi[p & 1], a, j ? xh.z : xh.x, j ? xh.w : xh.y);
     }
   }
@@ -127,7 +126,7 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
   for (int i = 0; i < 4; ++i) {
     const float lo = __fadd_rn(Plo[0][i], Plo[1][i]);
     const float hi = __fadd_rn(Phi[0][i], Phi[1][i]);
-    const float P = fmaf(-1024.f, Cs[i], fmaf(hi, 0.0625f, lo));  // sum_k x_k * sc * q
+    const float P = fmaf(-1024.f, Cs[i], __fadd_rn(lo, hi));  // sum_k x_k * sc * q
     const float d = (i < 2) ? dg : d8, dm = (i < 2) ? dmg : dm8;
     acc[i] = fmaf(-dm, Cm[i], fmaf(d, P, acc[i]));
   }
