@@ -217,27 +217,46 @@ def combine(sel_w: np.ndarray, y_slots: np.ndarray, y_shared) -> np.ndarray:
     return qo.bf16_round(facc)
 
 
-def moe_layer(x_bf, wr_t, experts_deq, shared_deq, topk: int, bias=None, scale=RSCALE_DEFAULT):
+def swiglu_magnitude(h_bf, wd) -> np.ndarray:
+    """sum_k |h_k| * |w_d[n, k]| per output: the scale the reference's own SwiGLU tolerance uses
+    (tools/swiglu_q4k_gen.py:91-95)."""
+    return np.abs(np.asarray(h_bf, np.float64)) @ np.abs(np.asarray(wd, np.float64)).T
+
+
+def moe_layer(x_bf, wr_t, experts_deq, shared_deq, topk: int, bias=None, scale=RSCALE_DEFAULT, want_mag=False):
     """The MoE branch of decoder_block (glm_model_q4k_ref.py:797-809) on M token rows.
 
     experts_deq: callable e -> (wg [F,H], wu [F,H], wd [H,F]) fp32 dequantised weights
     (called once per expert in the union of selections); shared_deq: same tuple or None.
-    Returns (out bf16-valued fp32 [M, H], sel, sel_w).
+    Returns (out bf16-valued fp32 [M, H], sel, sel_w), plus the per-output magnitude
+    sum_slots |w| * sum_k |h||w_d| (+ shared) when want_mag.
     """
     x = np.asarray(x_bf, F32)
     sel, sel_w, _ = moe_router(x, wr_t, topk, bias, scale)
     M = x.shape[0]
     union = sorted(set(int(e) for e in sel.reshape(-1)))
-    y_by_e = {}
+    y_by_e, mag_by_e = {}, {}
     for e in union:
         wg, wu, wd = experts_deq(e)
-        y_by_e[e] = swiglu_expert(x, wg, wu, wd)          # rows are independent
+        h = swiglu_hidden(x, wg, wu)
+        y_by_e[e] = qo.matmul_seq(h, wd)                  # rows are independent
+        if want_mag:
+            mag_by_e[e] = swiglu_magnitude(h, wd)
     H = next(iter(y_by_e.values())).shape[1]
     y_slots = np.empty((M, topk, H), F32)
+    mag = np.zeros((M, H), np.float64)
     for m in range(M):
         for s in range(topk):
-            y_slots[m, s] = y_by_e[int(sel[m, s])][m]
+            e = int(sel[m, s])
+            y_slots[m, s] = y_by_e[e][m]
+            if want_mag:
+                mag[m] += abs(float(sel_w[m, s])) * mag_by_e[e][m]
     y_sh = None
     if shared_deq is not None:
-        y_sh = swiglu_expert(x, *shared_deq)
-    return combine(sel_w, y_slots, y_sh), sel, sel_w
+        wg, wu, wd = shared_deq
+        h = swiglu_hidden(x, wg, wu)
+        y_sh = qo.matmul_seq(h, wd)
+        if want_mag:
+            mag += swiglu_magnitude(h, wd)
+    out = combine(sel_w, y_slots, y_sh)
+    return (out, sel, sel_w, mag) if want_mag else (out, sel, sel_w)
