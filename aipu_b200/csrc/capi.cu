@@ -94,7 +94,44 @@ struct aipu_ctx {
   void* moe = nullptr;
   size_t moe_bytes = 0;
   int flags = 0;  // AIPU_FLAG_*
+  // prefill scratch (grown on demand)
+  void* pre = nullptr;
+  size_t pre_bytes = 0;
 };
+
+static int grow(void** buf, size_t* have, size_t need, const char* what) {
+  if (need <= *have) return OK;
+  cudaFree(*buf);
+  *buf = nullptr;
+  *have = 0;
+  if (cudaMalloc(buf, need) != cudaSuccess) return set_error(ENOMEM_, what);
+  *have = need;
+  return OK;
+}
+
+// prescaled activations for the tensor-core GEMM, carved from one buffer
+struct PreX {
+  __half* xh;
+  int* shift;
+  __half* sx;
+  float* sxsb;
+};
+static size_t al256x(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+static size_t prex_bytes(int64_t R, int64_t K) {
+  return al256x(2 * R * K) + al256x(4 * R) + al256x(2 * R * (K / 256) * 16) + al256x(4 * R * (K / 256));
+}
+static PreX prex_carve(void* base, int64_t R, int64_t K) {
+  uint8_t* b = static_cast<uint8_t*>(base);
+  PreX px;
+  px.xh = reinterpret_cast<__half*>(b);
+  b += al256x(2 * R * K);
+  px.shift = reinterpret_cast<int*>(b);
+  b += al256x(4 * R);
+  px.sx = reinterpret_cast<__half*>(b);
+  b += al256x(2 * R * (K / 256) * 16);
+  px.sxsb = reinterpret_cast<float*>(b);
+  return px;
+}
 
 static const int kMaxTiles = 1 << 16;
 
@@ -171,6 +208,7 @@ int aipu_ctx_destroy(aipu_ctx* c) {
   cudaFree(c->status);
   cudaFree(c->router_counters);
   cudaFree(c->moe);
+  cudaFree(c->pre);
   if (c->side) cudaStreamDestroy(c->side);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
@@ -347,6 +385,7 @@ static int moe_scratch(aipu_ctx* c, int64_t M, int64_t E, int T, int64_t H, int6
   for (size_t v : sz) total += v;
   if (total > c->moe_bytes) {
     cudaFree(c->moe);
+  cudaFree(c->pre);
     c->moe = nullptr;
     c->moe_bytes = 0;
     if (cudaMalloc(&c->moe, total) != cudaSuccess) return set_error(ENOMEM_, "moe: scratch allocation");
@@ -502,4 +541,34 @@ extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt,
                          static_cast<uint16_t*>(y), s, false);
   if (tmp) cudaFreeAsync(tmp, s);
   return rc;
+}
+
+extern "C" int aipu_q4k_gemm_tc(aipu_ctx* c, int wtype, const void* w, int64_t N, int64_t K, const void* x, int64_t M,
+                                void* y, void* stream) {
+  if (!c || !w || !x || !y || N <= 0 || M <= 0 || K <= 0 || K % 256 || (wtype != AIPU_Q4_K && wtype != AIPU_Q6_K) ||
+      N > INT32_MAX || M > (1 << 24) || (reinterpret_cast<uintptr_t>(x) & 15u))
+    return set_error(EINVAL_, "gemm_tc: bad arguments (Q4_K/Q6_K, K % 256 == 0, 16-byte aligned bf16 x)");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = grow(&c->pre, &c->pre_bytes, prex_bytes(M, K), "gemm_tc: scratch");
+  if (rc) return rc;
+  const PreX px = prex_carve(c->pre, M, K);
+  rc = prescale_launch(static_cast<const uint16_t*>(x), static_cast<int>(M), static_cast<int>(K), nullptr, nullptr,
+                       px.xh, px.shift, px.sx, px.sxsb, s, false);
+  if (rc) return rc;
+  TcParams p = {};
+  p.wt = wtype;
+  p.w0 = static_cast<const uint8_t*>(w);
+  p.row_bytes = row_bytes_of(wtype, K);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.M = static_cast<int>(M);
+  p.xh = px.xh;
+  p.xshift = px.shift;
+  p.sx = px.sx;
+  p.sxsb = px.sxsb;
+  p.y = static_cast<uint16_t*>(y);
+  p.status = c->status;
+  const int nt = 64;
+  return tc_gemm_launch(p, nt, static_cast<int>((M + nt - 1) / nt), s, true);
 }

@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace aipu {
@@ -35,6 +36,30 @@ struct CombineParams {
   const uint16_t* y_shared; // bf16 [M, H] (nullable)
   uint16_t* out;            // bf16 [M, H]
 };
+
+// prefill GEMM on tcgen05 (tc_gemm.cu)
+struct TcParams {
+  int wt;                  // WT_Q4K or WT_Q6K
+  int swiglu;              // 1: A rows 0..63 gate rows, 64..127 up rows; y = h = bf16(silu(g) * u)
+  const uint8_t* w0;       // weights (gate rows for swiglu), expert e at w0 + e * expert_stride
+  const uint8_t* w1;       // up rows (swiglu)
+  int64_t row_bytes;
+  int64_t expert_stride;
+  int N, K, M;             // output rows per matrix, reduction length, tokens (dense mode)
+  const __half* xh;        // prescaled fp16 activations [rows, K]
+  const int* xshift;       // [rows] power-of-two prescale
+  const __half* sx;        // [rows, K/256, 16] sub-block sums (Q4_K)
+  const float* sxsb;       // [rows, K/256] super-block sums (Q4_K)
+  const int* x_rows;       // position -> activation row (nullable: identity)
+  const int4* tiles;       // per tile (group, first position, tokens, 0) (nullable: dense tiles over M)
+  const int* tile_count;   // device number of tiles (nullable)
+  const int* group_ids;    // group -> expert (nullable: identity)
+  uint16_t* y;             // bf16 [positions, N]
+  int* status;
+};
+int tc_gemm_launch(const TcParams& p, int nt, int max_tiles, cudaStream_t s, bool pdl);
+int prescale_launch(const uint16_t* x, int R, int K, const int* rows, const int* n_rows_dev, __half* xh, int* shift,
+                    __half* sx, float* sxsb, cudaStream_t s, bool pdl);
 
 int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, int out_bf16, cudaStream_t s);
 int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,

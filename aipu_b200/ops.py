@@ -121,6 +121,20 @@ def gemm(wtype: int, w: torch.Tensor, N: int, K: int, x: torch.Tensor, mode: str
     return out
 
 
+def gemm_tc(wtype: int, w: torch.Tensor, N: int, K: int, x: torch.Tensor, ctx: Optional[Context] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Prefill GEMM on tcgen05: y[M, N] bf16 = x[M, K] (bf16) x W^T, Q4_K or Q6_K rows."""
+    _need_cuda(w, x, out)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != K:
+        raise ValueError("x must be bf16 [M, K]")
+    ctx = ctx or Context.default(w.device)
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=w.device)
+    check(lib().aipu_q4k_gemm_tc(ctx.handle, wtype, _ptr(w), N, K, _ptr(x), M, _ptr(out), _stream(w.device)))
+    return out
+
+
 def gemm_grouped(wtype: int, w: torch.Tensor, n_mats: int, N: int, K: int, x: torch.Tensor,
                  mat_stride: Optional[int] = None, ctx: Optional[Context] = None,
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:

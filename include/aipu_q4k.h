@@ -106,6 +106,17 @@ int aipu_q4k_gemm(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K,
 int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype, int64_t M,
                           void* y, void* stream);
 
+/* Prefill GEMM on the 5th-generation tensor cores (tcgen05 MMA, fp32 accumulators in TMEM):
+ * y[M, N] (bf16) = x[M, K] (bf16, 16-byte aligned) x W[N rows, K]^T for Q4_K or Q6_K weights and many
+ * token rows. Weights are dequantised in shared memory to exact fp16 operands (Q4_K: 1024 + sc*q;
+ * Q6_K: two exact halves of sc*q), tokens are prescaled to fp16 by a power of two; fp32
+ * accumulation per super-block, scales applied in the epilogue. Within 1 bf16 ulp of the sequential
+ * reference (same bar as AIPU_MODE_FAST). The context grows a scratch buffer for the prescaled rows.
+ * Replaces: tools/q4k_ref.py:86-92 matmul_q4k_col over many activation rows (the prefill use of
+ *           src/glm_matmul_q4k.v). */
+int aipu_q4k_gemm_tc(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K, const void* x, int64_t M, void* y,
+                     void* stream);
+
 /* Grouped fast GEMM: n_mats independent matrices of N rows x K (matrix g at w + g * mat_stride
  * bytes) applied to the same activations x[M, K] in ONE launch; y[g, M, N] (bf16). This is the
  * decode pattern of several projections or experts fed by the same token rows (e.g. all experts of
