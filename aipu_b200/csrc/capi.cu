@@ -456,9 +456,157 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
   return OK;
 }
 
+// ------------------------------------------------------------------ MoE prefill (many tokens)
+// router -> per-expert token lists -> SwiGLU gate/up and down on the tensor cores, grouped by
+// expert -> shared expert (dense) -> slot-order combine. The weights of each expert are dequantised
+// once per (128-row tile, token tile) for all the expert's tokens.
+static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y, int32_t* sel_out,
+                       void* sel_w_out, cudaStream_t s) {
+  const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
+  const int T = W->topk;
+  const int64_t P = M * T;
+  const int nt = 64;
+  const int64_t max_tiles = (P + nt - 1) / nt + E;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
+  size_t sz[12] = {al256x(2 * M * E), al256x(4 * P), al256x(2 * P), al256x(4 * P), al256x(4 * P),
+                   al256x(16 * max_tiles), al256x(4), prex_bytes(M, H), al256x(2 * P * F), prex_bytes(P, F),
+                   al256x(2 * P * H), shared ? al256x(2 * M * F) + prex_bytes(M, F) + al256x(2 * M * H) : 0};
+  size_t total = 0;
+  for (size_t v : sz) total += v;
+  int rc = grow(&c->pre, &c->pre_bytes, total, "moe_prefill: scratch");
+  if (rc) return rc;
+  uint8_t* b = static_cast<uint8_t*>(c->pre);
+  void* ptr[12];
+  for (int i = 0; i < 12; ++i) {
+    ptr[i] = b;
+    b += sz[i];
+  }
+  uint16_t* gate = static_cast<uint16_t*>(ptr[0]);
+  int32_t* sel = static_cast<int32_t*>(ptr[1]);
+  uint16_t* sel_w = static_cast<uint16_t*>(ptr[2]);
+  int32_t* pos_of = static_cast<int32_t*>(ptr[3]);
+  int32_t* perm_tok = static_cast<int32_t*>(ptr[4]);
+  int4* tiles = static_cast<int4*>(ptr[5]);
+  int32_t* n_tiles = static_cast<int32_t*>(ptr[6]);
+  const PreX px = prex_carve(ptr[7], M, H);
+  uint16_t* h_perm = static_cast<uint16_t*>(ptr[8]);
+  const PreX ph = prex_carve(ptr[9], P, F);
+  uint16_t* y_perm = static_cast<uint16_t*>(ptr[10]);
+  uint16_t* h_sh = shared ? static_cast<uint16_t*>(ptr[11]) : nullptr;
+  const PreX phs = shared ? prex_carve(static_cast<uint8_t*>(ptr[11]) + al256x(2 * M * F), M, F) : PreX{};
+  uint16_t* y_sh = shared ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(ptr[11]) + al256x(2 * M * F) +
+                                                        prex_bytes(M, F))
+                          : nullptr;
+
+  RouterParams rp = {};
+  rp.wt = W->router_wtype;
+  rp.w = static_cast<const uint8_t*>(W->router_w);
+  rp.bias = W->router_bias;
+  rp.x = static_cast<const uint16_t*>(x);
+  rp.M = static_cast<int>(M);
+  rp.K = static_cast<int>(H);
+  rp.E = static_cast<int>(E);
+  rp.topk = T;
+  rp.scale = W->scale;
+  rp.gate = gate;
+  rp.sel = sel;
+  rp.sel_w = sel_w;
+  rp.counters = c->router_counters;
+  rp.status = c->status;
+  if ((rc = router_launch(rp, s, false))) return rc;
+  PermParams pp = {sel, static_cast<int>(M), T, static_cast<int>(E), nt, perm_tok, pos_of, tiles, n_tiles};
+  if ((rc = perm_launch(pp, s))) return rc;
+  if ((rc = prescale_launch(static_cast<const uint16_t*>(x), static_cast<int>(M), static_cast<int>(H), nullptr,
+                            nullptr, px.xh, px.shift, px.sx, px.sxsb, s, true)))
+    return rc;
+  TcParams g = {};
+  g.wt = W->gate_wtype;
+  g.swiglu = 1;
+  g.w0 = static_cast<const uint8_t*>(W->gate_w);
+  g.w1 = static_cast<const uint8_t*>(W->up_w);
+  g.row_bytes = row_bytes_of(W->gate_wtype, H);
+  g.expert_stride = F * g.row_bytes;
+  g.N = static_cast<int>(F);
+  g.K = static_cast<int>(H);
+  g.M = static_cast<int>(M);
+  g.xh = px.xh;
+  g.xshift = px.shift;
+  g.sx = px.sx;
+  g.sxsb = px.sxsb;
+  g.x_rows = perm_tok;
+  g.tiles = tiles;
+  g.tile_count = n_tiles;
+  g.y = h_perm;
+  g.status = c->status;
+  if ((rc = tc_gemm_launch(g, nt, static_cast<int>(max_tiles), s, true))) return rc;
+  if ((rc = prescale_launch(h_perm, static_cast<int>(P), static_cast<int>(F), nullptr, nullptr, ph.xh, ph.shift, ph.sx,
+                            ph.sxsb, s, true)))
+    return rc;
+  TcParams dn = g;
+  dn.wt = W->down_wtype;
+  dn.swiglu = 0;
+  dn.w0 = static_cast<const uint8_t*>(W->down_w);
+  dn.w1 = nullptr;
+  dn.row_bytes = row_bytes_of(W->down_wtype, F);
+  dn.expert_stride = H * dn.row_bytes;
+  dn.N = static_cast<int>(H);
+  dn.K = static_cast<int>(F);
+  dn.xh = ph.xh;
+  dn.xshift = ph.shift;
+  dn.sx = ph.sx;
+  dn.sxsb = ph.sxsb;
+  dn.x_rows = nullptr;
+  dn.y = y_perm;
+  if ((rc = tc_gemm_launch(dn, nt, static_cast<int>(max_tiles), s, true))) return rc;
+  if (shared) {
+    TcParams sg = g;
+    sg.w0 = static_cast<const uint8_t*>(W->shared_gate_w);
+    sg.w1 = static_cast<const uint8_t*>(W->shared_up_w);
+    sg.expert_stride = 0;
+    sg.x_rows = nullptr;
+    sg.tiles = nullptr;
+    sg.tile_count = nullptr;
+    sg.y = h_sh;
+    if ((rc = tc_gemm_launch(sg, nt, static_cast<int>((M + nt - 1) / nt), s, true))) return rc;
+    if ((rc = prescale_launch(h_sh, static_cast<int>(M), static_cast<int>(F), nullptr, nullptr, phs.xh, phs.shift,
+                              phs.sx, phs.sxsb, s, true)))
+      return rc;
+    TcParams sd = dn;
+    sd.w0 = static_cast<const uint8_t*>(W->shared_down_w);
+    sd.expert_stride = 0;
+    sd.xh = phs.xh;
+    sd.xshift = phs.shift;
+    sd.sx = phs.sx;
+    sd.sxsb = phs.sxsb;
+    sd.tiles = nullptr;
+    sd.tile_count = nullptr;
+    sd.y = y_sh;
+    if ((rc = tc_gemm_launch(sd, nt, static_cast<int>((M + nt - 1) / nt), s, true))) return rc;
+  }
+  CombineParams cp = {};
+  cp.M = static_cast<int>(M);
+  cp.H = static_cast<int>(H);
+  cp.topk = T;
+  cp.slot_map = pos_of;
+  cp.sel_w = sel_w;
+  cp.y_union = y_perm;
+  cp.y_shared = y_sh;
+  cp.out = static_cast<uint16_t*>(y);
+  cp.rows_are_positions = 1;
+  if ((rc = combine_launch(cp, s, true))) return rc;
+  if (sel_out && (rc = set_cuda_error(cudaMemcpyAsync(sel_out, sel, 4 * P, cudaMemcpyDeviceToDevice, s), "copy sel")))
+    return rc;
+  if (sel_w_out &&
+      (rc = set_cuda_error(cudaMemcpyAsync(sel_w_out, sel_w, 2 * P, cudaMemcpyDeviceToDevice, s), "copy sel_w")))
+    return rc;
+  return OK;
+}
+
+static const int64_t kPrefillMinTokens = 64;
+
 extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y,
                               int32_t* sel_out, void* sel_w_out, void* stream) {
-  if (!c || !W || !x || !y || M <= 0 || M > 1024) return set_error(EINVAL_, "moe_layer: bad arguments");
+  if (!c || !W || !x || !y || M <= 0 || M > 8192) return set_error(EINVAL_, "moe_layer: bad arguments");
   const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
   const int T = W->topk;
   if (H % 256 || F % 256 || E <= 0 || E > 1024 || T <= 0 || T > 16 || T > E || !W->gate_w || !W->up_w ||
@@ -467,6 +615,11 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
     return set_error(EINVAL_, "moe_layer: bad weights descriptor");
   DeviceGuard dg(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // many tokens: the tensor-core path (SwiGLU gate/up in Q4_K, down in Q4_K or Q6_K)
+  if (M >= kPrefillMinTokens && W->gate_wtype == AIPU_Q4_K &&
+      (W->down_wtype == AIPU_Q4_K || W->down_wtype == AIPU_Q6_K) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0)
+    return moe_prefill(c, W, x, M, y, sel_out, sel_w_out, s);
+  if (M > 1024) return set_error(EINVAL_, "moe_layer: more than 1024 tokens need Q4_K gate/up and Q4_K/Q6_K down");
   MoeScratch sc = {};
   int rc = moe_scratch(c, M, E, T, H, F, sc);
   if (rc) return rc;

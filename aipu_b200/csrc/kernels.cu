@@ -341,7 +341,8 @@ __global__ void combine_kernel(const CombineParams p) {
     for (int s = 0; s < p.topk; ++s) {
       const int u = p.slot_map[m * p.topk + s];
       const float wv = bf16_bits_to_f32(p.sel_w[m * p.topk + s]);
-      const float yv = bf16_bits_to_f32(p.y_union[(static_cast<int64_t>(u) * p.M + m) * p.H + d]);
+      const int64_t row = p.rows_are_positions ? static_cast<int64_t>(u) : static_cast<int64_t>(u) * p.M + m;
+      const float yv = bf16_bits_to_f32(p.y_union[row * p.H + d]);
       facc = __fadd_rn(facc, __fmul_rn(wv, yv));
     }
     if (p.y_shared) facc = __fadd_rn(facc, bf16_bits_to_f32(p.y_shared[i]));
@@ -356,6 +357,57 @@ int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl) {
   if (blocks > 4096) blocks = 4096;
   CombineParams q = p;
   return launch_kernel(reinterpret_cast<const void*>(combine_kernel), dim3(blocks), dim3(256), 0, s, pdl, &q);
+}
+
+// ------------------------------------------------------------------ prefill permutation
+// One CTA of 1024 threads. Experts are assigned to warps; for each expert a warp walks the tokens in
+// order, 32 at a time, and places every token that selected it with a ballot prefix, so the token
+// order inside an expert's list is ascending and the result is deterministic. A position is never
+// shared: a token selects an expert at most once.
+__global__ void __launch_bounds__(1024) perm_kernel(const PermParams p) {
+  pdl_wait();
+  __shared__ int cnt[1024];
+  __shared__ int off[1025];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e < p.E; e += 1024) cnt[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < p.T * p.topk; i += 1024) atomicAdd(&cnt[p.sel[i]], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0, nt = 0;
+    for (int e = 0; e < p.E; ++e) {
+      off[e] = acc;
+      for (int t0 = 0; t0 < cnt[e]; t0 += p.nt) p.tiles[nt++] = make_int4(e, acc + t0, min(p.nt, cnt[e] - t0), 0);
+      acc += cnt[e];
+    }
+    off[p.E] = acc;
+    *p.n_tiles = nt;
+  }
+  __syncthreads();
+  for (int e = warp; e < p.E; e += 32) {
+    int base = off[e];
+    for (int t0 = 0; t0 < p.T; t0 += 32) {
+      const int t = t0 + lane;
+      int slot = -1;
+      if (t < p.T)
+        for (int s = 0; s < p.topk; ++s)
+          if (p.sel[t * p.topk + s] == e) slot = s;
+      const unsigned m = __ballot_sync(0xffffffffu, slot >= 0);
+      if (slot >= 0) {
+        const int pos = base + __popc(m & ((1u << lane) - 1u));
+        p.perm_tok[pos] = t;
+        p.pos_of[t * p.topk + slot] = pos;
+      }
+      base += __popc(m);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+int perm_launch(const PermParams& p, cudaStream_t s) {
+  if (p.E > 1024 || p.E <= 0) return set_error(EINVAL_, "perm: E must be 1..1024");
+  PermParams q = p;
+  return launch_kernel(reinterpret_cast<const void*>(perm_kernel), dim3(1), dim3(1024), 0, s, true, &q);
 }
 
 // ------------------------------------------------------------------ activations

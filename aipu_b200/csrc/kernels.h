@@ -32,10 +32,23 @@ struct CombineParams {
   int M, H, topk;
   const int32_t* slot_map;  // [M, topk]
   const uint16_t* sel_w;    // bf16 [M, topk]
-  const uint16_t* y_union;  // bf16 [U, M, H]
+  const uint16_t* y_union;  // bf16 [U, M, H] (decode) or [positions, H] (rows_are_positions)
   const uint16_t* y_shared; // bf16 [M, H] (nullable)
   uint16_t* out;            // bf16 [M, H]
+  int rows_are_positions;   // 1: slot_map holds the row of y_union directly
 };
+
+// prefill token permutation (kernels.cu): per-expert token lists in token order, the position of
+// every (token, slot), and the tile list of the grouped tensor-core GEMM
+struct PermParams {
+  const int32_t* sel;      // [T, topk]
+  int T, topk, E, nt;      // tokens, slots, experts, tokens per tile
+  int32_t* perm_tok;       // [T*topk] token of each position
+  int32_t* pos_of;         // [T, topk] position of each (token, slot)
+  int4* tiles;             // (expert, first position, tokens, 0)
+  int32_t* n_tiles;        // [1]
+};
+int perm_launch(const PermParams& p, cudaStream_t s);
 
 // prefill GEMM on tcgen05 (tc_gemm.cu)
 struct TcParams {
