@@ -109,29 +109,7 @@ static int grow(void** buf, size_t* have, size_t need, const char* what) {
   return OK;
 }
 
-// prescaled activations for the tensor-core GEMM, carved from one buffer
-struct PreX {
-  __half* xh;
-  int* shift;
-  __half* sx;
-  float* sxsb;
-};
 static size_t al256x(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
-static size_t prex_bytes(int64_t R, int64_t K) {
-  return al256x(2 * R * K) + al256x(4 * R) + al256x(2 * R * (K / 256) * 16) + al256x(4 * R * (K / 256));
-}
-static PreX prex_carve(void* base, int64_t R, int64_t K) {
-  uint8_t* b = static_cast<uint8_t*>(base);
-  PreX px;
-  px.xh = reinterpret_cast<__half*>(b);
-  b += al256x(2 * R * K);
-  px.shift = reinterpret_cast<int*>(b);
-  b += al256x(4 * R);
-  px.sx = reinterpret_cast<__half*>(b);
-  b += al256x(2 * R * (K / 256) * 16);
-  px.sxsb = reinterpret_cast<float*>(b);
-  return px;
-}
 
 static const int kMaxTiles = 1 << 16;
 
@@ -460,43 +438,47 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
 // router -> per-expert token lists -> SwiGLU gate/up and down on the tensor cores, grouped by
 // expert -> shared expert (dense) -> slot-order combine. The weights of each expert are dequantised
 // once per (128-row tile, token tile) for all the expert's tokens.
+// Many-token MoE layer: router -> per-segment token lists (the shared expert is segment E) ->
+// tiled prescale of the permuted tokens -> SwiGLU gate/up on tcgen05 -> tiled prescale of h ->
+// down projection on tcgen05 -> slot-order combine (reference: glm_model_q4k_ref.py:663-809).
 static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y, int32_t* sel_out,
                        void* sel_w_out, cudaStream_t s) {
   const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
   const int T = W->topk;
   const int64_t P = M * T;
-  const int nt = 64;
-  const int64_t max_tiles = (P + nt - 1) / nt + E;
+  const int nt = 64;  // tokens per tile: about the tokens an expert gets at top-8 of 256
   const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
-  size_t sz[12] = {al256x(2 * M * E), al256x(4 * P), al256x(2 * P), al256x(4 * P), al256x(4 * P),
-                   al256x(16 * max_tiles), al256x(4), prex_bytes(M, H), al256x(2 * P * F), prex_bytes(P, F),
-                   al256x(2 * P * H), shared ? al256x(2 * M * F) + prex_bytes(M, F) + al256x(2 * M * H) : 0};
+  const int64_t Pmax = perm_max_positions(M, T, static_cast<int>(E), shared);
+  const int64_t max_tiles = perm_max_tiles(M, T, static_cast<int>(E), shared, nt);
+  size_t sz[13] = {al256x(2 * M * E), al256x(4 * P),  al256x(2 * P),        al256x(4 * P),   al256x(4 * M),
+                   al256x(4 * Pmax),  al256x(16 * max_tiles), al256x(16),  al256x(xt_bytes(Pmax, H)),
+                   al256x(4 * Pmax),  al256x(2 * Pmax * F), al256x(xt_bytes(Pmax, F)), al256x(2 * Pmax * H)};
   size_t total = 0;
   for (size_t v : sz) total += v;
+  total += al256x(4 * Pmax);  // shift of h
   int rc = grow(&c->pre, &c->pre_bytes, total, "moe_prefill: scratch");
   if (rc) return rc;
   uint8_t* b = static_cast<uint8_t*>(c->pre);
-  void* ptr[12];
-  for (int i = 0; i < 12; ++i) {
+  void* ptr[14];
+  for (int i = 0; i < 13; ++i) {
     ptr[i] = b;
     b += sz[i];
   }
+  ptr[13] = b;
   uint16_t* gate = static_cast<uint16_t*>(ptr[0]);
   int32_t* sel = static_cast<int32_t*>(ptr[1]);
   uint16_t* sel_w = static_cast<uint16_t*>(ptr[2]);
   int32_t* pos_of = static_cast<int32_t*>(ptr[3]);
-  int32_t* perm_tok = static_cast<int32_t*>(ptr[4]);
-  int4* tiles = static_cast<int4*>(ptr[5]);
-  int32_t* n_tiles = static_cast<int32_t*>(ptr[6]);
-  const PreX px = prex_carve(ptr[7], M, H);
-  uint16_t* h_perm = static_cast<uint16_t*>(ptr[8]);
-  const PreX ph = prex_carve(ptr[9], P, F);
-  uint16_t* y_perm = static_cast<uint16_t*>(ptr[10]);
-  uint16_t* h_sh = shared ? static_cast<uint16_t*>(ptr[11]) : nullptr;
-  const PreX phs = shared ? prex_carve(static_cast<uint8_t*>(ptr[11]) + al256x(2 * M * F), M, F) : PreX{};
-  uint16_t* y_sh = shared ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(ptr[11]) + al256x(2 * M * F) +
-                                                        prex_bytes(M, F))
-                          : nullptr;
+  int32_t* shared_pos = static_cast<int32_t*>(ptr[4]);
+  int32_t* perm_tok = static_cast<int32_t*>(ptr[5]);
+  int4* tiles = static_cast<int4*>(ptr[6]);
+  int32_t* counts = static_cast<int32_t*>(ptr[7]);  // [0] tiles, [1] positions
+  uint8_t* xt = static_cast<uint8_t*>(ptr[8]);
+  int* xshift = static_cast<int*>(ptr[9]);
+  uint16_t* h_perm = static_cast<uint16_t*>(ptr[10]);
+  uint8_t* ht = static_cast<uint8_t*>(ptr[11]);
+  uint16_t* y_perm = static_cast<uint16_t*>(ptr[12]);
+  int* hshift = static_cast<int*>(ptr[13]);
 
   RouterParams rp = {};
   rp.wt = W->router_wtype;
@@ -514,75 +496,64 @@ static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, in
   rp.counters = c->router_counters;
   rp.status = c->status;
   if ((rc = router_launch(rp, s, false))) return rc;
-  PermParams pp = {sel, static_cast<int>(M), T, static_cast<int>(E), nt, perm_tok, pos_of, tiles, n_tiles};
+  PermParams pp = {};
+  pp.sel = sel;
+  pp.T = static_cast<int>(M);
+  pp.topk = T;
+  pp.E = static_cast<int>(E);
+  pp.nt = nt;
+  pp.with_shared = shared ? 1 : 0;
+  pp.perm_tok = perm_tok;
+  pp.pos_of = pos_of;
+  pp.shared_pos = shared_pos;
+  pp.tiles = tiles;
+  pp.n_tiles = counts;
+  pp.n_pos = counts + 1;
   if ((rc = perm_launch(pp, s))) return rc;
-  if ((rc = prescale_launch(static_cast<const uint16_t*>(x), static_cast<int>(M), static_cast<int>(H), nullptr,
-                            nullptr, px.xh, px.shift, px.sx, px.sxsb, s, true)))
+  if ((rc = prescale_tiled_launch(static_cast<const uint16_t*>(x), static_cast<int>(M), static_cast<int>(H), perm_tok,
+                                  0, static_cast<int>(Pmax), counts + 1, xt, xshift, s, true)))
     return rc;
   TcParams g = {};
   g.wt = W->gate_wtype;
   g.swiglu = 1;
-  g.w0 = static_cast<const uint8_t*>(W->gate_w);
-  g.w1 = static_cast<const uint8_t*>(W->up_w);
+  g.shared_id = shared ? static_cast<int>(E) : -1;
+  g.w[0] = static_cast<const uint8_t*>(W->gate_w);
+  g.w[1] = static_cast<const uint8_t*>(W->up_w);
+  g.ws[0] = static_cast<const uint8_t*>(W->shared_gate_w);
+  g.ws[1] = static_cast<const uint8_t*>(W->shared_up_w);
   g.row_bytes = row_bytes_of(W->gate_wtype, H);
   g.expert_stride = F * g.row_bytes;
   g.N = static_cast<int>(F);
   g.K = static_cast<int>(H);
   g.M = static_cast<int>(M);
-  g.xh = px.xh;
-  g.xshift = px.shift;
-  g.sx = px.sx;
-  g.sxsb = px.sxsb;
-  g.x_rows = perm_tok;
+  g.xt = xt;
+  g.xshift = xshift;
   g.tiles = tiles;
-  g.tile_count = n_tiles;
+  g.tile_count = counts;
   g.y = h_perm;
   g.status = c->status;
-  if ((rc = tc_gemm_launch(g, nt, static_cast<int>(max_tiles), s, true))) return rc;
-  if ((rc = prescale_launch(h_perm, static_cast<int>(P), static_cast<int>(F), nullptr, nullptr, ph.xh, ph.shift, ph.sx,
-                            ph.sxsb, s, true)))
+  if ((rc = tc_gemm_launch(g, nt, static_cast<int>(E), static_cast<int>(max_tiles), c->num_sms, s, true))) return rc;
+  if ((rc = prescale_tiled_launch(h_perm, static_cast<int>(Pmax), static_cast<int>(F), perm_tok, 1,
+                                  static_cast<int>(Pmax), counts + 1, ht, hshift, s, true)))
     return rc;
-  TcParams dn = g;
+  TcParams dn = {};
   dn.wt = W->down_wtype;
   dn.swiglu = 0;
-  dn.w0 = static_cast<const uint8_t*>(W->down_w);
-  dn.w1 = nullptr;
+  dn.shared_id = g.shared_id;
+  dn.w[0] = static_cast<const uint8_t*>(W->down_w);
+  dn.ws[0] = static_cast<const uint8_t*>(W->shared_down_w);
   dn.row_bytes = row_bytes_of(W->down_wtype, F);
   dn.expert_stride = H * dn.row_bytes;
   dn.N = static_cast<int>(H);
   dn.K = static_cast<int>(F);
-  dn.xh = ph.xh;
-  dn.xshift = ph.shift;
-  dn.sx = ph.sx;
-  dn.sxsb = ph.sxsb;
-  dn.x_rows = nullptr;
+  dn.M = static_cast<int>(M);
+  dn.xt = ht;
+  dn.xshift = hshift;
+  dn.tiles = tiles;
+  dn.tile_count = counts;
   dn.y = y_perm;
-  if ((rc = tc_gemm_launch(dn, nt, static_cast<int>(max_tiles), s, true))) return rc;
-  if (shared) {
-    TcParams sg = g;
-    sg.w0 = static_cast<const uint8_t*>(W->shared_gate_w);
-    sg.w1 = static_cast<const uint8_t*>(W->shared_up_w);
-    sg.expert_stride = 0;
-    sg.x_rows = nullptr;
-    sg.tiles = nullptr;
-    sg.tile_count = nullptr;
-    sg.y = h_sh;
-    if ((rc = tc_gemm_launch(sg, nt, static_cast<int>((M + nt - 1) / nt), s, true))) return rc;
-    if ((rc = prescale_launch(h_sh, static_cast<int>(M), static_cast<int>(F), nullptr, nullptr, phs.xh, phs.shift,
-                              phs.sx, phs.sxsb, s, true)))
-      return rc;
-    TcParams sd = dn;
-    sd.w0 = static_cast<const uint8_t*>(W->shared_down_w);
-    sd.expert_stride = 0;
-    sd.xh = phs.xh;
-    sd.xshift = phs.shift;
-    sd.sx = phs.sx;
-    sd.sxsb = phs.sxsb;
-    sd.tiles = nullptr;
-    sd.tile_count = nullptr;
-    sd.y = y_sh;
-    if ((rc = tc_gemm_launch(sd, nt, static_cast<int>((M + nt - 1) / nt), s, true))) return rc;
-  }
+  dn.status = c->status;
+  if ((rc = tc_gemm_launch(dn, nt, static_cast<int>(E), static_cast<int>(max_tiles), c->num_sms, s, true))) return rc;
   CombineParams cp = {};
   cp.M = static_cast<int>(M);
   cp.H = static_cast<int>(H);
@@ -590,7 +561,7 @@ static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, in
   cp.slot_map = pos_of;
   cp.sel_w = sel_w;
   cp.y_union = y_perm;
-  cp.y_shared = y_sh;
+  cp.shared_rows = shared ? shared_pos : nullptr;
   cp.out = static_cast<uint16_t*>(y);
   cp.rows_are_positions = 1;
   if ((rc = combine_launch(cp, s, true))) return rc;
@@ -703,25 +674,26 @@ extern "C" int aipu_q4k_gemm_tc(aipu_ctx* c, int wtype, const void* w, int64_t N
     return set_error(EINVAL_, "gemm_tc: bad arguments (Q4_K/Q6_K, K % 256 == 0, 16-byte aligned bf16 x)");
   DeviceGuard dg(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = grow(&c->pre, &c->pre_bytes, prex_bytes(M, K), "gemm_tc: scratch");
+  const size_t xb = al256x(xt_bytes(M, K));
+  int rc = grow(&c->pre, &c->pre_bytes, xb + al256x(4 * M), "gemm_tc: scratch");
   if (rc) return rc;
-  const PreX px = prex_carve(c->pre, M, K);
-  rc = prescale_launch(static_cast<const uint16_t*>(x), static_cast<int>(M), static_cast<int>(K), nullptr, nullptr,
-                       px.xh, px.shift, px.sx, px.sxsb, s, false);
+  uint8_t* xt = static_cast<uint8_t*>(c->pre);
+  int* shift = reinterpret_cast<int*>(xt + xb);
+  const int rpad = static_cast<int>((M + 7) & ~7LL);
+  rc = prescale_tiled_launch(static_cast<const uint16_t*>(x), static_cast<int>(M), static_cast<int>(K), nullptr, 0,
+                             rpad, nullptr, xt, shift, s, false);
   if (rc) return rc;
   TcParams p = {};
   p.wt = wtype;
-  p.w0 = static_cast<const uint8_t*>(w);
+  p.shared_id = -1;
+  p.w[0] = static_cast<const uint8_t*>(w);
   p.row_bytes = row_bytes_of(wtype, K);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.M = static_cast<int>(M);
-  p.xh = px.xh;
-  p.xshift = px.shift;
-  p.sx = px.sx;
-  p.sxsb = px.sxsb;
+  p.xt = xt;
+  p.xshift = shift;
   p.y = static_cast<uint16_t*>(y);
   p.status = c->status;
-  const int nt = 64;
-  return tc_gemm_launch(p, nt, static_cast<int>((M + nt - 1) / nt), s, true);
+  return tc_gemm_launch(p, 128, 1, static_cast<int>((M + 127) / 128), c->num_sms, s, true);
 }

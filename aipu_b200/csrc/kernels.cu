@@ -332,27 +332,53 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
 // (tools/glm_model_q4k_ref.py:799-809)
 __global__ void combine_kernel(const CombineParams p) {
   pdl_wait();
-  const int64_t total = static_cast<int64_t>(p.M) * p.H;
+  // 8 consecutive outputs per thread (H % 8 == 0): 16-byte loads of every expert row
+  const int hv = p.H >> 3;
+  const int64_t total = static_cast<int64_t>(p.M) * hv;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int m = static_cast<int>(i / p.H);
-    const int d = static_cast<int>(i - static_cast<int64_t>(m) * p.H);
-    float facc = 0.f;
+    const int m = static_cast<int>(i / hv);
+    const int d8 = static_cast<int>(i - static_cast<int64_t>(m) * hv);
+    float facc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) facc[j] = 0.f;
     for (int s = 0; s < p.topk; ++s) {
       const int u = p.slot_map[m * p.topk + s];
       const float wv = bf16_bits_to_f32(p.sel_w[m * p.topk + s]);
       const int64_t row = p.rows_are_positions ? static_cast<int64_t>(u) : static_cast<int64_t>(u) * p.M + m;
-      const float yv = bf16_bits_to_f32(p.y_union[row * p.H + d]);
-      facc = __fadd_rn(facc, __fmul_rn(wv, yv));
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.y_union + row * p.H) + d8);
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        facc[2 * j] = __fadd_rn(facc[2 * j], __fmul_rn(wv, bf16_bits_to_f32(w4[j] & 0xFFFFu)));
+        facc[2 * j + 1] = __fadd_rn(facc[2 * j + 1], __fmul_rn(wv, bf16_bits_to_f32(w4[j] >> 16)));
+      }
     }
-    if (p.y_shared) facc = __fadd_rn(facc, bf16_bits_to_f32(p.y_shared[i]));
-    p.out[i] = bf16_rne_bits(facc);
+    const uint16_t* sh = nullptr;
+    if (p.shared_rows) sh = p.y_union + static_cast<int64_t>(p.shared_rows[m]) * p.H;
+    else if (p.y_shared) sh = p.y_shared + static_cast<int64_t>(m) * p.H;
+    if (sh) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(sh) + d8);
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        facc[2 * j] = __fadd_rn(facc[2 * j], bf16_bits_to_f32(w4[j] & 0xFFFFu));
+        facc[2 * j + 1] = __fadd_rn(facc[2 * j + 1], bf16_bits_to_f32(w4[j] >> 16));
+      }
+    }
+    uint4 o;
+    o.x = bf16_rne_bits(facc[0]) | (static_cast<uint32_t>(bf16_rne_bits(facc[1])) << 16);
+    o.y = bf16_rne_bits(facc[2]) | (static_cast<uint32_t>(bf16_rne_bits(facc[3])) << 16);
+    o.z = bf16_rne_bits(facc[4]) | (static_cast<uint32_t>(bf16_rne_bits(facc[5])) << 16);
+    o.w = bf16_rne_bits(facc[6]) | (static_cast<uint32_t>(bf16_rne_bits(facc[7])) << 16);
+    reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(m) * p.H)[d8] = o;
   }
   pdl_launch_dependents();
 }
 
 int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl) {
-  const int64_t total = static_cast<int64_t>(p.M) * p.H;
+  if (p.H % 8) return set_error(EINVAL_, "combine: H % 8 != 0");
+  const int64_t total = static_cast<int64_t>(p.M) * (p.H / 8);
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 4096) blocks = 4096;
   CombineParams q = p;
@@ -360,54 +386,85 @@ int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl) {
 }
 
 // ------------------------------------------------------------------ prefill permutation
-// One CTA of 1024 threads. Experts are assigned to warps; for each expert a warp walks the tokens in
-// order, 32 at a time, and places every token that selected it with a ballot prefix, so the token
-// order inside an expert's list is ascending and the result is deterministic. A position is never
-// shared: a token selects an expert at most once.
-__global__ void __launch_bounds__(1024) perm_kernel(const PermParams p) {
+// One CTA per segment (expert e < E; segment E = shared expert). Every CTA counts the selections of
+// all experts (shared-memory histogram), takes its segment's start as the padded prefix of the
+// counts, then walks the tokens in order, 256 at a time, and places each token that selected its
+// expert with a block-wide prefix of flags, so the order inside a segment is ascending and the
+// result deterministic. A position is never shared: a token selects an expert at most once.
+// CTA 0 also writes the tile list (segments in order, nt tokens per tile) and the position count.
+__global__ void __launch_bounds__(256) perm_kernel(const PermParams p) {
   pdl_wait();
-  __shared__ int cnt[1024];
-  __shared__ int off[1025];
+  __shared__ int cnt[1025];
+  __shared__ int wsum[8];
+  __shared__ int s_off;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int e = tid; e < p.E; e += 1024) cnt[e] = 0;
+  const int seg = blockIdx.x;
+  const int nseg = p.E + (p.with_shared ? 1 : 0);
+  for (int e = tid; e < nseg; e += 256) cnt[e] = (e == p.E) ? p.T : 0;
   __syncthreads();
-  for (int i = tid; i < p.T * p.topk; i += 1024) atomicAdd(&cnt[p.sel[i]], 1);
+  for (int i = tid; i < p.T * p.topk; i += 256) atomicAdd(&cnt[p.sel[i]], 1);
+  __syncthreads();
+  // start of this segment: sum over earlier segments of the count rounded up to 8
+  int part = 0;
+  for (int e = tid; e < seg; e += 256) part += (cnt[e] + 7) & ~7;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) wsum[warp] = part;
   __syncthreads();
   if (tid == 0) {
-    int acc = 0, nt = 0;
-    for (int e = 0; e < p.E; ++e) {
-      off[e] = acc;
-      for (int t0 = 0; t0 < cnt[e]; t0 += p.nt) p.tiles[nt++] = make_int4(e, acc + t0, min(p.nt, cnt[e] - t0), 0);
-      acc += cnt[e];
-    }
-    off[p.E] = acc;
-    *p.n_tiles = nt;
+    int acc = 0;
+    for (int w = 0; w < 8; ++w) acc += wsum[w];
+    s_off = acc;
   }
   __syncthreads();
-  for (int e = warp; e < p.E; e += 32) {
-    int base = off[e];
-    for (int t0 = 0; t0 < p.T; t0 += 32) {
-      const int t = t0 + lane;
-      int slot = -1;
-      if (t < p.T)
-        for (int s = 0; s < p.topk; ++s)
-          if (p.sel[t * p.topk + s] == e) slot = s;
-      const unsigned m = __ballot_sync(0xffffffffu, slot >= 0);
-      if (slot >= 0) {
-        const int pos = base + __popc(m & ((1u << lane) - 1u));
-        p.perm_tok[pos] = t;
-        p.pos_of[t * p.topk + slot] = pos;
-      }
-      base += __popc(m);
+  const int off = s_off;
+  if (seg == 0 && tid == 0) {
+    int acc = 0, nt = 0;
+    for (int e = 0; e < nseg; ++e) {
+      for (int t0 = 0; t0 < cnt[e]; t0 += p.nt) p.tiles[nt++] = make_int4(e, acc + t0, min(p.nt, cnt[e] - t0), 0);
+      acc += (cnt[e] + 7) & ~7;
     }
+    *p.n_tiles = nt;
+    *p.n_pos = acc;
   }
+  int base = off;
+  for (int t0 = 0; t0 < p.T; t0 += 256) {
+    const int t = t0 + tid;
+    int slot = -1;
+    if (t < p.T) {
+      if (seg == p.E) {
+        slot = p.topk;
+      } else {
+        for (int s = 0; s < p.topk; ++s)
+          if (p.sel[t * p.topk + s] == seg) slot = s;
+      }
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, slot >= 0);
+    __syncthreads();  // wsum reuse
+    if (lane == 0) wsum[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < 8; ++w) {
+      before += (w < warp) ? wsum[w] : 0;
+      total += wsum[w];
+    }
+    if (slot >= 0) {
+      const int pos = base + before + __popc(m & ((1u << lane) - 1u));
+      p.perm_tok[pos] = t;
+      if (slot == p.topk) p.shared_pos[t] = pos;
+      else p.pos_of[t * p.topk + slot] = pos;
+    }
+    base += total;
+  }
+  for (int pos = base + tid; pos < off + (((base - off) + 7) & ~7); pos += 256) p.perm_tok[pos] = -1;
   pdl_launch_dependents();
 }
 
 int perm_launch(const PermParams& p, cudaStream_t s) {
-  if (p.E > 1024 || p.E <= 0) return set_error(EINVAL_, "perm: E must be 1..1024");
+  if (p.E > 1024 || p.E <= 0 || p.nt <= 0) return set_error(EINVAL_, "perm: E must be 1..1024");
   PermParams q = p;
-  return launch_kernel(reinterpret_cast<const void*>(perm_kernel), dim3(1), dim3(1024), 0, s, true, &q);
+  return launch_kernel(reinterpret_cast<const void*>(perm_kernel), dim3(p.E + (p.with_shared ? 1 : 0)), dim3(256), 0,
+                       s, true, &q);
 }
 
 // ------------------------------------------------------------------ activations

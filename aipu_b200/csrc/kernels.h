@@ -36,43 +36,57 @@ struct CombineParams {
   const uint16_t* y_shared; // bf16 [M, H] (nullable)
   uint16_t* out;            // bf16 [M, H]
   int rows_are_positions;   // 1: slot_map holds the row of y_union directly
+  const int32_t* shared_rows; // [M] row of y_union holding the shared expert's output (nullable)
 };
 
-// prefill token permutation (kernels.cu): per-expert token lists in token order, the position of
-// every (token, slot), and the tile list of the grouped tensor-core GEMM
+// prefill token permutation (kernels.cu): segment e (expert e; segment E = the shared expert over
+// all tokens, when present) holds the tokens that selected e in ascending token order, starting at a
+// multiple of 8 positions; the pad positions after a segment hold token -1. Also the position of
+// every (token, slot), the shared-expert position of every token, and the tile list.
 struct PermParams {
   const int32_t* sel;      // [T, topk]
   int T, topk, E, nt;      // tokens, slots, experts, tokens per tile
-  int32_t* perm_tok;       // [T*topk] token of each position
+  int with_shared;         // 1: add segment E with every token
+  int32_t* perm_tok;       // [positions] token of each position (-1: pad)
   int32_t* pos_of;         // [T, topk] position of each (token, slot)
-  int4* tiles;             // (expert, first position, tokens, 0)
+  int32_t* shared_pos;     // [T] position of each token in the shared segment (with_shared)
+  int4* tiles;             // (segment, first position, tokens, 0)
   int32_t* n_tiles;        // [1]
+  int32_t* n_pos;          // [1] positions used (padded)
 };
 int perm_launch(const PermParams& p, cudaStream_t s);
+// upper bound of the positions perm_kernel uses
+inline int64_t perm_max_positions(int64_t T, int topk, int E, int with_shared) {
+  return T * topk + (with_shared ? T : 0) + 8 * static_cast<int64_t>(E + 1);
+}
+inline int64_t perm_max_tiles(int64_t T, int topk, int E, int with_shared, int nt) {
+  return (T * topk + nt - 1) / nt + E + (with_shared ? (T + nt - 1) / nt : 0);
+}
 
-// prefill GEMM on tcgen05 (tc_gemm.cu)
+// prefill GEMM on tcgen05 (tc_gemm.cu): persistent, items = (tile of <= nt tokens, row tile), nt 64 or 128
 struct TcParams {
   int wt;                  // WT_Q4K or WT_Q6K
-  int swiglu;              // 1: A rows 0..63 gate rows, 64..127 up rows; y = h = bf16(silu(g) * u)
-  const uint8_t* w0;       // weights (gate rows for swiglu), expert e at w0 + e * expert_stride
-  const uint8_t* w1;       // up rows (swiglu)
+  int swiglu;              // 1: 64 gate + 64 up rows per item; y = h = bf16(silu(g) * u)
+  int use_tmap;            // set by tc_gemm_launch
+  int shared_id;           // segment id that uses the shared-expert weights ws (-1: none)
+  const uint8_t* w[2];     // routed weights (gate/down, up), expert e at w + e * expert_stride
+  const uint8_t* ws[2];    // shared-expert weights (gate/down, up)
   int64_t row_bytes;
   int64_t expert_stride;
   int N, K, M;             // output rows per matrix, reduction length, tokens (dense mode)
-  const __half* xh;        // prescaled fp16 activations [rows, K]
-  const int* xshift;       // [rows] power-of-two prescale
-  const __half* sx;        // [rows, K/256, 16] sub-block sums (Q4_K)
-  const float* sxsb;       // [rows, K/256] super-block sums (Q4_K)
-  const int* x_rows;       // position -> activation row (nullable: identity)
-  const int4* tiles;       // per tile (group, first position, tokens, 0) (nullable: dense tiles over M)
-  const int* tile_count;   // device number of tiles (nullable)
-  const int* group_ids;    // group -> expert (nullable: identity)
+  const uint8_t* xt;       // prescaled activations in the tiled operand layout (prescale_tiled)
+  const int* xshift;       // [positions] power-of-two prescale
+  const int4* tiles;       // per tile (segment, first position, tokens, 0) (nullable: dense tiles over M)
+  const int* tile_count;   // device number of tiles
   uint16_t* y;             // bf16 [positions, N]
   int* status;
+  alignas(64) CUtensorMap wmap[2];
+  alignas(64) CUtensorMap smap[2];
 };
-int tc_gemm_launch(const TcParams& p, int nt, int max_tiles, cudaStream_t s, bool pdl);
-int prescale_launch(const uint16_t* x, int R, int K, const int* rows, const int* n_rows_dev, __half* xh, int* shift,
-                    __half* sx, float* sxsb, cudaStream_t s, bool pdl);
+int tc_gemm_launch(TcParams& p, int nt, int n_experts, int max_tiles, int num_sms, cudaStream_t s, bool pdl);
+size_t xt_bytes(int64_t R, int64_t K);
+int prescale_tiled_launch(const uint16_t* x, int R, int K, const int* rows, int rows_mask, int n_pos_max,
+                          const int* n_pos_dev, uint8_t* xt, int* shift, cudaStream_t s, bool pdl);
 
 int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, int out_bf16, cudaStream_t s);
 int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,

@@ -215,16 +215,7 @@ def moe_decode(M_list=(1, 4), reps=200):
 
     d = torch.device("cuda", torch.cuda.current_device())
     H, Fd, E, T = 6144, 2048, 256, 8
-    W = ops.MoeLayerWeights(
-        hidden=H, ffn=Fd, n_experts=E, topk=T, router_wtype=F.F32,
-        router_w=torch.randn((H, E), device=d, generator=torch.Generator(device=d).manual_seed(1)) * 0.02,
-        router_bias=torch.randn((E,), device=d, generator=torch.Generator(device=d).manual_seed(2)) * 0.01,
-        gate_w=F.random_rows_dev(F.Q4_K, E * Fd, H, seed=11, device=d),
-        up_w=F.random_rows_dev(F.Q4_K, E * Fd, H, seed=12, device=d),
-        down_w=F.random_rows_dev(F.Q6_K, E * H, Fd, seed=13, device=d),
-        shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=14, device=d),
-        shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=15, device=d),
-        shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
+    W = moe_layer_weights(d)
     ctx = ops.Context(d)
     out = {}
     expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
@@ -254,9 +245,67 @@ def moe_decode(M_list=(1, 4), reps=200):
         byts = H * E * 4 + (union + 1) * expert_bytes
         out[f"M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(M / t, 1), "union_experts": union,
                         "hbm_bytes": byts, "hbm_gbs": round(byts / t / 1e9, 1)}
+    out["prefill"] = moe_prefill(W)
     del W
     torch.cuda.empty_cache()
     return out
+
+
+def moe_layer_weights(d):
+    """BASELINE configs 3/4 weights: 256 routed experts + 1 shared, hidden 6144, FFN 2048."""
+    import torch
+
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    H, Fd, E, T = 6144, 2048, 256, 8
+    return ops.MoeLayerWeights(
+        hidden=H, ffn=Fd, n_experts=E, topk=T, router_wtype=F.F32,
+        router_w=torch.randn((H, E), device=d, generator=torch.Generator(device=d).manual_seed(1)) * 0.02,
+        router_bias=torch.randn((E,), device=d, generator=torch.Generator(device=d).manual_seed(2)) * 0.01,
+        gate_w=F.random_rows_dev(F.Q4_K, E * Fd, H, seed=11, device=d),
+        up_w=F.random_rows_dev(F.Q4_K, E * Fd, H, seed=12, device=d),
+        down_w=F.random_rows_dev(F.Q6_K, E * H, Fd, seed=13, device=d),
+        shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=14, device=d),
+        shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=15, device=d),
+        shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
+
+
+def moe_prefill(W, M=2048, reps=10):
+    """BASELINE config 4 on one GPU: one MoE layer over 2048 tokens (router, per-expert token lists,
+    tcgen05 SwiGLU and down GEMMs grouped by expert, shared expert, combine), CUDA-graph replays.
+    Tensor FLOPs counted = 2 * (token-expert pairs + tokens for the shared expert) * 3 * H * F."""
+    import torch
+
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    H, Fd, T = W.hidden, W.ffn, W.topk
+    ctx = ops.Context(d)
+    x = torch.randn((M, H), device=d, generator=torch.Generator(device=d).manual_seed(4)).to(torch.bfloat16)
+    y = torch.empty((M, H), dtype=torch.bfloat16, device=d)
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        ops.moe_layer(W, x, ctx=ctx, out=y)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            ops.moe_layer(W, x, ctx=ctx, out=y)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / reps / 1e3
+    flops = 2.0 * (M * T + M) * 3 * H * Fd
+    _, tf_peak, kind = peaks()
+    return {"tokens": M, "ms_per_layer": round(t * 1e3, 3), "tokens_per_s": round(M / t, 1),
+            "tensor_tflops": round(flops / t / 1e12, 1), "frac_of_bf16_peak": round(flops / t / 1e12 / tf_peak, 4),
+            "peak_source": kind, "flops": flops}
 
 
 def main():
