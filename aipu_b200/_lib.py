@@ -17,6 +17,7 @@ Q4_K, Q6_K, Q8_0, F16, F32 = 0, 1, 2, 3, 4
 DT_F32, DT_BF16 = 0, 1
 MODE_FAST, MODE_STRICT = 0, 1
 FLAG_PDL = 1
+FLAG_STRICT = 2
 
 c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 

@@ -195,7 +195,7 @@ int aipu_ctx_destroy(aipu_ctx* c) {
 }
 
 int aipu_ctx_set_flags(aipu_ctx* c, int flags) {
-  if (!c || (flags & ~AIPU_FLAG_PDL)) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
+  if (!c || (flags & ~(AIPU_FLAG_PDL | AIPU_FLAG_STRICT))) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
   c->flags = flags;
   return OK;
 }
@@ -363,7 +363,6 @@ static int moe_scratch(aipu_ctx* c, int64_t M, int64_t E, int T, int64_t H, int6
   for (size_t v : sz) total += v;
   if (total > c->moe_bytes) {
     cudaFree(c->moe);
-  cudaFree(c->pre);
     c->moe = nullptr;
     c->moe_bytes = 0;
     if (cudaMalloc(&c->moe, total) != cudaSuccess) return set_error(ENOMEM_, "moe: scratch allocation");
@@ -394,6 +393,49 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
                          int n_groups,
                          const void* x, int64_t M, uint16_t* h, uint16_t* y, cudaStream_t s, bool pdl) {
   const int64_t gstride = F * row_bytes_of(gwt, H), dstride = H * row_bytes_of(dwt, F);
+  if (c->flags & AIPU_FLAG_STRICT) {
+    // bit-exact chains (tools/glm_model_q4k_ref.py:702-708): gate into h, up into a temporary,
+    // h = bf16(silu(gate) * up) in place, then the down projection of h
+    const int64_t n = static_cast<int64_t>(n_groups) * M * F;
+    uint16_t* up = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&up), 2 * n, s) != cudaSuccess)
+      return set_error(ENOMEM_, "swiglu (strict): scratch");
+    StrictParams p = {};
+    p.wt = gwt;
+    p.w = static_cast<const uint8_t*>(gw);
+    p.w_group_stride = gstride;
+    p.group_ids = group_ids;
+    p.n_groups_dev = n_groups_dev;
+    p.N = static_cast<int>(F);
+    p.K = static_cast<int>(H);
+    p.M = static_cast<int>(M);
+    p.x = x;
+    p.xt = XT_BF16;
+    p.y = h;
+    p.y_group_stride = M * F;
+    int rc = strict_gemm_grouped_launch(p, n_groups, s);
+    if (!rc) {
+      p.w = static_cast<const uint8_t*>(uw);
+      p.y = up;
+      rc = strict_gemm_grouped_launch(p, n_groups, s);
+    }
+    if (!rc) rc = swiglu_elem_launch(h, up, n, h, s);
+    if (!rc) {
+      StrictParams q = p;
+      q.wt = dwt;
+      q.w = static_cast<const uint8_t*>(dw);
+      q.w_group_stride = dstride;
+      q.N = static_cast<int>(H);
+      q.K = static_cast<int>(F);
+      q.x = h;
+      q.x_group_stride = M * F;
+      q.y = y;
+      q.y_group_stride = M * H;
+      rc = strict_gemm_grouped_launch(q, n_groups, s);
+    }
+    cudaFreeAsync(up, s);
+    return rc;
+  }
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
     const int mb = static_cast<int>(std::min<int64_t>(8, M - m0));
     GemvParams p = {};
@@ -435,9 +477,6 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
 }
 
 // ------------------------------------------------------------------ MoE prefill (many tokens)
-// router -> per-expert token lists -> SwiGLU gate/up and down on the tensor cores, grouped by
-// expert -> shared expert (dense) -> slot-order combine. The weights of each expert are dequantised
-// once per (128-row tile, token tile) for all the expert's tokens.
 // Many-token MoE layer: router -> per-segment token lists (the shared expert is segment E) ->
 // tiled prescale of the permuted tokens -> SwiGLU gate/up on tcgen05 -> tiled prescale of h ->
 // down projection on tcgen05 -> slot-order combine (reference: glm_model_q4k_ref.py:663-809).
@@ -587,10 +626,13 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
   DeviceGuard dg(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // many tokens: the tensor-core path (SwiGLU gate/up in Q4_K, down in Q4_K or Q6_K)
-  if (M >= kPrefillMinTokens && W->gate_wtype == AIPU_Q4_K &&
+  const bool strict = (c->flags & AIPU_FLAG_STRICT) != 0;
+  if (!strict && M >= kPrefillMinTokens && W->gate_wtype == AIPU_Q4_K &&
       (W->down_wtype == AIPU_Q4_K || W->down_wtype == AIPU_Q6_K) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0)
     return moe_prefill(c, W, x, M, y, sel_out, sel_w_out, s);
-  if (M > 1024) return set_error(EINVAL_, "moe_layer: more than 1024 tokens need Q4_K gate/up and Q4_K/Q6_K down");
+  if (M > 1024)
+    return set_error(EINVAL_, strict ? "moe_layer (strict): at most 1024 tokens per call"
+                                     : "moe_layer: more than 1024 tokens need Q4_K gate/up and Q4_K/Q6_K down");
   MoeScratch sc = {};
   int rc = moe_scratch(c, M, E, T, H, F, sc);
   if (rc) return rc;

@@ -41,48 +41,84 @@ int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, i
 // (tools/q4k_ref.py:86-92). 32 rows per block, one thread per (row, token); weights of a 256-wide
 // K chunk are dequantised exactly into shared memory, then every thread runs its own chain.
 constexpr int STRICT_ROWS = 32;
-__global__ void strict_gemm_kernel(int wt, const uint8_t* __restrict__ w, int64_t row_bytes, int N, int K,
-                                   const void* __restrict__ x, int xt, int M, uint16_t* __restrict__ y,
-                                   float* __restrict__ y_f32) {
+__global__ void strict_gemm_kernel(const StrictParams p) {
   __shared__ float ws[STRICT_ROWS][257];
+  const int g = blockIdx.z;
+  if (p.n_groups_dev && g >= *p.n_groups_dev) return;
+  const int e = p.group_ids ? p.group_ids[g] : g;
+  const uint8_t* w = p.w + static_cast<int64_t>(e) * p.w_group_stride;
+  const int64_t row_bytes = row_bytes_of(p.wt, p.K);
   const int r = threadIdx.x & 31;
   const int mloc = threadIdx.x >> 5;
   const int m = blockIdx.y * 8 + mloc;
   const int n = blockIdx.x * STRICT_ROWS + r;
   const int nthr = blockDim.x;
+  const int esz = (p.xt == XT_F32) ? 4 : 2;
+  const uint8_t* x = static_cast<const uint8_t*>(p.x) + static_cast<int64_t>(g) * p.x_group_stride * esz;
   float acc = 0.f;
-  for (int k0 = 0; k0 < K; k0 += 256) {
-    const int kl = min(256, K - k0);
+  for (int k0 = 0; k0 < p.K; k0 += 256) {
+    const int kl = min(256, p.K - k0);
     __syncthreads();
     for (int idx = threadIdx.x; idx < STRICT_ROWS * kl; idx += nthr) {
       const int rr = idx / kl, kk = idx - rr * kl;
       const int nn = blockIdx.x * STRICT_ROWS + rr;
-      ws[rr][kk] = (nn < N) ? deq_one(wt, w + static_cast<int64_t>(nn) * row_bytes, k0 + kk) : 0.f;
+      ws[rr][kk] = (nn < p.N) ? deq_one(p.wt, w + static_cast<int64_t>(nn) * row_bytes, k0 + kk) : 0.f;
     }
     __syncthreads();
-    if (m < M) {
-      const int64_t xo = static_cast<int64_t>(m) * K + k0;
+    if (m < p.M) {
+      const int64_t xo = static_cast<int64_t>(m) * p.K + k0;
       for (int kk = 0; kk < kl; ++kk) {
-        const float xv = (xt == XT_F32) ? __ldg(reinterpret_cast<const float*>(x) + xo + kk)
-                                        : bf16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(x) + xo + kk));
+        const float xv = (p.xt == XT_F32) ? __ldg(reinterpret_cast<const float*>(x) + xo + kk)
+                                          : bf16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(x) + xo + kk));
         acc = __fadd_rn(acc, __fmul_rn(xv, ws[r][kk]));
       }
     }
   }
-  if (m < M && n < N) {
-    if (y) y[static_cast<int64_t>(m) * N + n] = bf16_rne_bits(acc);
-    if (y_f32) y_f32[static_cast<int64_t>(m) * N + n] = acc;
+  if (m < p.M && n < p.N) {
+    const int64_t o = static_cast<int64_t>(g) * p.y_group_stride + static_cast<int64_t>(m) * p.N + n;
+    if (p.y) p.y[o] = bf16_rne_bits(acc);
+    if (p.y_f32) p.y_f32[o] = acc;
   }
+}
+
+int strict_gemm_grouped_launch(const StrictParams& p, int n_groups, cudaStream_t s) {
+  if (p.N <= 0 || p.M <= 0 || p.K <= 0 || n_groups <= 0) return OK;
+  const int mb = p.M < 8 ? p.M : 8;
+  dim3 grid((p.N + STRICT_ROWS - 1) / STRICT_ROWS, (p.M + 7) / 8, n_groups);
+  if (grid.y > 65535 || grid.z > 65535) return set_error(EINVAL_, "strict gemm: too many tokens or groups");
+  StrictParams q = p;
+  return launch_kernel(reinterpret_cast<const void*>(strict_gemm_kernel), grid, dim3(32 * mb), 0, s, false, &q);
 }
 
 int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,
                        cudaStream_t s) {
-  if (N <= 0 || M <= 0 || K <= 0) return OK;
-  const int mb = M < 8 ? M : 8;
-  dim3 grid((N + STRICT_ROWS - 1) / STRICT_ROWS, (M + 7) / 8);
-  strict_gemm_kernel<<<grid, 32 * mb, 0, s>>>(wt, static_cast<const uint8_t*>(w), row_bytes_of(wt, K), N, K, x, xt,
-                                              M, y, y_f32);
-  return set_cuda_error(cudaGetLastError(), "strict_gemm_kernel");
+  StrictParams p = {};
+  p.wt = wt;
+  p.w = static_cast<const uint8_t*>(w);
+  p.N = N;
+  p.K = K;
+  p.M = M;
+  p.x = x;
+  p.xt = xt;
+  p.y = y;
+  p.y_f32 = y_f32;
+  return strict_gemm_grouped_launch(p, 1, s);
+}
+
+// h = bf16( fp32(silu_bf(g)) * fp32(u) ): the SwiGLU product of tools/glm_model_q4k_ref.py:706
+__global__ void swiglu_elem_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, int64_t n,
+                                   uint16_t* __restrict__ h) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    h[i] = bf16_rne_bits(__fmul_rn(glm_silu_bf(bf16_bits_to_f32(g[i])), bf16_bits_to_f32(u[i])));
+}
+
+int swiglu_elem_launch(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* h, cudaStream_t s) {
+  if (n <= 0) return OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 8192) blocks = 8192;
+  swiglu_elem_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(g, u, n, h);
+  return set_cuda_error(cudaGetLastError(), "swiglu_elem_kernel");
 }
 
 // ------------------------------------------------------------------ strict router

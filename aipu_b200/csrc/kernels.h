@@ -89,6 +89,24 @@ int prescale_tiled_launch(const uint16_t* x, int R, int K, const int* rows, int 
                           const int* n_pos_dev, uint8_t* xt, int* shift, cudaStream_t s, bool pdl);
 
 int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, int out_bf16, cudaStream_t s);
+// exact GEMM (sequential fp32 chains), optionally over groups (experts): group g uses weights
+// w + group_ids[g] * w_group_stride, activations x + g * x_group_stride, output y + g * y_group_stride
+struct StrictParams {
+  int wt;
+  const uint8_t* w;
+  int64_t w_group_stride;
+  const int* group_ids;     // nullable: identity
+  const int* n_groups_dev;  // nullable: all launched groups are live
+  int N, K, M;
+  const void* x;
+  int xt;
+  int64_t x_group_stride;   // elements
+  uint16_t* y;              // bf16 (nullable)
+  float* y_f32;             // fp32 accumulators (nullable)
+  int64_t y_group_stride;   // elements
+};
+int strict_gemm_grouped_launch(const StrictParams& p, int n_groups, cudaStream_t s);
+int swiglu_elem_launch(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* h, cudaStream_t s);
 int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,
                        cudaStream_t s);
 int router_launch(const RouterParams& p, cudaStream_t s, bool pdl);

@@ -63,10 +63,12 @@ class Context:
         except Exception:
             pass
 
-    def set_flags(self, pdl: bool = False) -> "Context":
+    def set_flags(self, pdl: bool = False, strict: bool = False) -> "Context":
         """pdl=True: fast GEMMs start streaming weights while the previous kernel drains (only when no
-        kernel right before a GEMM writes its weights)."""
-        check(lib().aipu_ctx_set_flags(self.handle, L.FLAG_PDL if pdl else 0))
+        kernel right before a GEMM writes its weights). strict=True: swiglu_expert and moe_layer run
+        the bit-exact path (the reference's sequential fp32 chains)."""
+        flags = (L.FLAG_PDL if pdl else 0) | (L.FLAG_STRICT if strict else 0)
+        check(lib().aipu_ctx_set_flags(self.handle, flags))
         return self
 
     def status(self) -> int:

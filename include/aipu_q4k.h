@@ -66,6 +66,11 @@ int aipu_ctx_destroy(aipu_ctx* ctx);
  * starts while the previous kernel on the stream is still running (activations are read only after
  * that kernel completes). Set it only when no kernel just before the GEMM writes the weights. */
 #define AIPU_FLAG_PDL 1
+/* AIPU_FLAG_STRICT: aipu_swiglu_expert and aipu_moe_layer run the bit-exact path: every GEMM as
+ * the reference's sequential fp32 chain in K order (tools/q4k_ref.py:86-92), the SwiGLU product
+ * and the combine in the reference's op order, so outputs equal tools/glm_model_q4k_ref.py
+ * swiglu_expert / the decoder block's MoE branch bit for bit (slower: no tensor cores). */
+#define AIPU_FLAG_STRICT 2
 int aipu_ctx_set_flags(aipu_ctx* ctx, int flags);
 /* device status word of the context (0 = no bounded wait ever gave up); resets it to 0 */
 int aipu_ctx_status(aipu_ctx* ctx, int* status);

@@ -326,3 +326,83 @@ def test_gemm_grouped_matches_single(wt):
         assert_close_bf16(bf16_np(y[g]), ref, f"group {g}")
         single = ops.gemm(wt, to_dev(w[g]), N, K, np_to_bf16_dev(x))
         assert qo.ulp_diff_bf16(bf16_np(single), bf16_np(y[g])).max() <= 1
+
+
+def _strict_ctx():
+    return ops.Context(dev()).set_flags(strict=True)
+
+
+def test_swiglu_expert_strict_bitexact():
+    """Strict mode: gate, up, SiLU product and down exactly as tools/glm_model_q4k_ref.py:702-708."""
+    H, Fd, M = 6144, 2048, 3
+    wg = F.random_rows_np(F.Q4_K, Fd, H, seed=31)
+    wu = F.random_rows_np(F.Q4_K, Fd, H, seed=32)
+    wd = F.random_rows_np(F.Q6_K, H, Fd, seed=33)
+    x = qo.bf16_round(np.random.default_rng(4).standard_normal((M, H)).astype(F32))
+    g_ = qo.dequant_rows(F.Q4_K, wg, Fd, H)
+    u_ = qo.dequant_rows(F.Q4_K, wu, Fd, H)
+    d_ = qo.dequant_rows(F.Q6_K, wd, H, Fd)
+    h_ref = mo.swiglu_hidden(x, g_, u_)
+    y_ref = qo.matmul_seq(h_ref, d_)
+    y, h = ops.swiglu_expert(F.Q4_K, to_dev(wg), to_dev(wu), F.Q6_K, to_dev(wd), H, Fd, np_to_bf16_dev(x),
+                             ctx=_strict_ctx(), return_hidden=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(bf16_np(h).view(np.uint32), h_ref.view(np.uint32))
+    assert np.array_equal(bf16_np(y).view(np.uint32), y_ref.view(np.uint32))
+
+
+def test_moe_layer_reference_fixture_strict(golden):
+    """Strict mode reproduces the reference decoder-block MoE branch bit for bit."""
+    g = golden("moe_golden")
+    E, T, D, Fd = (int(v) for v in g["moe_meta"])
+    Fp = 256
+    gate = np.zeros((E + 1, Fp, 144), np.uint8)
+    up = np.zeros((E + 1, Fp, 144), np.uint8)
+    gate[:, :Fd] = g["moe_gate_w"]
+    up[:, :Fd] = g["moe_up_w"]
+    down = g["moe_down_w"]
+    W = ops.MoeLayerWeights(hidden=D, ffn=Fp, n_experts=E, topk=T, router_wtype=F.Q4_K,
+                            router_w=to_dev(g["moe_router_w"]), gate_w=to_dev(gate[:E]), up_w=to_dev(up[:E]),
+                            down_w=to_dev(down[:E]), gate_wtype=F.Q4_K, down_wtype=F.Q4_K,
+                            shared_gate_w=to_dev(gate[E]), shared_up_w=to_dev(up[E]), shared_down_w=to_dev(down[E]))
+    y, sel, sw = ops.moe_layer(W, np_to_bf16_dev(g["moe_x"].view(F32)), ctx=_strict_ctx(), return_routing=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(sel.cpu().numpy(), g["moe_sel"])
+    assert np.array_equal(bf16_np(sw).view(np.uint32), g["moe_sw"])
+    assert np.array_equal(bf16_np(y).view(np.uint32), g["moe_y"])
+
+
+@pytest.mark.parametrize("M,H,Fd,E", [(1, 6144, 2048, 256), (4, 6144, 2048, 256), (70, 512, 256, 16)])
+def test_moe_layer_config3_strict_bitexact(M, H, Fd, E):
+    """Strict mode at BASELINE config-3 dims (and 70 tokens, past the tensor-core threshold, at
+    reduced dims): outputs bit-identical to the oracle's sequential restatement of the reference."""
+    d = dev()
+    T = 8
+    gate = F.random_rows_dev(F.Q4_K, E * Fd, H, seed=41, device=d)
+    up = F.random_rows_dev(F.Q4_K, E * Fd, H, seed=42, device=d)
+    down = F.random_rows_dev(F.Q6_K, E * H, Fd, seed=43, device=d)
+    sg = F.random_rows_dev(F.Q4_K, Fd, H, seed=44, device=d)
+    su = F.random_rows_dev(F.Q4_K, Fd, H, seed=45, device=d)
+    sd = F.random_rows_dev(F.Q6_K, H, Fd, seed=46, device=d)
+    rng = np.random.default_rng(19 + M)
+    wr = rng.normal(0, 0.02, (H, E)).astype(F32)
+    bias = rng.normal(0, 0.01, E).astype(F32)
+    x = qo.bf16_round(rng.standard_normal((M, H)).astype(F32))
+    W = ops.MoeLayerWeights(hidden=H, ffn=Fd, n_experts=E, topk=T, router_wtype=F.F32, router_w=to_dev(wr),
+                            router_bias=to_dev(bias), gate_w=gate, up_w=up, down_w=down,
+                            shared_gate_w=sg, shared_up_w=su, shared_down_w=sd)
+    y, sel, sw = ops.moe_layer(W, np_to_bf16_dev(x), ctx=_strict_ctx(), return_routing=True)
+    torch.cuda.synchronize()
+    gate_v, up_v, down_v = gate.view(E, Fd, -1), up.view(E, Fd, -1), down.view(E, H, -1)
+
+    def deq(e):
+        return (qo.dequant_rows(F.Q4_K, gate_v[e].cpu().numpy(), Fd, H),
+                qo.dequant_rows(F.Q4_K, up_v[e].cpu().numpy(), Fd, H),
+                qo.dequant_rows(F.Q6_K, down_v[e].cpu().numpy(), H, Fd))
+
+    shared = (qo.dequant_rows(F.Q4_K, sg.cpu().numpy(), Fd, H), qo.dequant_rows(F.Q4_K, su.cpu().numpy(), Fd, H),
+              qo.dequant_rows(F.Q6_K, sd.cpu().numpy(), H, Fd))
+    y_ref, sel_ref, sw_ref = mo.moe_layer(x, wr.T.copy(), deq, shared, T, bias=bias)
+    assert np.array_equal(sel.cpu().numpy(), sel_ref)
+    assert np.array_equal(bf16_np(sw).view(np.uint32), sw_ref.view(np.uint32))
+    assert np.array_equal(bf16_np(y).view(np.uint32), y_ref.view(np.uint32))
