@@ -67,6 +67,10 @@ SIGNATURES = {
                                c_void_p, c_void_p]),
     "aipu_swiglu_expert": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64, c_int64,
                                    c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "aipu_moe_experts": (c_int, [c_void_p, ctypes.POINTER(MoeWeights), c_int64, c_void_p, c_int64, c_void_p, c_void_p,
+                                 c_int64, c_int64, c_void_p, c_void_p]),
+    "aipu_moe_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                 c_void_p, c_void_p]),
 }
 
 _lib = None

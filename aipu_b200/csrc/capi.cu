@@ -97,6 +97,8 @@ struct aipu_ctx {
   // prefill scratch (grown on demand)
   void* pre = nullptr;
   size_t pre_bytes = 0;
+  void* rt = nullptr;     // router outputs of the many-token path
+  size_t rt_bytes = 0;
 };
 
 static int grow(void** buf, size_t* have, size_t need, const char* what) {
@@ -187,6 +189,7 @@ int aipu_ctx_destroy(aipu_ctx* c) {
   cudaFree(c->router_counters);
   cudaFree(c->moe);
   cudaFree(c->pre);
+  cudaFree(c->rt);
   if (c->side) cudaStreamDestroy(c->side);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
@@ -477,71 +480,66 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
 }
 
 // ------------------------------------------------------------------ MoE prefill (many tokens)
-// Many-token MoE layer: router -> per-segment token lists (the shared expert is segment E) ->
-// tiled prescale of the permuted tokens -> SwiGLU gate/up on tcgen05 -> tiled prescale of h ->
-// down projection on tcgen05 -> slot-order combine (reference: glm_model_q4k_ref.py:663-809).
-static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y, int32_t* sel_out,
-                       void* sel_w_out, cudaStream_t s) {
+// Expert computation of the many-token path on the tensor cores, for given selections: per-segment
+// token lists (local experts of [expert_lo, expert_lo + E); segment E = the shared expert over tokens
+// [shared_t0, shared_t0 + shared_n)) -> tiled prescale of the permuted tokens -> SwiGLU gate/up on
+// tcgen05 -> tiled prescale of h -> down projection on tcgen05. Outputs (in c->pre): y_perm rows by
+// position, pos_of[M * T] (-1: expert not local), shared_pos[shared_n].
+struct TcExperts {
+  uint16_t* y_perm;
+  int32_t* pos_of;
+  int32_t* shared_pos;
+  uint8_t* aux;  // caller scratch after the expert buffers
+};
+static int moe_experts_tc(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, const int32_t* sel,
+                          int64_t expert_lo, int64_t shared_t0, int64_t shared_n, size_t aux_bytes, TcExperts& out,
+                          cudaStream_t s) {
   const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
   const int T = W->topk;
-  const int64_t P = M * T;
   const int nt = 64;  // tokens per tile: about the tokens an expert gets at top-8 of 256
-  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
-  const int64_t Pmax = perm_max_positions(M, T, static_cast<int>(E), shared);
-  const int64_t max_tiles = perm_max_tiles(M, T, static_cast<int>(E), shared, nt);
-  size_t sz[13] = {al256x(2 * M * E), al256x(4 * P),  al256x(2 * P),        al256x(4 * P),   al256x(4 * M),
-                   al256x(4 * Pmax),  al256x(16 * max_tiles), al256x(16),  al256x(xt_bytes(Pmax, H)),
-                   al256x(4 * Pmax),  al256x(2 * Pmax * F), al256x(xt_bytes(Pmax, F)), al256x(2 * Pmax * H)};
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w && shared_n > 0;
+  const int64_t Pmax = M * T + (shared ? shared_n : 0) + 8 * (E + 1);
+  const int64_t max_tiles = (M * T + nt - 1) / nt + E + (shared ? (shared_n + nt - 1) / nt : 0);
+  size_t sz[12] = {al256x(4 * M * T),         al256x(4 * std::max<int64_t>(shared_n, 1)), al256x(4 * Pmax),
+                   al256x(16 * max_tiles),    al256x(16),                                 al256x(xt_bytes(Pmax, H)),
+                   al256x(4 * Pmax),          al256x(2 * Pmax * F),                       al256x(xt_bytes(Pmax, F)),
+                   al256x(2 * Pmax * H),      al256x(4 * Pmax),                           al256x(aux_bytes)};
   size_t total = 0;
   for (size_t v : sz) total += v;
-  total += al256x(4 * Pmax);  // shift of h
-  int rc = grow(&c->pre, &c->pre_bytes, total, "moe_prefill: scratch");
+  int rc = grow(&c->pre, &c->pre_bytes, total, "moe: tensor-core scratch");
   if (rc) return rc;
   uint8_t* b = static_cast<uint8_t*>(c->pre);
-  void* ptr[14];
-  for (int i = 0; i < 13; ++i) {
+  void* ptr[12];
+  for (int i = 0; i < 12; ++i) {
     ptr[i] = b;
     b += sz[i];
   }
-  ptr[13] = b;
-  uint16_t* gate = static_cast<uint16_t*>(ptr[0]);
-  int32_t* sel = static_cast<int32_t*>(ptr[1]);
-  uint16_t* sel_w = static_cast<uint16_t*>(ptr[2]);
-  int32_t* pos_of = static_cast<int32_t*>(ptr[3]);
-  int32_t* shared_pos = static_cast<int32_t*>(ptr[4]);
-  int32_t* perm_tok = static_cast<int32_t*>(ptr[5]);
-  int4* tiles = static_cast<int4*>(ptr[6]);
-  int32_t* counts = static_cast<int32_t*>(ptr[7]);  // [0] tiles, [1] positions
-  uint8_t* xt = static_cast<uint8_t*>(ptr[8]);
-  int* xshift = static_cast<int*>(ptr[9]);
-  uint16_t* h_perm = static_cast<uint16_t*>(ptr[10]);
-  uint8_t* ht = static_cast<uint8_t*>(ptr[11]);
-  uint16_t* y_perm = static_cast<uint16_t*>(ptr[12]);
-  int* hshift = static_cast<int*>(ptr[13]);
+  int32_t* pos_of = static_cast<int32_t*>(ptr[0]);
+  int32_t* shared_pos = static_cast<int32_t*>(ptr[1]);
+  int32_t* perm_tok = static_cast<int32_t*>(ptr[2]);
+  int4* tiles = static_cast<int4*>(ptr[3]);
+  int32_t* counts = static_cast<int32_t*>(ptr[4]);  // [0] tiles, [1] positions
+  uint8_t* xt = static_cast<uint8_t*>(ptr[5]);
+  int* xshift = static_cast<int*>(ptr[6]);
+  uint16_t* h_perm = static_cast<uint16_t*>(ptr[7]);
+  uint8_t* ht = static_cast<uint8_t*>(ptr[8]);
+  uint16_t* y_perm = static_cast<uint16_t*>(ptr[9]);
+  int* hshift = static_cast<int*>(ptr[10]);
+  out.y_perm = y_perm;
+  out.pos_of = pos_of;
+  out.shared_pos = shared_pos;
+  out.aux = static_cast<uint8_t*>(ptr[11]);
 
-  RouterParams rp = {};
-  rp.wt = W->router_wtype;
-  rp.w = static_cast<const uint8_t*>(W->router_w);
-  rp.bias = W->router_bias;
-  rp.x = static_cast<const uint16_t*>(x);
-  rp.M = static_cast<int>(M);
-  rp.K = static_cast<int>(H);
-  rp.E = static_cast<int>(E);
-  rp.topk = T;
-  rp.scale = W->scale;
-  rp.gate = gate;
-  rp.sel = sel;
-  rp.sel_w = sel_w;
-  rp.counters = c->router_counters;
-  rp.status = c->status;
-  if ((rc = router_launch(rp, s, false))) return rc;
   PermParams pp = {};
   pp.sel = sel;
   pp.T = static_cast<int>(M);
   pp.topk = T;
   pp.E = static_cast<int>(E);
   pp.nt = nt;
+  pp.expert_lo = static_cast<int>(expert_lo);
   pp.with_shared = shared ? 1 : 0;
+  pp.shared_t0 = static_cast<int>(shared_t0);
+  pp.shared_n = shared ? static_cast<int>(shared_n) : 0;
   pp.perm_tok = perm_tok;
   pp.pos_of = pos_of;
   pp.shared_pos = shared_pos;
@@ -592,24 +590,61 @@ static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, in
   dn.tile_count = counts;
   dn.y = y_perm;
   dn.status = c->status;
-  if ((rc = tc_gemm_launch(dn, nt, static_cast<int>(E), static_cast<int>(max_tiles), c->num_sms, s, true))) return rc;
-  CombineParams cp = {};
-  cp.M = static_cast<int>(M);
-  cp.H = static_cast<int>(H);
-  cp.topk = T;
-  cp.slot_map = pos_of;
-  cp.sel_w = sel_w;
-  cp.y_union = y_perm;
-  cp.shared_rows = shared ? shared_pos : nullptr;
-  cp.out = static_cast<uint16_t*>(y);
-  cp.rows_are_positions = 1;
-  if ((rc = combine_launch(cp, s, true))) return rc;
-  if (sel_out && (rc = set_cuda_error(cudaMemcpyAsync(sel_out, sel, 4 * P, cudaMemcpyDeviceToDevice, s), "copy sel")))
-    return rc;
-  if (sel_w_out &&
-      (rc = set_cuda_error(cudaMemcpyAsync(sel_w_out, sel_w, 2 * P, cudaMemcpyDeviceToDevice, s), "copy sel_w")))
-    return rc;
-  return OK;
+  return tc_gemm_launch(dn, nt, static_cast<int>(E), static_cast<int>(max_tiles), c->num_sms, s, true);
+}
+
+// Many-token MoE layer on one GPU: router -> moe_experts_tc (all experts, shared over all tokens) ->
+// slot-order combine straight from the position-ordered rows (reference: glm_model_q4k_ref.py:663-809).
+static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y, int32_t* sel_out,
+                       void* sel_w_out, cudaStream_t s) {
+  const int64_t H = W->hidden, E = W->n_experts;
+  const int T = W->topk;
+  const int64_t P = M * T;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
+  // router outputs live in the caller-scratch tail of the tensor-core scratch
+  const size_t aux = al256x(2 * M * E) + al256x(4 * P) + al256x(2 * P);
+  TcExperts te = {};
+  // router outputs in their own context buffer (the expert pass may grow the tensor-core scratch)
+  int rc = grow(&c->rt, &c->rt_bytes, aux, "moe_prefill: router scratch");
+  if (rc) return rc;
+  uint16_t* gate = static_cast<uint16_t*>(c->rt);
+  int32_t* sel = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(gate) + al256x(2 * M * E));
+  uint16_t* sel_w = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(sel) + al256x(4 * P));
+  RouterParams rp = {};
+  rp.wt = W->router_wtype;
+  rp.w = static_cast<const uint8_t*>(W->router_w);
+  rp.bias = W->router_bias;
+  rp.x = static_cast<const uint16_t*>(x);
+  rp.M = static_cast<int>(M);
+  rp.K = static_cast<int>(H);
+  rp.E = static_cast<int>(E);
+  rp.topk = T;
+  rp.scale = W->scale;
+  rp.gate = gate;
+  rp.sel = sel;
+  rp.sel_w = sel_w;
+  rp.counters = c->router_counters;
+  rp.status = c->status;
+  rc = router_launch(rp, s, false);
+  if (!rc) rc = moe_experts_tc(c, W, x, M, sel, 0, 0, shared ? M : 0, 0, te, s);
+  if (!rc) {
+    CombineParams cp = {};
+    cp.M = static_cast<int>(M);
+    cp.H = static_cast<int>(H);
+    cp.topk = T;
+    cp.slot_map = te.pos_of;
+    cp.sel_w = sel_w;
+    cp.y_union = te.y_perm;
+    cp.shared_rows = shared ? te.shared_pos : nullptr;
+    cp.out = static_cast<uint16_t*>(y);
+    cp.rows_are_positions = 1;
+    rc = combine_launch(cp, s, true);
+  }
+  if (!rc && sel_out)
+    rc = set_cuda_error(cudaMemcpyAsync(sel_out, sel, 4 * P, cudaMemcpyDeviceToDevice, s), "copy sel");
+  if (!rc && sel_w_out)
+    rc = set_cuda_error(cudaMemcpyAsync(sel_w_out, sel_w, 2 * P, cudaMemcpyDeviceToDevice, s), "copy sel_w");
+  return rc;
 }
 
 static const int64_t kPrefillMinTokens = 64;
@@ -686,6 +721,65 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
       (rc = set_cuda_error(cudaMemcpyAsync(sel_w_out, sc.sel_w, 2 * M * T, cudaMemcpyDeviceToDevice, s), "copy sel_w")))
     return rc;
   return OK;
+}
+
+// ------------------------------------------------------------------ expert-parallel pieces
+extern "C" int aipu_moe_experts(aipu_ctx* c, const aipu_moe_weights* W, int64_t expert_lo, const void* x, int64_t M,
+                                const int32_t* sel, void* y_slots, int64_t shared_t0, int64_t shared_n,
+                                void* y_shared, void* stream) {
+  if (!c || !W || !x || !sel || !y_slots || M <= 0 || M > 65536 || expert_lo < 0)
+    return set_error(EINVAL_, "moe_experts: bad arguments");
+  const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
+  const int T = W->topk;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w && y_shared && shared_n > 0;
+  if (H % 256 || F % 256 || E <= 0 || E > 1024 || T <= 0 || T > 16 || !W->gate_w || !W->up_w || !W->down_w ||
+      W->gate_wtype != W->up_wtype || W->gate_wtype == AIPU_F32 || W->down_wtype == AIPU_F32 ||
+      (shared && (shared_t0 < 0 || shared_t0 + shared_n > M)))
+    return set_error(EINVAL_, "moe_experts: bad weights descriptor or shared token range");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool strict = (c->flags & AIPU_FLAG_STRICT) != 0;
+  int rc;
+  if (!strict && M >= kPrefillMinTokens && W->gate_wtype == AIPU_Q4_K &&
+      (W->down_wtype == AIPU_Q4_K || W->down_wtype == AIPU_Q6_K) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    TcExperts te = {};
+    rc = moe_experts_tc(c, W, x, M, sel, expert_lo, shared_t0, shared ? shared_n : 0, 0, te, s);
+    if (!rc)
+      rc = gather_slots_launch(te.pos_of, static_cast<int>(M), T, H, te.y_perm, 1, 0,
+                               static_cast<uint16_t*>(y_slots), s);
+    if (!rc && shared)
+      rc = gather_slots_launch(te.shared_pos, static_cast<int>(shared_n), 1, H, te.y_perm, 1, 0,
+                               static_cast<uint16_t*>(y_shared), s);
+    return rc;
+  }
+  if (M > 1024) return set_error(EINVAL_, "moe_experts: more than 1024 tokens need the tensor-core path");
+  MoeScratch sc = {};
+  if ((rc = moe_scratch(c, M, E, T, H, F, sc))) return rc;
+  if ((rc = union_launch(sel, static_cast<int>(M), T, static_cast<int>(expert_lo), static_cast<int>(E), sc.union_ids,
+                         sc.n_union, sc.slot_map, s)))
+    return rc;
+  const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
+  rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F,
+                     static_cast<int>(E), sc.union_ids, sc.n_union, Umax, x, M, sc.h, sc.y, s, false);
+  if (!rc)
+    rc = gather_slots_launch(sc.slot_map, static_cast<int>(M), T, H, sc.y, M, 1, static_cast<uint16_t*>(y_slots), s);
+  if (!rc && shared)
+    rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
+                       H, F, 1, nullptr, nullptr, 1, static_cast<const uint16_t*>(x) + shared_t0 * H, shared_n,
+                       sc.h_sh, static_cast<uint16_t*>(y_shared), s, false);
+  return rc;
+}
+
+extern "C" int aipu_moe_combine(aipu_ctx* c, int64_t M, int64_t H, int topk, const int32_t* sel, const void* sel_w,
+                                int64_t experts_per_piece, const void* pieces, const void* y_shared, void* out,
+                                void* stream) {
+  if (!c || !sel || !sel_w || !pieces || !out || M <= 0 || H <= 0 || H % 8 || topk <= 0 || experts_per_piece <= 0)
+    return set_error(EINVAL_, "moe_combine: bad arguments");
+  DeviceGuard dg(c->device);
+  return combine_pieces_launch(sel, static_cast<const uint16_t*>(sel_w), static_cast<int>(M), topk, H,
+                               static_cast<int>(experts_per_piece), static_cast<const uint16_t*>(pieces),
+                               static_cast<const uint16_t*>(y_shared), static_cast<uint16_t*>(out),
+                               static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt, const void* uw, int dwt,

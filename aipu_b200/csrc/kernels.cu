@@ -1,5 +1,6 @@
 // Exact (bit-for-bit) kernels: dequant, strict sequential GEMM, strict router with sigmoid
 // top-K, and the MoE weighted combine. Each follows the reference golden op for op.
+#include <algorithm>
 #include <cstdio>
 
 
@@ -422,12 +423,13 @@ int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl) {
 }
 
 // ------------------------------------------------------------------ prefill permutation
-// One CTA per segment (expert e < E; segment E = shared expert). Every CTA counts the selections of
-// all experts (shared-memory histogram), takes its segment's start as the padded prefix of the
-// counts, then walks the tokens in order, 256 at a time, and places each token that selected its
-// expert with a block-wide prefix of flags, so the order inside a segment is ascending and the
-// result deterministic. A position is never shared: a token selects an expert at most once.
-// CTA 0 also writes the tile list (segments in order, nt tokens per tile) and the position count.
+// One CTA per segment (local expert e < E; segment E = shared expert over a token range). Every CTA
+// counts the local selections of all experts (shared-memory histogram), takes its segment's start as
+// the padded prefix of the counts, then walks the tokens in order, 256 at a time, and places each
+// token that selected its expert with a block-wide prefix of flags, so the order inside a segment is
+// ascending and the result deterministic. A position is never shared: a token selects an expert at
+// most once. CTA 0 also writes the tile list (segments in order, nt tokens per tile) and the
+// position count; slots whose expert is not local get position -1.
 __global__ void __launch_bounds__(256) perm_kernel(const PermParams p) {
   pdl_wait();
   __shared__ int cnt[1025];
@@ -436,9 +438,12 @@ __global__ void __launch_bounds__(256) perm_kernel(const PermParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int seg = blockIdx.x;
   const int nseg = p.E + (p.with_shared ? 1 : 0);
-  for (int e = tid; e < nseg; e += 256) cnt[e] = (e == p.E) ? p.T : 0;
+  for (int e = tid; e < nseg; e += 256) cnt[e] = (e == p.E) ? p.shared_n : 0;
   __syncthreads();
-  for (int i = tid; i < p.T * p.topk; i += 256) atomicAdd(&cnt[p.sel[i]], 1);
+  for (int i = tid; i < p.T * p.topk; i += 256) {
+    const int le = p.sel[i] - p.expert_lo;
+    if (le >= 0 && le < p.E) atomicAdd(&cnt[le], 1);
+  }
   __syncthreads();
   // start of this segment: sum over earlier segments of the count rounded up to 8
   int part = 0;
@@ -463,16 +468,18 @@ __global__ void __launch_bounds__(256) perm_kernel(const PermParams p) {
     *p.n_tiles = nt;
     *p.n_pos = acc;
   }
+  const bool shared_seg = (seg == p.E);
+  const int t_lo = shared_seg ? p.shared_t0 : 0, t_hi = shared_seg ? p.shared_t0 + p.shared_n : p.T;
   int base = off;
-  for (int t0 = 0; t0 < p.T; t0 += 256) {
+  for (int t0 = t_lo; t0 < t_hi; t0 += 256) {
     const int t = t0 + tid;
     int slot = -1;
-    if (t < p.T) {
-      if (seg == p.E) {
+    if (t < t_hi) {
+      if (shared_seg) {
         slot = p.topk;
       } else {
         for (int s = 0; s < p.topk; ++s)
-          if (p.sel[t * p.topk + s] == seg) slot = s;
+          if (p.sel[t * p.topk + s] - p.expert_lo == seg) slot = s;
       }
     }
     const unsigned m = __ballot_sync(0xffffffffu, slot >= 0);
@@ -487,12 +494,18 @@ __global__ void __launch_bounds__(256) perm_kernel(const PermParams p) {
     if (slot >= 0) {
       const int pos = base + before + __popc(m & ((1u << lane) - 1u));
       p.perm_tok[pos] = t;
-      if (slot == p.topk) p.shared_pos[t] = pos;
+      if (slot == p.topk) p.shared_pos[t - p.shared_t0] = pos;
       else p.pos_of[t * p.topk + slot] = pos;
     }
     base += total;
   }
   for (int pos = base + tid; pos < off + (((base - off) + 7) & ~7); pos += 256) p.perm_tok[pos] = -1;
+  // slots of non-local experts (each written by exactly one CTA: the one of segment 0)
+  if (seg == 0)
+    for (int i = tid; i < p.T * p.topk; i += 256) {
+      const int le = p.sel[i] - p.expert_lo;
+      if (le < 0 || le >= p.E) p.pos_of[i] = -1;
+    }
   pdl_launch_dependents();
 }
 
@@ -501,6 +514,123 @@ int perm_launch(const PermParams& p, cudaStream_t s) {
   PermParams q = p;
   return launch_kernel(reinterpret_cast<const void*>(perm_kernel), dim3(p.E + (p.with_shared ? 1 : 0)), dim3(256), 0,
                        s, true, &q);
+}
+
+// ------------------------------------------------------------------ union of local experts (decode)
+// One CTA: flag the local experts any slot selected, prefix-count them into the sorted union, then
+// map every slot to its union index (-1: expert not local).
+__global__ void __launch_bounds__(1024) union_kernel(const int32_t* __restrict__ sel, int M, int topk, int expert_lo,
+                                                     int E, int32_t* __restrict__ union_ids,
+                                                     int32_t* __restrict__ n_union, int32_t* __restrict__ slot_map) {
+  __shared__ int flag[1024];
+  __shared__ int idx[1024];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += 1024) flag[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < M * topk; i += 1024) {
+    const int le = sel[i] - expert_lo;
+    if (le >= 0 && le < E) flag[le] = 1;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int u = 0;
+    for (int e = 0; e < E; ++e) {
+      idx[e] = flag[e] ? u : -1;
+      if (flag[e]) union_ids[u++] = e;
+    }
+    *n_union = u;
+  }
+  __syncthreads();
+  for (int i = tid; i < M * topk; i += 1024) {
+    const int le = sel[i] - expert_lo;
+    slot_map[i] = (le >= 0 && le < E) ? idx[le] : -1;
+  }
+}
+
+int union_launch(const int32_t* sel, int M, int topk, int expert_lo, int E, int32_t* union_ids, int32_t* n_union,
+                 int32_t* slot_map, cudaStream_t s) {
+  if (E <= 0 || E > 1024) return set_error(EINVAL_, "union: E must be 1..1024");
+  union_kernel<<<1, 1024, 0, s>>>(sel, M, topk, expert_lo, E, union_ids, n_union, slot_map);
+  return set_cuda_error(cudaGetLastError(), "union_kernel");
+}
+
+// ------------------------------------------------------------------ slot gather / EP combine
+__global__ void gather_slots_kernel(const int32_t* __restrict__ index, int M, int topk, int64_t H,
+                                    const uint16_t* __restrict__ rows, int64_t row_mul, int64_t row_add,
+                                    uint16_t* __restrict__ y_slots) {
+  const int64_t hv = H / 8;
+  const int64_t total = static_cast<int64_t>(M) * topk * hv;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t ms = i / hv, v = i - ms * hv;
+    const int m = static_cast<int>(ms / topk);
+    const int ix = index[ms];
+    if (ix < 0) continue;
+    const int64_t r = static_cast<int64_t>(ix) * row_mul + static_cast<int64_t>(m) * row_add;
+    reinterpret_cast<uint4*>(y_slots + ms * H)[v] = __ldg(reinterpret_cast<const uint4*>(rows + r * H) + v);
+  }
+}
+
+int gather_slots_launch(const int32_t* index, int M, int topk, int64_t H, const uint16_t* rows, int64_t row_mul,
+                        int64_t row_add, uint16_t* y_slots, cudaStream_t s) {
+  if (H % 8) return set_error(EINVAL_, "gather_slots: H % 8 != 0");
+  const int64_t total = static_cast<int64_t>(M) * topk * (H / 8);
+  int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  if (blocks <= 0) return OK;
+  gather_slots_kernel<<<blocks, 256, 0, s>>>(index, M, topk, H, rows, row_mul, row_add, y_slots);
+  return set_cuda_error(cudaGetLastError(), "gather_slots_kernel");
+}
+
+__global__ void combine_pieces_kernel(const int32_t* __restrict__ sel, const uint16_t* __restrict__ sel_w, int M,
+                                      int topk, int64_t H, int epp, const uint16_t* __restrict__ pieces,
+                                      const uint16_t* __restrict__ shared, uint16_t* __restrict__ out) {
+  const int64_t hv = H / 8;
+  const int64_t total = static_cast<int64_t>(M) * hv;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / hv);
+    const int64_t v = i - static_cast<int64_t>(m) * hv;
+    float facc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) facc[j] = 0.f;
+    for (int s = 0; s < topk; ++s) {
+      const int e = sel[m * topk + s];
+      const float wv = bf16_bits_to_f32(sel_w[m * topk + s]);
+      const int64_t row = (static_cast<int64_t>(e / epp) * M + m) * topk + s;
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(pieces + row * H) + v);
+      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        facc[2 * j] = __fadd_rn(facc[2 * j], __fmul_rn(wv, bf16_bits_to_f32(w4[j] & 0xFFFFu)));
+        facc[2 * j + 1] = __fadd_rn(facc[2 * j + 1], __fmul_rn(wv, bf16_bits_to_f32(w4[j] >> 16)));
+      }
+    }
+    if (shared) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(shared + static_cast<int64_t>(m) * H) + v);
+      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        facc[2 * j] = __fadd_rn(facc[2 * j], bf16_bits_to_f32(w4[j] & 0xFFFFu));
+        facc[2 * j + 1] = __fadd_rn(facc[2 * j + 1], bf16_bits_to_f32(w4[j] >> 16));
+      }
+    }
+    uint4 o;
+    o.x = bf16_rne_bits(facc[0]) | (static_cast<uint32_t>(bf16_rne_bits(facc[1])) << 16);
+    o.y = bf16_rne_bits(facc[2]) | (static_cast<uint32_t>(bf16_rne_bits(facc[3])) << 16);
+    o.z = bf16_rne_bits(facc[4]) | (static_cast<uint32_t>(bf16_rne_bits(facc[5])) << 16);
+    o.w = bf16_rne_bits(facc[6]) | (static_cast<uint32_t>(bf16_rne_bits(facc[7])) << 16);
+    reinterpret_cast<uint4*>(out + static_cast<int64_t>(m) * H)[v] = o;
+  }
+}
+
+int combine_pieces_launch(const int32_t* sel, const uint16_t* sel_w, int M, int topk, int64_t H, int epp,
+                          const uint16_t* pieces, const uint16_t* shared, uint16_t* out, cudaStream_t s) {
+  if (H % 8 || epp <= 0) return set_error(EINVAL_, "combine_pieces: bad arguments");
+  const int64_t total = static_cast<int64_t>(M) * (H / 8);
+  int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  if (blocks <= 0) return OK;
+  combine_pieces_kernel<<<blocks, 256, 0, s>>>(sel, sel_w, M, topk, H, epp, pieces, shared, out);
+  return set_cuda_error(cudaGetLastError(), "combine_pieces_kernel");
 }
 
 // ------------------------------------------------------------------ activations

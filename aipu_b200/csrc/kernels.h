@@ -44,17 +44,33 @@ struct CombineParams {
 // multiple of 8 positions; the pad positions after a segment hold token -1. Also the position of
 // every (token, slot), the shared-expert position of every token, and the tile list.
 struct PermParams {
-  const int32_t* sel;      // [T, topk]
-  int T, topk, E, nt;      // tokens, slots, experts, tokens per tile
-  int with_shared;         // 1: add segment E with every token
+  const int32_t* sel;      // [T, topk] global expert ids
+  int T, topk, E, nt;      // tokens, slots, local experts, tokens per tile
+  int expert_lo;           // global id of local expert 0: sel - expert_lo outside [0, E) is not local
+  int with_shared;         // 1: add segment E with tokens [shared_t0, shared_t0 + shared_n)
+  int shared_t0, shared_n;
   int32_t* perm_tok;       // [positions] token of each position (-1: pad)
-  int32_t* pos_of;         // [T, topk] position of each (token, slot)
-  int32_t* shared_pos;     // [T] position of each token in the shared segment (with_shared)
+  int32_t* pos_of;         // [T, topk] position of each (token, slot), -1 for a non-local expert
+  int32_t* shared_pos;     // [shared_n] position of each shared-segment token (with_shared)
   int4* tiles;             // (segment, first position, tokens, 0)
   int32_t* n_tiles;        // [1]
   int32_t* n_pos;          // [1] positions used (padded)
 };
 int perm_launch(const PermParams& p, cudaStream_t s);
+
+// Union of the local experts selected by M tokens (sorted) and the index of each (token, slot) in
+// it, -1 when the slot's expert is not local (global id - expert_lo outside [0, E)).
+int union_launch(const int32_t* sel, int M, int topk, int expert_lo, int E, int32_t* union_ids, int32_t* n_union,
+                 int32_t* slot_map, cudaStream_t s);
+// y_slots[m, s, :] = rows[index[m * topk + s]] (bf16 rows of H) for index >= 0; row index
+// r_of(i) = index * row_mul + m * row_add (decode: union-major [U, M, H] rows: row_mul = M, row_add = 1)
+int gather_slots_launch(const int32_t* index, int M, int topk, int64_t H, const uint16_t* rows, int64_t row_mul,
+                        int64_t row_add, uint16_t* y_slots, cudaStream_t s);
+// Expert-parallel combine: out[m] = bf16( sum_s sel_w[m,s] * pieces[owner(sel[m,s])][m, s] + shared[m] )
+// in slot order, owner(e) = e / experts_per_piece; pieces [P, M, topk, H] bf16.
+int combine_pieces_launch(const int32_t* sel, const uint16_t* sel_w, int M, int topk, int64_t H,
+                          int experts_per_piece, const uint16_t* pieces, const uint16_t* shared, uint16_t* out,
+                          cudaStream_t s);
 // upper bound of the positions perm_kernel uses
 inline int64_t perm_max_positions(int64_t T, int topk, int E, int with_shared) {
   return T * topk + (with_shared ? T : 0) + 8 * static_cast<int64_t>(E + 1);

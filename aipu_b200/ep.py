@@ -1,0 +1,111 @@
+"""Expert-parallel MoE layer: the routed experts sharded over the ranks of a process group (one
+process per GPU, NCCL over NVLink), the router and the shared expert replicated.
+
+One layer call on every rank, for that rank's M tokens (the same M on every rank):
+
+  1. route the local tokens (bit-exact router kernel);
+  2. dispatch: all-gather the tokens and their selections (G*M rows);
+  3. each rank runs its experts [r*E/G, (r+1)*E/G) on every gathered token that selected one of them
+     (aipu_moe_experts: the grouped GEMV for few tokens, the tcgen05 path for many) and the shared
+     expert on its own tokens;
+  4. combine: an all-to-all returns to each owner the per-slot expert outputs of its tokens, and the
+     owner combines them in slot order (aipu_moe_combine), the reference's order, so the result is
+     the one-GPU layer's.
+
+The compute steps go through ``backend`` (the CUDA library by default); the communication uses
+torch.distributed, so the same orchestration runs with the gloo backend on CPU in tests, with a
+host backend that restates the compute.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+class CudaBackend:
+    """The library's kernels on the current CUDA device."""
+
+    def __init__(self, ctx: Optional[ops.Context] = None):
+        self.ctx = ctx
+
+    def route(self, W: ops.MoeLayerWeights, x: torch.Tensor):
+        sel, sw, _ = ops.moe_router(W.router_wtype, W.router_w, x, W.n_experts_total, W.topk, bias=W.router_bias,
+                                    scale=W.scale, ctx=self.ctx)
+        return sel, sw
+
+    def experts(self, W_local: ops.MoeLayerWeights, expert_lo: int, x: torch.Tensor, sel: torch.Tensor,
+                shared_range: tuple):
+        return ops.moe_experts(W_local, expert_lo, x, sel, shared_range=shared_range, ctx=self.ctx)
+
+    def combine(self, sel, sel_w, experts_per_piece, pieces, y_shared):
+        return ops.moe_combine(sel, sel_w, experts_per_piece, pieces, y_shared, ctx=self.ctx)
+
+
+@dataclass
+class ShardedMoeWeights:
+    """Routed experts [expert_lo, expert_lo + local.n_experts) of an E-expert layer, plus the
+    replicated router and shared expert (held in ``local``)."""
+    local: ops.MoeLayerWeights
+    expert_lo: int
+    n_experts_total: int
+
+    @property
+    def topk(self):
+        return self.local.topk
+
+    @property
+    def hidden(self):
+        return self.local.hidden
+
+
+def shard(W: ops.MoeLayerWeights, rank: int, world: int) -> ShardedMoeWeights:
+    """Rank ``rank``'s share of a full layer (views of W's expert tensors)."""
+    if W.n_experts % world:
+        raise ValueError("experts must divide evenly over the ranks")
+    n = W.n_experts // world
+    return ShardedMoeWeights(ops.expert_slice(W, rank * n, n), rank * n, W.n_experts)
+
+
+class _RouterView:
+    """The router fields of a sharded layer, with the global expert count."""
+
+    def __init__(self, S: ShardedMoeWeights):
+        L = S.local
+        self.router_wtype, self.router_w, self.router_bias = L.router_wtype, L.router_w, L.router_bias
+        self.n_experts_total, self.topk, self.scale = S.n_experts_total, L.topk, L.scale
+
+
+class ExpertParallelMoE:
+    """The MoE branch of a decoder block with experts sharded over ``group`` (default: WORLD)."""
+
+    def __init__(self, weights: ShardedMoeWeights, group=None, backend=None):
+        self.W = weights
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if weights.n_experts_total != weights.local.n_experts * self.world:
+            raise ValueError("every rank must hold n_experts_total / world experts")
+        self.backend = backend or CudaBackend()
+        self.router = _RouterView(weights)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        W, G, r = self.W, self.world, self.rank
+        M, H = x.shape
+        T = W.topk
+        sel, sw = self.backend.route(self.router, x)
+        # dispatch: every rank sees every token and its selection
+        x_all = torch.empty((G * M, H), dtype=x.dtype, device=x.device)
+        sel_all = torch.empty((G * M, T), dtype=sel.dtype, device=sel.device)
+        dist.all_gather_into_tensor(x_all, x.contiguous(), group=self.group)
+        dist.all_gather_into_tensor(sel_all, sel.contiguous(), group=self.group)
+        # local experts on all tokens, shared expert on this rank's tokens
+        y_slots, y_sh = self.backend.experts(W.local, W.expert_lo, x_all, sel_all, (r * M, M))
+        # combine: rows [q*M, (q+1)*M) of y_slots go back to rank q
+        pieces = torch.empty((G, M, T, H), dtype=y_slots.dtype, device=y_slots.device)
+        dist.all_to_all_single(pieces.view(G * M, T, H), y_slots.contiguous(), group=self.group)
+        return self.backend.combine(sel, sw, W.local.n_experts, pieces, y_sh)

@@ -181,7 +181,7 @@ class MoeLayerWeights:
     n_experts: int
     topk: int
     router_wtype: int
-    router_w: torch.Tensor
+    router_w: Optional[torch.Tensor]
     gate_w: torch.Tensor
     up_w: torch.Tensor
     down_w: torch.Tensor
@@ -197,7 +197,7 @@ class MoeLayerWeights:
         s = L.MoeWeights()
         s.hidden, s.ffn, s.n_experts, s.topk, s.scale = self.hidden, self.ffn, self.n_experts, self.topk, self.scale
         s.router_wtype = self.router_wtype
-        s.router_w = self.router_w.data_ptr()
+        s.router_w = self.router_w.data_ptr() if self.router_w is not None else None
         s.router_bias = self.router_bias.data_ptr() if self.router_bias is not None else None
         s.gate_wtype = s.up_wtype = self.gate_wtype
         s.down_wtype = self.down_wtype
@@ -240,3 +240,52 @@ def swiglu_expert(gate_wtype: int, gate_w: torch.Tensor, up_w: torch.Tensor, dow
     check(lib().aipu_swiglu_expert(ctx.handle, gate_wtype, _ptr(gate_w), gate_wtype, _ptr(up_w), down_wtype,
                                    _ptr(down_w), H, F, _ptr(x), M, _ptr(h), _ptr(y), _stream(x.device)))
     return (y, h) if return_hidden else y
+
+
+def expert_slice(W: MoeLayerWeights, lo: int, n: int) -> MoeLayerWeights:
+    """The weights of routed experts [lo, lo + n) of W (views, no copy), shared expert and router kept."""
+    F_rb = row_bytes(W.gate_wtype, W.hidden)
+    D_rb = row_bytes(W.down_wtype, W.ffn)
+    g = W.gate_w.view(-1)[lo * W.ffn * F_rb:(lo + n) * W.ffn * F_rb]
+    u = W.up_w.view(-1)[lo * W.ffn * F_rb:(lo + n) * W.ffn * F_rb]
+    d = W.down_w.view(-1)[lo * W.hidden * D_rb:(lo + n) * W.hidden * D_rb]
+    return MoeLayerWeights(hidden=W.hidden, ffn=W.ffn, n_experts=n, topk=W.topk, router_wtype=W.router_wtype,
+                           router_w=W.router_w, gate_w=g, up_w=u, down_w=d, gate_wtype=W.gate_wtype,
+                           down_wtype=W.down_wtype, router_bias=W.router_bias, shared_gate_w=W.shared_gate_w,
+                           shared_up_w=W.shared_up_w, shared_down_w=W.shared_down_w, scale=W.scale)
+
+
+def moe_experts(W_local: MoeLayerWeights, expert_lo: int, x: torch.Tensor, sel: torch.Tensor,
+                y_slots: Optional[torch.Tensor] = None, shared_range: Optional[tuple] = None,
+                ctx: Optional[Context] = None):
+    """Expert computation of one expert-parallel rank: y_slots[m, s] for the slots whose expert is in
+    [expert_lo, expert_lo + W_local.n_experts), and the shared expert of tokens shared_range=(t0, n).
+    Returns (y_slots [M, topk, H], y_shared [n, H] or None)."""
+    _need_cuda(x, sel, y_slots)
+    if x.dtype != torch.bfloat16 or sel.dtype != torch.int32:
+        raise ValueError("moe_experts: x must be bf16 and sel int32")
+    M = x.shape[0]
+    ctx = ctx or Context.default(x.device)
+    if y_slots is None:
+        y_slots = torch.empty((M, W_local.topk, W_local.hidden), dtype=torch.bfloat16, device=x.device)
+    t0, n = shared_range if shared_range is not None else (0, 0)
+    y_sh = torch.empty((n, W_local.hidden), dtype=torch.bfloat16, device=x.device) if n > 0 else None
+    cs = W_local.cstruct()
+    check(lib().aipu_moe_experts(ctx.handle, ctypes.byref(cs), expert_lo, _ptr(x), M, _ptr(sel), _ptr(y_slots), t0, n,
+                                 _ptr(y_sh), _stream(x.device)))
+    return y_slots, y_sh
+
+
+def moe_combine(sel: torch.Tensor, sel_w: torch.Tensor, experts_per_piece: int, pieces: torch.Tensor,
+                y_shared: Optional[torch.Tensor] = None, ctx: Optional[Context] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[m] = bf16( sum_s sel_w[m, s] * pieces[sel[m, s] // experts_per_piece][m, s] + y_shared[m] ),
+    slot order; pieces [P, M, topk, H] bf16."""
+    _need_cuda(sel, sel_w, pieces, y_shared, out)
+    P, M, T, H = pieces.shape
+    ctx = ctx or Context.default(pieces.device)
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=pieces.device)
+    check(lib().aipu_moe_combine(ctx.handle, M, H, T, _ptr(sel), _ptr(sel_w), experts_per_piece, _ptr(pieces),
+                                 _ptr(y_shared), _ptr(out), _stream(pieces.device)))
+    return out

@@ -182,6 +182,24 @@ int aipu_swiglu_expert(aipu_ctx* ctx, int gate_wtype, const void* gate_w, int up
                        int down_wtype, const void* down_w, int64_t H, int64_t F, const void* x, int64_t M, void* h,
                        void* y, void* stream);
 
+/* Expert-parallel pieces. A rank holds the routed experts [expert_lo, expert_lo + W->n_experts)
+ * (W's gate/up/down point at them, back to back) and the replicated shared expert; router fields of
+ * W are unused. For tokens x[M, H] (bf16) and their global selections sel[M, topk]:
+ *   aipu_moe_experts: y_slots[m, s, :] = SwiGLU expert sel[m, s] of x[m] for every slot whose expert
+ *     is local (other slots are left untouched); y_shared[i, :] = shared expert of token
+ *     shared_t0 + i for i < shared_n (y_shared may be NULL). Many tokens use the tensor cores,
+ *     AIPU_FLAG_STRICT the bit-exact chains.
+ *   aipu_moe_combine: out[m] = bf16( sum_s sel_w[m, s] * pieces[sel[m, s] / experts_per_piece][m, s]
+ *     + y_shared[m] ) in slot order, pieces [P, M, topk, H] bf16 (the y_slots of every rank, as an
+ *     all-to-all returns them) -- the reference's combine order, so the layer equals the one-GPU one.
+ * No counterpart function in the reference (its MoE runs on one device): the pieces are the
+ * decoder-block MoE branch of tools/glm_model_q4k_ref.py:797-809 split at the expert loop. */
+int aipu_moe_experts(aipu_ctx* ctx, const aipu_moe_weights* w_local, int64_t expert_lo, const void* x, int64_t M,
+                     const int32_t* sel, void* y_slots, int64_t shared_t0, int64_t shared_n, void* y_shared,
+                     void* stream);
+int aipu_moe_combine(aipu_ctx* ctx, int64_t M, int64_t H, int topk, const int32_t* sel, const void* sel_w,
+                     int64_t experts_per_piece, const void* pieces, const void* y_shared, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
