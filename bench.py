@@ -308,6 +308,80 @@ def moe_prefill(W, M=2048, reps=10):
             "peak_source": kind, "flops": flops}
 
 
+def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
+    """BASELINE config 3/5 decode layer with the 256 routed experts sharded over the N ranks
+    (256/N per GPU, NCCL all-gather dispatch and all-to-all return); every rank decodes M tokens.
+    tokens/s = N * M / (max-over-ranks device time per layer)."""
+    import torch
+    import torch.distributed as dist
+
+    from aipu_b200 import ep
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    H, Fd, E, T = 6144, 2048, 256, 8
+    n = E // world
+    g = torch.Generator(device=d)
+    local = ops.MoeLayerWeights(
+        hidden=H, ffn=Fd, n_experts=n, topk=T, router_wtype=F.F32,
+        router_w=torch.randn((H, E), device=d, generator=g.manual_seed(1)) * 0.02,
+        router_bias=torch.randn((E,), device=d, generator=g.manual_seed(2)) * 0.01,
+        gate_w=F.random_rows_dev(F.Q4_K, n * Fd, H, seed=11 + 100 * rank, device=d),
+        up_w=F.random_rows_dev(F.Q4_K, n * Fd, H, seed=12 + 100 * rank, device=d),
+        down_w=F.random_rows_dev(F.Q6_K, n * H, Fd, seed=13 + 100 * rank, device=d),
+        shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=14, device=d),
+        shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=15, device=d),
+        shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
+    layer = ep.ExpertParallelMoE(ep.ShardedMoeWeights(local, rank * n, E), backend=ep.CudaBackend(ops.Context(d)))
+    expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
+    out = {}
+    for M in M_list:
+        x = torch.randn((M, H), device=d, generator=g.manual_seed(100 + M + 7 * rank)).to(torch.bfloat16)
+        for _ in range(5):
+            layer(x)
+        torch.cuda.synchronize()
+        # one layer (router, NCCL dispatch, experts, NCCL return, combine) as a CUDA graph
+        run, graphed = (lambda: layer(x)), False
+        try:
+            gr = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                layer(x)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(gr, stream=s):
+                    layer(x)
+            torch.cuda.synchronize()
+            run, graphed = gr.replay, True
+        except Exception:  # capture unsupported here: time eager calls
+            torch.cuda.synchronize()
+        for _ in range(5):
+            run()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps / 1e3], device=d, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = float(t.item())
+        # experts this rank touched in one layer (union of its local experts over all N*M tokens)
+        sel_all = torch.empty((world * M, T), dtype=torch.int32, device=d)
+        sel, _, _ = ops.moe_router(F.F32, local.router_w, x, E, T, bias=local.router_bias)
+        dist.all_gather_into_tensor(sel_all, sel)
+        touched = len(set(v for v in sel_all.cpu().numpy().reshape(-1).tolist() if rank * n <= v < (rank + 1) * n))
+        byts = H * E * 4 + (touched + 1) * expert_bytes
+        out[f"M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(world * M / t, 1),
+                        "tokens_per_rank": M, "experts_per_gpu": n, "rank0_touched_experts": touched,
+                        "cuda_graph": graphed,
+                        "rank0_hbm_gbs": round(byts / t / 1e9, 1)}
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -416,6 +490,9 @@ def main():
     moe = None
     if rank == 0 and world == 1 and not args.no_moe:
         moe = moe_decode()
+    moe_ep = None
+    if world > 1 and not args.no_moe:
+        moe_ep = moe_decode_ep(world, rank)
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu_base = cpu_baseline_gemv()
@@ -435,7 +512,7 @@ def main():
                          "us_per_launch": round(step * 1e6, 3)},
             "single_launch": single,
             "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,
-            "clocks": clk.summary(), "moe_decode": moe,
+            "clocks": clk.summary(), "moe_decode": moe, "moe_decode_ep": moe_ep,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
