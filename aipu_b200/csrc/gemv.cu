@@ -10,7 +10,8 @@ namespace aipu {
 
 // ------------------------------------------------------------------ shared-memory layout
 // [mbarriers: NW x S][misc: prescale shifts per (group slot, column)][activations: XG x ncols fp16
-// columns][Q4_K sub-block sums][per-warp rings: NW x S slots x 16 rows x pitch]
+// columns][Q4_K sub-block sums: per (column, super-block) 64 bytes = fp16 hi[8], lo[8], lo2[8], pad]
+// [per-warp rings: NW x S slots x 16 rows x pitch]
 struct GemvLayout {
   int off_misc, off_xs, off_sxs, off_ring, total;
 };
@@ -21,7 +22,7 @@ __host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int 
   L.off_misc = GEMV_MAXW * GEMV_MAXS * 8;
   L.off_xs = L.off_misc + 256;
   L.off_sxs = L.off_xs + xg * ncols * xpitch;
-  const int sx = (wt == WT_Q4K) ? xg * ncols * (K / 256) * 32 : 0;
+  const int sx = (wt == WT_Q4K) ? xg * ncols * (K / 256) * 64 : 0;
   L.off_ring = (L.off_sxs + sx + 127) & ~127;
   L.total = L.off_ring + nw * nslots * 16 * pitch;
   return L;
@@ -59,12 +60,22 @@ __device__ __forceinline__ uint32_t imad_u32(uint32_t a, uint32_t b, uint32_t c)
   return d;
 }
 
+// Q4_K unit (16 rows x one super-block). Each code becomes an fp16 MMA operand 1024 + f q in the
+// upper mantissa bits, so the 1024 offset costs little precision: low nibbles by a mask and an integer
+// multiply-add (f = 64), high nibbles by one LOP3 on the nibble in place at bits 4-7 (f = 16); PRMT
+// moves bytes 1 and 3 down for the other half of the k positions. No scale multiply per code: every
+// MMA covers one 32-weight sub-block of every row, so D_j = sum_k x_k (1024 + f_j q_k) and
+//   sum_k x_k sc_j q_k = (sc_j / f_j) (D_j - 1024 S_j),
+// accumulated in fp32 with the row's 6-bit scale. The offsets 1024 sum_j (sc_j / f_j) S_j come from
+// MMAs of A = sc_j / f_j against the sub-block sums S_j held as three fp16 parts (33 bits), the min
+// term Cm = sum_j m_j S_j from one more MMA (two parts). acc += d * P - dmin * Cm.
+__device__ __forceinline__ float half_lo_f(uint32_t h2) { return __half2float(__ushort_as_half(h2 & 0xFFFFu)); }
+__device__ __forceinline__ float half_hi_f(uint32_t h2) { return __half2float(__ushort_as_half(h2 >> 16)); }
+
 __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol,
-                                         const uint32_t* sxcol, bool colok, int sb, int t, float (&acc)[4]) {
+                                         const uint32_t* sxcol, int sb, int t, float (&acc)[4]) {
   const uint4 hg = *reinterpret_cast<const uint4*>(rg);
   const uint4 h8 = *reinterpret_cast<const uint4*>(rg8);
-  const float dg = f16_bits_to_f32(hg.x), dmg = f16_bits_to_f32(hg.x >> 16);
-  const float d8 = f16_bits_to_f32(h8.x), dm8 = f16_bits_to_f32(h8.x >> 16);
   // 8 six-bit scales / mins per row, as packed bytes (get_scale_min_k4 for j = 0..7 at once)
   const uint32_t sc03g = hg.y & 0x3F3F3F3Fu, m03g = hg.z & 0x3F3F3F3Fu;
   const uint32_t sc47g = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
@@ -72,63 +83,72 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
   const uint32_t sc038 = h8.y & 0x3F3F3F3Fu, m038 = h8.z & 0x3F3F3F3Fu;
   const uint32_t sc478 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
   const uint32_t m478 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+  // fp16 (sc_2p / 64, sc_2p+1 / 16) pairs of both rows for the 4 groups p: 1024 + sc via PRMT, - 1024,
+  // * (1/64, 1/16)
+  const uint32_t h2_1_16 = 0x2C002400u;  // (1/64, 1/16)
+  uint32_t sg[4], s8[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t sel = (p & 1) ? 0x4342u : 0x4140u;
+    sg[p] = hmul2_u32(hsub2_u32(prmt((p < 2) ? sc03g : sc47g, 0x64u, sel), H2_1024), h2_1_16);
+    s8[p] = hmul2_u32(hsub2_u32(prmt((p < 2) ? sc038 : sc478, 0x64u, sel), H2_1024), h2_1_16);
+  }
 
-  float Plo[2][4] = {}, Phi[2][4] = {};  // two independent chains each for low / high nibbles
+  float P[4] = {0.f, 0.f, 0.f, 0.f};
   const uint8_t* xb = xcol + 2 * (sb * 256 + 8 * t);
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const uint32_t wg = (p < 2) ? sc03g : sc47g;
-    const uint32_t w8 = (p < 2) ? sc038 : sc478;
-    const int sl = 8 * ((2 * p) & 3), shh = 8 * ((2 * p + 1) & 3);
-    const uint32_t slg = (wg >> sl) & 0xFFu, shg = (wg >> shh) & 0xFFu;
-    const uint32_t sl8 = (w8 >> sl) & 0xFFu, sh8 = (w8 >> shh) & 0xFFu;
     const uint2 qg = *reinterpret_cast<const uint2*>(rg + 16 + 32 * p + 8 * t);
     const uint2 q8 = *reinterpret_cast<const uint2*>(rg8 + 16 + 32 * p + 8 * t);
-    uint4 xl = make_uint4(0, 0, 0, 0), xh = make_uint4(0, 0, 0, 0);
-    if (colok) {
-      xl = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p));
-      xh = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p + 32));
-    }
+    const uint4 xl = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p));
+    const uint4 xh = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p + 32));
+    float Dlo[4] = {0.f, 0.f, 0.f, 0.f}, Dhi[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const uint32_t w = j ? qg.y : qg.x, v = j ? q8.y : q8.x;
-      const uint32_t ws = w >> 8, vs = v >> 8;
+      const uint32_t ws = prmt(w, 0u, 0x4341u), vs = prmt(v, 0u, 0x4341u);  // bytes 1, 3 -> low bytes
       uint32_t a[4];
-      a[0] = imad_u32(w & 0x000F000Fu, slg, 0x64006400u);
-      a[1] = imad_u32(v & 0x000F000Fu, sl8, 0x64006400u);
-      a[2] = imad_u32(ws & 0x000F000Fu, slg, 0x64006400u);
-      a[3] = imad_u32(vs & 0x000F000Fu, sl8, 0x64006400u);
-      mma_f16_16816(Plo[p & 1], a, j ? xl.z : xl.x, j ? xl.w : xl.y);
-      a[0] = imad_u32((w >> 4) & 0x000F000Fu, shg, 0x64006400u);
-      a[1] = imad_u32((v >> 4) & 0x000F000Fu, sh8, 0x64006400u);
-      a[2] = imad_u32((w >> 12) & 0x000F000Fu, shg, 0x64006400u);
-      a[3] = imad_u32((v >> 12) & 0x000F000Fu, sh8, 0x64006400u);
-      mma_f16_16816(Phi[p & 1], a, j ? xh.z : xh.x, j ? xh.w : xh.y);
+      a[0] = imad_u32(w & 0x000F000Fu, 64u, H2_1024);
+      a[1] = imad_u32(v & 0x000F000Fu, 64u, H2_1024);
+      a[2] = imad_u32(ws & 0x000F000Fu, 64u, H2_1024);
+      a[3] = imad_u32(vs & 0x000F000Fu, 64u, H2_1024);
+      mma_f16_16816(Dlo, a, j ? xl.z : xl.x, j ? xl.w : xl.y);
+      a[0] = lop3_and_or(w, 0x00F000F0u, H2_1024);
+      a[1] = lop3_and_or(v, 0x00F000F0u, H2_1024);
+      a[2] = lop3_and_or(ws, 0x00F000F0u, H2_1024);
+      a[3] = lop3_and_or(vs, 0x00F000F0u, H2_1024);
+      mma_f16_16816(Dhi, a, j ? xh.z : xh.x, j ? xh.w : xh.y);
     }
+    const float slg = half_lo_f(sg[p]), shg = half_hi_f(sg[p]);
+    const float sl8 = half_lo_f(s8[p]), sh8 = half_hi_f(s8[p]);
+    P[0] = fmaf(shg, Dhi[0], fmaf(slg, Dlo[0], P[0]));
+    P[1] = fmaf(shg, Dhi[1], fmaf(slg, Dlo[1], P[1]));
+    P[2] = fmaf(sh8, Dhi[2], fmaf(sl8, Dlo[2], P[2]));
+    P[3] = fmaf(sh8, Dhi[3], fmaf(sl8, Dlo[3], P[3]));
   }
-  // min term Cm[row, col] = sum_j m_j * S_j[col], and the super-block sum S[col] = sum_j S_j[col]
+  // offsets Cs = sum_j (sc_j / f_j) S_j and the min term Cm = sum_j m_j S_j (k positions of this
+  // lane: sub-blocks 2t', 2t'+1 of the hi sums (b0) and of the lo sums (b1), t' = t & 3)
   float Cm[4] = {0.f, 0.f, 0.f, 0.f}, Cs[4] = {0.f, 0.f, 0.f, 0.f};
   {
     const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
     const uint32_t mg = hsub2_u32(prmt((t < 2) ? m03g : m47g, 0x64u, sel), H2_1024);
     const uint32_t m8 = hsub2_u32(prmt((t < 2) ? m038 : m478, 0x64u, sel), H2_1024);
-    uint32_t a[4] = {mg, m8, mg, m8};
-    uint32_t b0 = 0, b1 = 0;
-    if (colok) {
-      b0 = sxcol[sb * 8 + t];
-      b1 = sxcol[sb * 8 + 4 + t];
-    }
-    mma_f16_16816(Cm, a, b0, b1);
-    const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
-    mma_f16_16816(Cs, ones, b0, b1);
+    const uint32_t b0 = sxcol[sb * 16 + t], b1 = sxcol[sb * 16 + 4 + t], b2 = sxcol[sb * 16 + 8 + t];
+    const uint32_t am[4] = {mg, m8, mg, m8};
+    mma_f16_16816(Cm, am, b0, b1);
+    const uint32_t sgt = (t & 2) ? ((t & 1) ? sg[3] : sg[2]) : ((t & 1) ? sg[1] : sg[0]);
+    const uint32_t s8t = (t & 2) ? ((t & 1) ? s8[3] : s8[2]) : ((t & 1) ? s8[1] : s8[0]);
+    const uint32_t as[4] = {sgt, s8t, sgt, s8t};
+    mma_f16_16816(Cs, as, b0, b1);
+    mma_f16_16816(Cs, as, b2, 0u);  // third parts of the sums (k positions 8.. of A multiply zero)
   }
+  const float dg = f16_bits_to_f32(hg.x), dmg = f16_bits_to_f32(hg.x >> 16);
+  const float d8 = f16_bits_to_f32(h8.x), dm8 = f16_bits_to_f32(h8.x >> 16);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float lo = __fadd_rn(Plo[0][i], Plo[1][i]);
-    const float hi = __fadd_rn(Phi[0][i], Phi[1][i]);
-    const float P = fmaf(-1024.f, Cs[i], __fadd_rn(lo, hi));  // sum_k x_k * sc * q
+    const float Pi = fmaf(-1024.f, Cs[i], P[i]);  // sum_k x_k * sc * q
     const float d = (i < 2) ? dg : d8, dm = (i < 2) ? dmg : dm8;
-    acc[i] = fmaf(-dm, Cm[i], fmaf(d, P, acc[i]));
+    acc[i] = fmaf(-dm, Cm[i], fmaf(d, Pi, acc[i]));
   }
 }
 
@@ -372,7 +392,7 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
   int* misc = reinterpret_cast<int*>(smem + L.off_misc) + xs_slot * 8;
   uint8_t* xs = smem + L.off_xs + xs_slot * ncols * p.xpitch;
   const int K = p.K, M = p.M, nv = K / VEC, nsb = K / 256;
-  uint8_t* sxs = smem + L.off_sxs + xs_slot * ncols * nsb * 32;
+  uint8_t* sxs = smem + L.off_sxs + xs_slot * ncols * nsb * 64;
   const uint4* xv = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
                                                    static_cast<int64_t>(grp) * p.x_group_stride * (XT == XT_F32 ? 4 : 2));
   const bool one_pass = nv <= VPT * NT;
@@ -442,17 +462,24 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
             }
             if (v < nv && (v % LPS) == 0) {
               const int sub = v / LPS;
+              // the fp32 sum as three fp16 parts (33 significant bits)
               const __half hh = __float2half_rn(shi);
-              const __half hl = __float2half_rn(__fsub_rn(shi, __half2float(hh)));
-              __half* dst = reinterpret_cast<__half*>(sxs + (chi * nsb + sub / 8) * 32);
+              const float r1 = __fsub_rn(shi, __half2float(hh));
+              const __half hl = __float2half_rn(r1);
+              const __half hl2 = __float2half_rn(__fsub_rn(r1, __half2float(hl)));
+              __half* dst = reinterpret_cast<__half*>(sxs + (chi * nsb + sub / 8) * 64);
               dst[sub & 7] = hh;
               dst[8 + (sub & 7)] = hl;
+              dst[16 + (sub & 7)] = hl2;
               if (XT == XT_F32) {
                 const __half lh = __float2half_rn(slo);
-                const __half ll = __float2half_rn(__fsub_rn(slo, __half2float(lh)));
-                __half* d2 = reinterpret_cast<__half*>(sxs + ((chi + 1) * nsb + sub / 8) * 32);
+                const float q1 = __fsub_rn(slo, __half2float(lh));
+                const __half ll = __float2half_rn(q1);
+                const __half ll2 = __float2half_rn(__fsub_rn(q1, __half2float(ll)));
+                __half* d2 = reinterpret_cast<__half*>(sxs + ((chi + 1) * nsb + sub / 8) * 64);
                 d2[sub & 7] = lh;
                 d2[8 + (sub & 7)] = ll;
+                d2[16 + (sub & 7)] = ll2;
               }
             }
           }
@@ -608,6 +635,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
   // ------------------------------------------------------------------ per-warp main loop
   const int g = lane >> 2, t = lane & 3;
   const bool colok = g < ncols;
+  const int gx = colok ? g : 0;  // lanes of dead columns read column 0 (their results are never stored)
   const int* misc0 = reinterpret_cast<const int*>(smem + L.off_misc);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
@@ -630,12 +658,12 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     }
     const uint8_t* rg = st + g * p.pitch + hg;
     const uint8_t* r8 = st + (g + 8) * p.pitch + h8;
-    const uint8_t* xcol = smem + L.off_xs + (xsl * ncols + g) * p.xpitch;
+    const uint8_t* xcol = smem + L.off_xs + (xsl * ncols + gx) * p.xpitch;
     for (int i = 0; i < ch.n; ++i) {
       const int sb = ch.sb + i;
       if (WT == WT_Q4K) {
-        const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + (xsl * ncols + g) * nsb * 32);
-        unit_q4k(rg + i * UB, r8 + i * UB, xcol, sxcol, colok, sb, t, acc);
+        const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
+        unit_q4k(rg + i * UB, r8 + i * UB, xcol, sxcol, sb, t, acc);
       } else if (WT == WT_Q6K) {
         unit_q6k(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
       } else if (WT == WT_Q80) {
