@@ -144,6 +144,7 @@ __device__ void router_topk_token(const RouterParams& p, int m) {
   constexpr int MAXPL = 32;  // E <= 1024
   unsigned long long key[MAXPL];
   const int per = (E + 31) / 32;
+#pragma unroll
   for (int j = 0; j < MAXPL; ++j) {
     key[j] = 0ull;
     const int e = j * 32 + lane;
@@ -157,10 +158,12 @@ __device__ void router_topk_token(const RouterParams& p, int m) {
   int sel[16];
   for (int s = 0; s < T; ++s) {
     unsigned long long best = 0ull;
-    for (int j = 0; j < per; ++j) best = key[j] > best ? key[j] : best;
+#pragma unroll
+    for (int j = 0; j < MAXPL; ++j) best = key[j] > best ? key[j] : best;
     best = warp_max_u64(best);
     const int e = 0x7FFFFFFF - static_cast<int>(best & 0xFFFFFFFFull);
-    for (int j = 0; j < per; ++j)
+#pragma unroll
+    for (int j = 0; j < MAXPL; ++j)
       if (key[j] == best) key[j] = 0ull;
     sel[s] = e;
     win[s] = bf16_bits_to_f32(__ldcg(p.gate + static_cast<int64_t>(m) * E + e));
@@ -226,19 +229,40 @@ __device__ void router_union(const RouterParams& p) {
 // activation slices) into a shared-memory ring with 1-D bulk copies, so the chains never wait on
 // DRAM latency. GGUF-row routers dequantise each weight exactly in the chain.
 constexpr int RT_CHUNK = 128;   // k rows per stage
-constexpr int RT_NST = 6;       // ring depth
+// experts per CTA: 8 for few tokens (lanes 0..7 run the chains, four times the CTAs stream the
+// router), 32 for many tokens (every lane runs a chain)
 constexpr int RT_MB = 8;        // tokens per CTA
-constexpr int RT_WBYTES = RT_CHUNK * 32 * 4;
+template <int EG>
+struct RtCfg {
+  static constexpr int NST = (EG == 8) ? 16 : 6;  // ring depth
+  static constexpr int WBYTES = RT_CHUNK * EG * 4;
+};
 constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
 
+#ifdef RT_TRACE
+__device__ long long g_rt_trace[4];
+extern "C" int aipu_debug_rt_trace(long long* out) {
+  cudaMemcpyFromSymbol(out, g_rt_trace, sizeof(g_rt_trace));
+  static const long long z[4] = {};
+  cudaMemcpyToSymbol(g_rt_trace, z, sizeof(z));
+  return 0;
+}
+#endif
+template <int RT_EG>
 __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const __grid_constant__ RouterParams p) {
+  constexpr int RT_NST = RtCfg<RT_EG>::NST;
+  constexpr int RT_WBYTES = RtCfg<RT_EG>::WBYTES;
+#ifdef RT_TRACE
+  const long long t_start = clock64();
+#endif
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + RT_NST;
-  uint8_t* ring = smem + 128;
+  uint8_t* ring = smem + 256;  // barriers first (2 x RT_NST <= 32 of them); TMA destinations 128-byte aligned
   __shared__ int last_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.x * 32, e = e0 + lane;
+  const int e0 = blockIdx.x * RT_EG, e = e0 + lane;
+  const bool live = (lane < RT_EG) && (e < p.E);
   const int m0 = blockIdx.y * RT_MB;
   const int mb = min(RT_MB, p.M - m0);
   const int K = p.K, E = p.E;
@@ -291,29 +315,71 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const _
       for (int c = 0; c < nchunk; ++c) {
         const int slot = c % RT_NST;
         const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
+#ifdef RT_TRACE
+        const long long tw0 = clock64();
+#endif
         if (ok) ok = mbar_wait_bounded(&full[slot], (c / RT_NST) & 1, p.status, ST_TIMEOUT_FULL);
+#ifdef RT_TRACE
+        if (lane == 0 && blockIdx.x == 0 && blockIdx.y == 0 && warp == 0) g_rt_trace[0] += clock64() - tw0;
+#endif
         if (ok) {
           const uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
           const float* ws = reinterpret_cast<const float*>(st);
           const uint16_t* xs = reinterpret_cast<const uint16_t*>(st + RT_WBYTES + warp * RT_CHUNK * 2);
-#pragma unroll 8
-          for (int k = 0; k < kl; ++k) acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(xs[k]), ws[k * 32 + lane]));
+          if (kl == RT_CHUNK) {
+            // batches of 32 k, the operands of the next batch loaded while the dependent adds of
+            // this batch run in k order (the chain runs near the add latency)
+            const int pe = lane & (RT_EG - 1);
+            float wv[32];
+            uint4 xv[4];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) wv[i] = ws[i * RT_EG + pe];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = reinterpret_cast<const uint4*>(xs)[i];
+#pragma unroll
+            for (int k0b = 0; k0b < RT_CHUNK; k0b += 32) {
+              float pr[32];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  pr[8 * i + 2 * h] = __fmul_rn(__uint_as_float(xw[h] << 16), wv[8 * i + 2 * h]);
+                  pr[8 * i + 2 * h + 1] = __fmul_rn(__uint_as_float(xw[h] & 0xFFFF0000u), wv[8 * i + 2 * h + 1]);
+                }
+              }
+              if (k0b + 32 < RT_CHUNK) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) wv[i] = ws[(k0b + 32 + i) * RT_EG + pe];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) xv[i] = reinterpret_cast<const uint4*>(xs + k0b + 32)[i];
+              }
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc = __fadd_rn(acc, pr[i]);
+            }
+          } else {
+            for (int k = 0; k < kl; ++k)
+              acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(xs[k]), ws[k * RT_EG + (lane & (RT_EG - 1))]));
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
       }
-    } else if (e < E) {
+    } else if (live) {
       const uint8_t* row = p.w + static_cast<int64_t>(e) * row_bytes_of(p.wt, K);
       const int64_t xo = static_cast<int64_t>(m) * K;
       for (int k = 0; k < K; ++k)
         acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(__ldg(p.x + xo + k)), deq_one(p.wt, row, k)));
     }
-    if (e < E) {
+    if (live) {
       const float logit = bf16_round_f(acc);
       p.gate[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(glm_sigmoid_bf(logit));
       if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
     }
   }
+#ifdef RT_TRACE
+  if (lane == 0 && blockIdx.x == 0 && blockIdx.y == 0 && warp == 0) g_rt_trace[1] += clock64() - t_start;
+#endif
   // the last CTA of this token block selects top-K for its tokens; the last block builds the union
   named_bar_sync(1, 32 * RT_MB);
   if (threadIdx.x == 0) {
@@ -339,16 +405,14 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const _
   }
 }
 
-int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
-  if (p.E <= 0 || p.E > 1024 || p.topk <= 0 || p.topk > 16 || p.topk > p.E || p.M <= 0)
-    return set_error(EINVAL_, "router: need 1 <= topk <= min(16, E), E <= 1024");
-  if (p.wt == WT_F32 && (p.E % 4 != 0 || (reinterpret_cast<uintptr_t>(p.w) & 15u) ||
-                         (reinterpret_cast<uintptr_t>(p.x) & 15u) || (p.K % 8)))
-    return set_error(EINVAL_, "router: fp32 router needs E % 4 == 0, K % 8 == 0 and 16-byte aligned w, x");
+template <int EG>
+static int router_launch_eg(const RouterParams& p, cudaStream_t s, bool pdl) {
+  constexpr int NST = RtCfg<EG>::NST;
+  static_assert(2 * NST * 8 <= 256, "router barriers fit before the ring");
+  const int smem = 256 + NST * (RtCfg<EG>::WBYTES + RT_XBYTES);
   static bool attr = false;
-  const int smem = 128 + RT_NST * (RT_WBYTES + RT_XBYTES);
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(router_strict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(router_strict_kernel<EG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(router)");
     attr = true;
   }
@@ -356,12 +420,22 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
   if (p.wt == WT_F32) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.K)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.E) * 4};
-    const cuuint32_t box[2] = {32, RT_CHUNK};
+    const cuuint32_t box[2] = {EG, RT_CHUNK};
     const int rc = encode_tiled(&q.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.w, dims, strides, box);
     if (rc) return rc;
   }
-  return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel), dim3((p.E + 31) / 32, (p.M + RT_MB - 1) / RT_MB),
-                       dim3(32 * (RT_MB + 1)), smem, s, pdl, &q);
+  return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel<EG>),
+                       dim3((p.E + EG - 1) / EG, (p.M + RT_MB - 1) / RT_MB), dim3(32 * (RT_MB + 1)), smem, s, pdl, &q);
+}
+
+int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
+  if (p.E <= 0 || p.E > 1024 || p.topk <= 0 || p.topk > 16 || p.topk > p.E || p.M <= 0)
+    return set_error(EINVAL_, "router: need 1 <= topk <= min(16, E), E <= 1024");
+  if (p.wt == WT_F32 && (p.E % 4 != 0 || (reinterpret_cast<uintptr_t>(p.w) & 15u) ||
+                         (reinterpret_cast<uintptr_t>(p.x) & 15u) || (p.K % 8)))
+    return set_error(EINVAL_, "router: fp32 router needs E % 4 == 0, K % 8 == 0 and 16-byte aligned w, x");
+  // few token blocks: spread the router over more SMs; many: every lane of a CTA runs a chain
+  return (p.M <= 4 * RT_MB) ? router_launch_eg<8>(p, s, pdl) : router_launch_eg<32>(p, s, pdl);
 }
 
 // ------------------------------------------------------------------ combine
