@@ -71,6 +71,10 @@ SIGNATURES = {
                                  c_int64, c_int64, c_void_p, c_void_p]),
     "aipu_moe_combine": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_void_p]),
+    "aipu_ep_create": (c_int, [c_void_p, c_int, c_int, c_int64, c_int64, c_int, ctypes.POINTER(c_void_p), c_void_p]),
+    "aipu_ep_connect": (c_int, [c_void_p, c_void_p]),
+    "aipu_ep_moe_layer": (c_int, [c_void_p, ctypes.POINTER(MoeWeights), c_int64, c_void_p, c_int64, c_void_p, c_void_p]),
+    "aipu_ep_destroy": (c_int, [c_void_p]),
 }
 
 _lib = None

@@ -782,6 +782,164 @@ extern "C" int aipu_moe_combine(aipu_ctx* c, int64_t M, int64_t H, int topk, con
                                static_cast<cudaStream_t>(stream));
 }
 
+// ------------------------------------------------------------------ expert parallel over peer memory
+struct aipu_ep {
+  aipu_ctx* ctx = nullptr;
+  EpParams p = {};
+  void* buf = nullptr;   // this rank's symmetric buffer
+  size_t bytes = 0;
+  bool mapped[EP_MAX_RANKS] = {};
+  uint32_t* seq = nullptr;
+  void* loc = nullptr;   // local scratch: sel, sel_w, y_shared
+  int64_t E_local = 0;
+};
+
+extern "C" int aipu_ep_create(aipu_ctx* c, int world, int rank, int64_t max_tokens, int64_t hidden, int topk,
+                              aipu_ep** out, void* ipc_handle) {
+  if (!c || !out || !ipc_handle || world < 1 || world > EP_MAX_RANKS || rank < 0 || rank >= world ||
+      max_tokens <= 0 || max_tokens > 64 || hidden <= 0 || hidden % 256 || topk <= 0 || topk > 16)
+    return set_error(EINVAL_, "ep_create: bad arguments (world <= 8, tokens per rank <= 64)");
+  DeviceGuard dg(c->device);
+  aipu_ep* e = new aipu_ep();
+  e->ctx = c;
+  EpParams& p = e->p;
+  p.G = world;
+  p.rank = rank;
+  p.Mmax = static_cast<int>(max_tokens);
+  p.H = static_cast<int>(hidden);
+  p.T = topk;
+  const int64_t G = world, M = max_tokens, H = hidden, T = topk;
+  p.off_flags = 0;
+  p.off_in_sel = 256;
+  p.off_in_x = al256x(p.off_in_sel + 4 * G * M * T);
+  p.off_out = al256x(p.off_in_x + 2 * G * M * H);
+  e->bytes = al256x(p.off_out + 2 * G * M * T * H);
+  if (cudaMalloc(&e->buf, e->bytes) != cudaSuccess || cudaMemset(e->buf, 0, e->bytes) != cudaSuccess ||
+      cudaMalloc(reinterpret_cast<void**>(&e->seq), 256) != cudaSuccess || cudaMemset(e->seq, 0, 256) != cudaSuccess ||
+      cudaMalloc(&e->loc, al256x(4 * M * T) + al256x(2 * M * T) + al256x(2 * M * H)) != cudaSuccess) {
+    cudaFree(e->buf);
+    cudaFree(e->seq);
+    delete e;
+    return set_error(ENOMEM_, "ep_create: allocation");
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, e->buf) != cudaSuccess) {
+    cudaFree(e->buf);
+    cudaFree(e->seq);
+    cudaFree(e->loc);
+    delete e;
+    return set_error(ECUDA_, "ep_create: cudaIpcGetMemHandle");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  p.peers[rank] = static_cast<uint8_t*>(e->buf);
+  p.seq = e->seq;
+  p.status = c->status;
+  *out = e;
+  return OK;
+}
+
+extern "C" int aipu_ep_connect(aipu_ep* e, const void* handles) {
+  if (!e || !handles) return set_error(EINVAL_, "ep_connect: bad arguments");
+  DeviceGuard dg(e->ctx->device);
+  for (int q = 0; q < e->p.G; ++q) {
+    if (q == e->p.rank || e->mapped[q]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const uint8_t*>(handles) + q * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return set_error(ECUDA_, "ep_connect: cudaIpcOpenMemHandle (peer access over NVLink required)");
+    e->p.peers[q] = static_cast<uint8_t*>(ptr);
+    e->mapped[q] = true;
+  }
+  return OK;
+}
+
+extern "C" int aipu_ep_destroy(aipu_ep* e) {
+  if (!e) return OK;
+  DeviceGuard dg(e->ctx->device);
+  cudaDeviceSynchronize();
+  for (int q = 0; q < e->p.G; ++q)
+    if (e->mapped[q]) cudaIpcCloseMemHandle(e->p.peers[q]);
+  cudaFree(e->buf);
+  cudaFree(e->seq);
+  cudaFree(e->loc);
+  delete e;
+  return OK;
+}
+
+// One decode MoE layer with the routed experts sharded over the ranks (every rank calls it with the
+// same M): route the local tokens; store tokens and selections into every peer's inbox (peer stores,
+// released flags); shared expert on the local tokens; once every rank's tokens arrived, the local
+// experts on all of them (grouped GEMV, or the exact chains in strict mode) and their per-slot
+// outputs stored straight into each owner's outbox; once every piece arrived, the slot-order combine.
+extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t expert_lo, const void* x, int64_t M,
+                                 void* y, void* stream) {
+  if (!e || !W || !x || !y || M <= 0 || M > e->p.Mmax || W->hidden != e->p.H || W->topk != e->p.T ||
+      !W->router_w || (reinterpret_cast<uintptr_t>(x) & 15u))
+    return set_error(EINVAL_, "ep_moe_layer: bad arguments");
+  aipu_ctx* c = e->ctx;
+  const int64_t H = W->hidden, F = W->ffn, El = W->n_experts;
+  const int T = W->topk, G = e->p.G;
+  const int64_t Et = El * G;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
+  if (H % 256 || F % 256 || El <= 0 || Et > 1024 || W->gate_wtype != W->up_wtype || W->gate_wtype == AIPU_F32 ||
+      W->down_wtype == AIPU_F32 || expert_lo != static_cast<int64_t>(e->p.rank) * El)
+    return set_error(EINVAL_, "ep_moe_layer: bad weights descriptor (rank r holds experts [r*E, (r+1)*E))");
+  DeviceGuard dg(c->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t Gtok = G * M;
+  int32_t* sel = static_cast<int32_t*>(e->loc);
+  uint16_t* sel_w = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(e->loc) + al256x(4 * e->p.Mmax * T));
+  uint16_t* y_sh = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(e->loc) + al256x(4 * e->p.Mmax * T) +
+                                               al256x(2 * e->p.Mmax * T));
+  MoeScratch sc = {};
+  int rc = moe_scratch(c, Gtok, El, T, H, F, sc);
+  if (rc) return rc;
+  // 1. route the local tokens (all experts of the layer)
+  RouterParams rp = {};
+  rp.wt = W->router_wtype;
+  rp.w = static_cast<const uint8_t*>(W->router_w);
+  rp.bias = W->router_bias;
+  rp.x = static_cast<const uint16_t*>(x);
+  rp.M = static_cast<int>(M);
+  rp.K = static_cast<int>(H);
+  rp.E = static_cast<int>(Et);
+  rp.topk = T;
+  rp.scale = W->scale;
+  rp.gate = sc.gate;
+  rp.sel = sel;
+  rp.sel_w = sel_w;
+  rp.counters = c->router_counters;
+  rp.status = c->status;
+  if ((rc = router_launch(rp, s, false))) return rc;
+  // 2. dispatch
+  if ((rc = ep_bump_launch(e->p, s))) return rc;
+  if ((rc = ep_dispatch_launch(e->p, static_cast<const uint16_t*>(x), sel, static_cast<int>(M), s))) return rc;
+  // 3. shared expert on the local tokens while the peers' tokens arrive
+  if (shared && (rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype,
+                                    W->shared_down_w, H, F, 1, nullptr, nullptr, 1, x, M, sc.h_sh, y_sh, s, false)))
+    return rc;
+  // 4. every rank's tokens: local experts
+  if ((rc = ep_wait_launch(e->p, 0, s))) return rc;
+  const uint8_t* inbox = static_cast<const uint8_t*>(e->buf);
+  const int32_t* in_sel = reinterpret_cast<const int32_t*>(inbox + e->p.off_in_sel);
+  const uint16_t* in_x = reinterpret_cast<const uint16_t*>(inbox + e->p.off_in_x);
+  if ((rc = union_launch(in_sel, static_cast<int>(Gtok), T, static_cast<int>(expert_lo), static_cast<int>(El),
+                         sc.union_ids, sc.n_union, sc.slot_map, s)))
+    return rc;
+  const int Umax = static_cast<int>(std::min<int64_t>(El, Gtok * T));
+  if ((rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F,
+                          static_cast<int>(El), sc.union_ids, sc.n_union, Umax, in_x, Gtok, sc.h, sc.y, s, false)))
+    return rc;
+  // 5. per-slot outputs into the owners' outboxes
+  if ((rc = ep_return_launch(e->p, sc.slot_map, sc.y, static_cast<int>(M), static_cast<int>(Gtok), s))) return rc;
+  if ((rc = ep_wait_launch(e->p, 1, s))) return rc;
+  // 6. slot-order combine of this rank's tokens
+  return combine_pieces_launch(sel, sel_w, static_cast<int>(M), T, H, static_cast<int>(El),
+                               reinterpret_cast<const uint16_t*>(inbox + e->p.off_out), shared ? y_sh : nullptr,
+                               static_cast<uint16_t*>(y), s);
+}
+
 extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt, const void* uw, int dwt,
                                   const void* dw, int64_t H, int64_t F, const void* x, int64_t M, void* h, void* y,
                                   void* stream) {

@@ -68,6 +68,20 @@ int gather_slots_launch(const int32_t* index, int M, int topk, int64_t H, const 
                         int64_t row_add, uint16_t* y_slots, cudaStream_t s);
 // Expert-parallel combine: out[m] = bf16( sum_s sel_w[m,s] * pieces[owner(sel[m,s])][m, s] + shared[m] )
 // in slot order, owner(e) = e / experts_per_piece; pieces [P, M, topk, H] bf16.
+// expert-parallel exchange over peer memory (ep.cu)
+constexpr int EP_MAX_RANKS = 8;
+struct EpParams {
+  int G, rank, Mmax, H, T;
+  uint8_t* peers[EP_MAX_RANKS];  // every rank's symmetric buffer (this rank's own included)
+  int64_t off_flags, off_in_sel, off_in_x, off_out;
+  uint32_t* seq;                 // device sequence number of the current layer call (local)
+  int* status;
+};
+int ep_bump_launch(const EpParams& p, cudaStream_t s);
+int ep_dispatch_launch(const EpParams& p, const uint16_t* x, const int32_t* sel, int M, cudaStream_t s);
+int ep_wait_launch(const EpParams& p, int which, cudaStream_t s);
+int ep_return_launch(const EpParams& p, const int32_t* slot_map, const uint16_t* rows, int M, int Gtok,
+                     cudaStream_t s);
 int combine_pieces_launch(const int32_t* sel, const uint16_t* sel_w, int M, int topk, int64_t H,
                           int experts_per_piece, const uint16_t* pieces, const uint16_t* shared, uint16_t* out,
                           cudaStream_t s);

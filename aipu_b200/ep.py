@@ -14,16 +14,19 @@ One layer call on every rank, for that rank's M tokens (the same M on every rank
 
 The compute steps go through ``backend`` (the CUDA library by default); the communication uses
 torch.distributed, so the same orchestration runs with the gloo backend on CPU in tests, with a
-host backend that restates the compute.
+host backend that restates the compute. ``PeerExpertParallelMoE`` is the same layer with the
+exchange done inside the library over NVLink peer memory (decode sizes).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import ops
 
 
@@ -109,3 +112,51 @@ class ExpertParallelMoE:
         pieces = torch.empty((G, M, T, H), dtype=y_slots.dtype, device=y_slots.device)
         dist.all_to_all_single(pieces.view(G * M, T, H), y_slots.contiguous(), group=self.group)
         return self.backend.combine(sel, sw, W.local.n_experts, pieces, y_sh)
+
+
+class PeerExpertParallelMoE:
+    """The same layer with the exchange done by the library over NVLink peer memory (CUDA IPC):
+    tokens and selections are stored straight into every peer's inbox and the per-slot expert outputs
+    straight into each owner's outbox, with sequence-numbered flags (bounded device waits) instead of
+    NCCL collectives. Decode sizes: at most ``max_tokens`` (<= 64) tokens per rank and call; every
+    rank calls with the same number of tokens. torch.distributed is used once, to exchange the IPC
+    handles."""
+
+    def __init__(self, weights: ShardedMoeWeights, max_tokens: int = 8, group=None, ctx: Optional[ops.Context] = None):
+        self.W = weights
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if weights.n_experts_total != weights.local.n_experts * self.world:
+            raise ValueError("every rank must hold n_experts_total / world experts")
+        if weights.expert_lo != self.rank * weights.local.n_experts:
+            raise ValueError("rank r must hold experts [r * E_local, (r + 1) * E_local)")
+        d = torch.device("cuda", torch.cuda.current_device())
+        self.ctx = ctx or ops.Context(d)
+        self._cs = weights.local.cstruct()
+        self._cs.n_experts = weights.local.n_experts
+        h = ctypes.create_string_buffer(64)
+        ep = ctypes.c_void_p()
+        L.check(L.lib().aipu_ep_create(self.ctx.handle, self.world, self.rank, max_tokens, weights.hidden,
+                                       weights.topk, ctypes.byref(ep), h))
+        self._ep = ep
+        mine = torch.frombuffer(bytearray(h.raw), dtype=torch.uint8).to(d)
+        allh = torch.empty((self.world, 64), dtype=torch.uint8, device=d)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        handles = allh.cpu().numpy().tobytes()
+        L.check(L.lib().aipu_ep_connect(self._ep, handles))
+        dist.barrier(group=group)
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x.dtype != torch.bfloat16 or not x.is_cuda:
+            raise ValueError("tokens must be bf16 on the GPU")
+        M = x.shape[0]
+        if out is None:
+            out = torch.empty((M, self.W.hidden), dtype=torch.bfloat16, device=x.device)
+        L.check(L.lib().aipu_ep_moe_layer(self._ep, ctypes.byref(self._cs), self.W.expert_lo, x.data_ptr(), M,
+                                          out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream))
+        return out
+
+    def close(self):
+        if self._ep:
+            L.lib().aipu_ep_destroy(self._ep)
+            self._ep = None

@@ -308,6 +308,44 @@ def moe_prefill(W, M=2048, reps=10):
             "peak_source": kind, "flops": flops}
 
 
+def _time_ep_layer(layer, x, reps):
+    """Device time per call of an expert-parallel layer (CUDA graph when capture works), max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    d = x.device
+    for _ in range(5):
+        layer(x)
+    torch.cuda.synchronize()
+    run, graphed = (lambda: layer(x)), False
+    try:
+        gr = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            layer(x)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(gr, stream=s):
+                layer(x)
+        torch.cuda.synchronize()
+        run, graphed = gr.replay, True
+    except Exception:  # capture unsupported here: time eager calls
+        torch.cuda.synchronize()
+    for _ in range(5):
+        run()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps / 1e3], device=d, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"t": float(t.item()), "graphed": graphed}
+
+
 def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
     """BASELINE config 3/5 decode layer with the 256 routed experts sharded over the N ranks
     (256/N per GPU, NCCL all-gather dispatch and all-to-all return); every rank decodes M tokens.
@@ -333,52 +371,26 @@ def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
         shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=14, device=d),
         shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=15, device=d),
         shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
-    layer = ep.ExpertParallelMoE(ep.ShardedMoeWeights(local, rank * n, E), backend=ep.CudaBackend(ops.Context(d)))
+    sharded = ep.ShardedMoeWeights(local, rank * n, E)
+    layers = {"nccl": ep.ExpertParallelMoE(sharded, backend=ep.CudaBackend(ops.Context(d))),
+              "peer": ep.PeerExpertParallelMoE(sharded, max_tokens=max(M_list))}
     expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
     out = {}
-    for M in M_list:
-        x = torch.randn((M, H), device=d, generator=g.manual_seed(100 + M + 7 * rank)).to(torch.bfloat16)
-        for _ in range(5):
-            layer(x)
-        torch.cuda.synchronize()
-        # one layer (router, NCCL dispatch, experts, NCCL return, combine) as a CUDA graph
-        run, graphed = (lambda: layer(x)), False
-        try:
-            gr = torch.cuda.CUDAGraph()
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                layer(x)
-                torch.cuda.synchronize()
-                with torch.cuda.graph(gr, stream=s):
-                    layer(x)
-            torch.cuda.synchronize()
-            run, graphed = gr.replay, True
-        except Exception:  # capture unsupported here: time eager calls
-            torch.cuda.synchronize()
-        for _ in range(5):
-            run()
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            run()
-        e1.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / reps / 1e3], device=d, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t = float(t.item())
-        # experts this rank touched in one layer (union of its local experts over all N*M tokens)
-        sel_all = torch.empty((world * M, T), dtype=torch.int32, device=d)
-        sel, _, _ = ops.moe_router(F.F32, local.router_w, x, E, T, bias=local.router_bias)
-        dist.all_gather_into_tensor(sel_all, sel)
-        touched = len(set(v for v in sel_all.cpu().numpy().reshape(-1).tolist() if rank * n <= v < (rank + 1) * n))
-        byts = H * E * 4 + (touched + 1) * expert_bytes
-        out[f"M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(world * M / t, 1),
-                        "tokens_per_rank": M, "experts_per_gpu": n, "rank0_touched_experts": touched,
-                        "cuda_graph": graphed,
-                        "rank0_hbm_gbs": round(byts / t / 1e9, 1)}
+    for kind, layer in layers.items():
+        for M in M_list:
+            x = torch.randn((M, H), device=d, generator=g.manual_seed(100 + M + 7 * rank)).to(torch.bfloat16)
+            r = _time_ep_layer(layer, x, reps)
+            t = r["t"]
+            # experts this rank touched in one layer (union of its local experts over all N*M tokens)
+            sel_all = torch.empty((world * M, T), dtype=torch.int32, device=d)
+            sel, _, _ = ops.moe_router(F.F32, local.router_w, x, E, T, bias=local.router_bias)
+            dist.all_gather_into_tensor(sel_all, sel)
+            touched = len(set(v for v in sel_all.cpu().numpy().reshape(-1).tolist() if rank * n <= v < (rank + 1) * n))
+            byts = H * E * 4 + (touched + 1) * expert_bytes
+            out[f"{kind}_M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(world * M / t, 1),
+                                   "tokens_per_rank": M, "experts_per_gpu": n, "rank0_touched_experts": touched,
+                                   "cuda_graph": r["graphed"], "rank0_hbm_gbs": round(byts / t / 1e9, 1)}
+    layers["peer"].close()
     return out
 
 

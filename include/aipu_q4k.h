@@ -200,6 +200,25 @@ int aipu_moe_experts(aipu_ctx* ctx, const aipu_moe_weights* w_local, int64_t exp
 int aipu_moe_combine(aipu_ctx* ctx, int64_t M, int64_t H, int topk, const int32_t* sel, const void* sel_w,
                      int64_t experts_per_piece, const void* pieces, const void* y_shared, void* out, void* stream);
 
+/* Expert-parallel decode layer over NVLink peer memory (one process per GPU). Each rank creates an
+ * endpoint (a symmetric buffer for max_tokens tokens per rank) and gets its CUDA IPC handle
+ * (64 bytes); the caller exchanges the handles (e.g. an all-gather) and connects every rank to all
+ * the others. aipu_ep_moe_layer then runs one MoE layer for this rank's M tokens (the same M on
+ * every rank): route, store tokens and selections into every peer's inbox, the local experts on all
+ * ranks' tokens, per-slot outputs stored into each owner's outbox, slot-order combine. Arrival is
+ * signalled by sequence-numbered flags; every device wait is bounded (the context status word
+ * reports an expired wait). w_local: this rank's experts [rank * E, (rank + 1) * E) plus the
+ * replicated router (all experts) and shared expert. AIPU_FLAG_STRICT gives the one-GPU layer's
+ * bits. No counterpart in the reference (its MoE runs on one device); same contract as
+ * aipu_moe_layer (tools/glm_model_q4k_ref.py:797-809). */
+typedef struct aipu_ep aipu_ep;
+int aipu_ep_create(aipu_ctx* ctx, int world, int rank, int64_t max_tokens, int64_t hidden, int topk, aipu_ep** ep,
+                   void* ipc_handle);
+int aipu_ep_connect(aipu_ep* ep, const void* handles);
+int aipu_ep_moe_layer(aipu_ep* ep, const aipu_moe_weights* w_local, int64_t expert_lo, const void* x, int64_t M,
+                      void* y, void* stream);
+int aipu_ep_destroy(aipu_ep* ep);
+
 #ifdef __cplusplus
 }
 #endif

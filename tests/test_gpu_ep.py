@@ -4,8 +4,8 @@
   the all-to-all done by indexing), checked bit for bit against the one-GPU layer in strict mode and
   within the reference SwiGLU tolerance against the oracle in fast mode, for few tokens (grouped
   GEMV) and many (tcgen05);
-* two GPUs (skipped with fewer): ExpertParallelMoE over NCCL in child processes, strict mode, bit
-  for bit against the one-GPU layer.
+* two GPUs (skipped with fewer): ExpertParallelMoE over NCCL and PeerExpertParallelMoE over NVLink
+  peer memory in child processes, strict mode bit for bit against the one-GPU layer.
 """
 import os
 import socket
@@ -146,3 +146,58 @@ def test_expert_parallel_two_gpus_nccl_strict():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert res == {0: True, 1: True}
+
+
+def _p2p_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from aipu_b200 import ep
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    res = {}
+    try:
+        d = torch.device("cuda", rank)
+        W = _layer(d, 6144, 2048, 256, 8, seed=77)
+        for strict in (True, False):
+            ctx = ops.Context(d).set_flags(strict=strict)
+            layer = ep.PeerExpertParallelMoE(ep.shard(W, rank, world), max_tokens=4, ctx=ctx)
+            ok = True
+            for call, M in enumerate((3, 1, 4)):  # several calls: the flags advance per call
+                rng = np.random.default_rng(2000 + 10 * rank + call)
+                x = torch.from_numpy(qo.bf16_round(rng.standard_normal((M, 6144)).astype(F32))).to(d).to(torch.bfloat16)
+                out = layer(x)
+                ref = ops.moe_layer(W, x, ctx=ctx)
+                torch.cuda.synchronize()
+                if strict:
+                    ok = ok and bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
+                else:
+                    ud = qo.ulp_diff_bf16(_bf16_np(out), _bf16_np(ref))
+                    ok = ok and float(np.mean(ud <= 1)) >= 0.99
+            assert ctx.status() == 0
+            layer.close()
+            res["strict" if strict else "fast"] = ok
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_two_gpus_peer_memory():
+    """The NVLink peer-memory exchange: strict mode equals the one-GPU layer bit for bit, fast mode
+    within 1 ulp of it on >= 99 % of outputs, over several calls."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res == {0: {"strict": True, "fast": True}, 1: {"strict": True, "fast": True}}
