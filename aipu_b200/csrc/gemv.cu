@@ -688,32 +688,44 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
       if (whole) {
         gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, acc, lane);
       } else {
-        const int slot2 = (ch.tile == a / nsb) ? 0 : 1;
+        // this worker holds units [seg0, cc.u) of the tile: slot 0 = its first tile, 1 = its last
+        const int slot2 = (seg0 == a) ? 0 : 1;
         *reinterpret_cast<float4*>(p.partials + ((static_cast<int64_t>(wid) * 2 + slot2) * 32 + lane) * 4) =
             make_float4(acc[0], acc[1], acc[2], acc[3]);
         __threadfence();
         __syncwarp();
+        // arrivals count units: the piece that completes the tile's nsb units finishes it
         int old = 0;
-        if (lane == 0) old = atomicAdd(&p.counters[ch.tile], 1);
+        if (lane == 0) old = atomicAdd(&p.counters[ch.tile], cc.u - seg0);
         old = __shfl_sync(0xffffffffu, old, 0);
-        const int wf = worker_of_unit(static_cast<int64_t>(ch.tile) * nsb, U, W);
-        const int wl = worker_of_unit(static_cast<int64_t>(ch.tile + 1) * nsb - 1, U, W);
-        // workers with an empty range (more workers than units) hold no piece
-        int npieces = 0;
-        const int64_t U64 = U;
-        for (int w2 = wf; w2 <= wl; ++w2) npieces += (U64 * w2 / W < U64 * (w2 + 1) / W) ? 1 : 0;
-        if (old == npieces - 1) {
+        if (old + (cc.u - seg0) == nsb) {
           __threadfence();
+          // walk the workers whose ranges meet the tile, in worker order (range starts by
+          // floor(U w / W), stepped incrementally from the first one)
+          const int64_t t0u = static_cast<int64_t>(ch.tile) * nsb, t1u = t0u + nsb;
+          int w2 = worker_of_unit(t0u, U, W);
+          int64_t s = static_cast<int64_t>(U) * w2 / W;
+          int64_t frac = (static_cast<int64_t>(U) * w2) % W;
+          const int64_t qs = U / W, rs = U % W;
           float v[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int w2 = wf; w2 <= wl; ++w2) {
-            if (U64 * w2 / W == U64 * (w2 + 1) / W) continue;
-            const int s2 = (ch.tile == static_cast<int>((U64 * w2 / W) / nsb)) ? 0 : 1;
-            const float4 r = __ldcg(reinterpret_cast<const float4*>(
-                p.partials + ((static_cast<int64_t>(w2) * 2 + s2) * 32 + lane) * 4));
-            v[0] = __fadd_rn(v[0], r.x);
-            v[1] = __fadd_rn(v[1], r.y);
-            v[2] = __fadd_rn(v[2], r.z);
-            v[3] = __fadd_rn(v[3], r.w);
+          while (s < t1u && w2 < W) {
+            int64_t e = s + qs;
+            frac += rs;
+            if (frac >= W) {
+              frac -= W;
+              ++e;
+            }
+            if (e > s) {  // non-empty range [s, e) of worker w2
+              const int s2 = (s < t0u) ? 1 : 0;  // the tile is w2's first tile unless w2 began earlier
+              const float4 r = __ldcg(reinterpret_cast<const float4*>(
+                  p.partials + ((static_cast<int64_t>(w2) * 2 + s2) * 32 + lane) * 4));
+              v[0] = __fadd_rn(v[0], r.x);
+              v[1] = __fadd_rn(v[1], r.y);
+              v[2] = __fadd_rn(v[2], r.z);
+              v[3] = __fadd_rn(v[3], r.w);
+            }
+            s = e;
+            ++w2;
           }
           gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, v, lane);
           if (lane == 0) p.counters[ch.tile] = 0;
@@ -791,8 +803,11 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
     if (p.xg > GEMV_MAXXG) return set_error(-1, "gemv: too many activation groups per CTA");
   }
   const int limit = 232448 - 1024 - 2 * GEMV_MAXW * 4;  // dynamic smem limit minus static
+  // at least ~4 units per worker: fewer pieces per tile when a launch has few units
+  const int64_t want_w = std::max<int64_t>(4, std::min<int64_t>(16, U / (4 * static_cast<int64_t>(grid))));
   int nw = 0, ns = 0;
   for (int cand_w : {16, 12, 8, 4}) {
+    if (cand_w > want_w && cand_w > 4) continue;
     for (int cand_s = GEMV_MAXS; cand_s >= 2; --cand_s) {
       if (gemv_layout(wt, ncols, p.K, p.xg, cand_w, cand_s, p.pitch, p.xpitch).total <= limit) {
         nw = cand_w;
