@@ -71,6 +71,35 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// Shared-memory progress counters between two warps of a CTA (cheaper than an mbarrier round trip
+// when the waiting warp is on the critical path). Writer: its lanes' shared stores, __syncwarp, then
+// one lane publishes with st.release; reader: every lane polls with ld.acquire.
+__device__ __forceinline__ uint32_t ld_acquire_cta_shared(const uint32_t* f) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(f)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_cta_shared(uint32_t* f, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(f)), "r"(v) : "memory");
+}
+// Warp-uniform bounded wait until *f >= target (wrapping compare). Returns the value seen (>= target),
+// or target - 1 after `limit_cycles` (status bit set).
+__device__ __forceinline__ uint32_t warp_wait_counter(const uint32_t* f, uint32_t target, int* status, int bit,
+                                                      long long limit_cycles = 4000000000LL) {
+  // every lane acquires; the value returned is the warp minimum (each lane saw at least that much)
+  uint32_t v = ld_acquire_cta_shared(f) - target;
+  if (__all_sync(0xffffffffu, static_cast<int32_t>(v) >= 0)) return __reduce_min_sync(0xffffffffu, v) + target;
+  const long long t0 = clock64();
+  while (true) {
+    v = ld_acquire_cta_shared(f) - target;
+    if (__all_sync(0xffffffffu, static_cast<int32_t>(v) >= 0)) return __reduce_min_sync(0xffffffffu, v) + target;
+    if (__any_sync(0xffffffffu, clock64() - t0 > limit_cycles)) {
+      if (status && (threadIdx.x & 31) == 0) atomicOr(status, bit);
+      return target - 1u;
+    }
+  }
+}
+
 // 1-D bulk copy global -> shared, completion counted on an mbarrier (the untiled TMA path).
 // dst, src 16-byte aligned, bytes a multiple of 16. No multicast.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -91,6 +120,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, 
 }
 
 // ------------------------------------------------------------------ programmatic dependent launch
+// atomic add with release (this thread's and, through a preceding barrier, its CTA's writes) and
+// acquire (the writes released by earlier adders) at GPU scope; returns the old value
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -129,64 +129,121 @@ int swiglu_elem_launch(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t
 // wins ties), balanced add tree, Quake rsqrt^2 renormalisation x SCALE (glm_model_q4k_ref.py:669-681).
 // Stage 3 (the last token to finish): the sorted union of selected experts over all tokens and
 // each (token, slot)'s index into it, for the grouped expert GEMVs and the combine.
-__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
-    v = w > v ? w : v;
-  }
-  return v;
-}
-
-__device__ void router_topk_token(const RouterParams& p, int m) {
+// One warp per token. Lane l holds experts [l*per, (l+1)*per) (per = ceil(E/32)) as (order key of
+// the score, 0x7FFFFFFF - e) and its own best; each of the T rounds takes the warp maximum with two
+// redux.sync (key, then the lowest index among equal keys), the winner's lane replaces its best.
+// The T winning gates stay in registers; the balanced tree is the zero-padded 16-leaf tree, which
+// equals the reference's 2^ceil(log2 T)-leaf tree (the padding contributes exact +0 additions).
+template <int MAXPL>  // experts per lane: 8 (E <= 256) or 32 (E <= 1024)
+__device__ void router_topk_token_pl(const RouterParams& p, int m, const float* bias_pre, int* sel_s) {
   const int lane = threadIdx.x & 31;
   const int E = p.E, T = p.topk;
-  constexpr int MAXPL = 32;  // E <= 1024
-  unsigned long long key[MAXPL];
   const int per = (E + 31) / 32;
+  const int eb = lane * per;
+  uint32_t kh[MAXPL];
+  uint16_t gb[MAXPL];
+  const uint16_t* g = p.gate + static_cast<int64_t>(m) * E;
 #pragma unroll
   for (int j = 0; j < MAXPL; ++j) {
-    key[j] = 0ull;
-    const int e = j * 32 + lane;
+    kh[j] = 0u;
+    gb[j] = 0;
+    const int e = eb + j;
     if (j < per && e < E) {
-      const float gate = bf16_bits_to_f32(__ldcg(p.gate + static_cast<int64_t>(m) * E + e));
-      const float score = p.bias ? __fadd_rn(gate, __ldg(p.bias + e)) : gate;
-      key[j] = (static_cast<unsigned long long>(f32_order_key(score)) << 32) | static_cast<uint32_t>(0x7FFFFFFF - e);
+      gb[j] = __ldcg(g + e);
+      const float gate = bf16_bits_to_f32(gb[j]);
+      const float score = p.bias ? __fadd_rn(gate, bias_pre ? bias_pre[j] : __ldg(p.bias + e)) : gate;
+      kh[j] = f32_order_key(score);
     }
   }
+  // the lane's best: highest key, lowest index among equal keys (strict > keeps the first)
+  uint32_t bk;
+  int bj;
+  bk = 0u;
+  bj = -1;
+#pragma unroll
+  for (int j = 0; j < MAXPL; ++j)
+    if (j < per && eb + j < E && (bj < 0 || kh[j] > bk)) {
+      bk = kh[j];
+      bj = j;
+    }
   float win[16];
-  int sel[16];
-  for (int s = 0; s < T; ++s) {
-    unsigned long long best = 0ull;
+  int my_sel = 0;       // lane s keeps the s-th selection
+  float my_win = 0.f;
+  uint32_t taken = 0u;  // this lane's selected entries (bit j)
 #pragma unroll
-    for (int j = 0; j < MAXPL; ++j) best = key[j] > best ? key[j] : best;
-    best = warp_max_u64(best);
-    const int e = 0x7FFFFFFF - static_cast<int>(best & 0xFFFFFFFFull);
+  for (int s = 0; s < 16; ++s) {
+    win[s] = 0.f;
+    if (s < T) {
+      const bool has = bj >= 0;
+      const uint32_t top = __reduce_max_sync(0xffffffffu, has ? bk : 0u);
+      const uint32_t lo = (has && bk == top) ? static_cast<uint32_t>(0x7FFFFFFF - (eb + bj)) : 0u;
+      const uint32_t best_lo = __reduce_max_sync(0xffffffffu, lo);
+      const int e = 0x7FFFFFFF - static_cast<int>(best_lo);
+      const int wl = e / per;
+      uint16_t gsel = 0;
 #pragma unroll
-    for (int j = 0; j < MAXPL; ++j)
-      if (key[j] == best) key[j] = 0ull;
-    sel[s] = e;
-    win[s] = bf16_bits_to_f32(__ldcg(p.gate + static_cast<int64_t>(m) * E + e));
-  }
-  if (lane == 0) {
-    // balanced fp32 add tree of ceil(log2 T) levels, +0 padded (glm_model_q4k_ref.py:691-699)
-    float node[16];
-    int lev = 1;
-    while ((1 << lev) < T) ++lev;
-    const int npow = 1 << lev;
-    for (int i = 0; i < npow; ++i) node[i] = i < T ? win[i] : 0.f;
-    for (int l = 0, n = npow; l < lev; ++l, n >>= 1)
-      for (int i = 0; i < n / 2; ++i) node[i] = __fadd_rn(node[2 * i], node[2 * i + 1]);
-    const float rr = quake_rsqrt(node[0]);
-    const float rs = __fmul_rn(__fmul_rn(rr, rr), p.scale);
-    for (int s = 0; s < T; ++s) {
-      p.sel[m * T + s] = sel[s];
-      p.sel_w[m * T + s] = bf16_rne_bits(__fmul_rn(win[s], rs));
+      for (int j = 0; j < MAXPL; ++j)
+        if (j == bj) gsel = gb[j];
+      win[s] = bf16_bits_to_f32(__shfl_sync(0xffffffffu, gsel, wl));
+      if (lane == s) {
+        my_sel = e;
+        my_win = win[s];
+      }
+      if (lane == wl) {
+        taken |= 1u << bj;
+        bj = -1;
+        bk = 0u;
+#pragma unroll
+        for (int j = 0; j < MAXPL; ++j)
+          if (j < per && eb + j < E && !((taken >> j) & 1u) && (bj < 0 || kh[j] > bk)) {
+            bk = kh[j];
+            bj = j;
+          }
+      }
     }
+  }
+  // balanced fp32 add tree (glm_model_q4k_ref.py:691-699), 16 leaves, +0 padded
+  float node[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) node[i] = win[i];
+#pragma unroll
+  for (int n = 16; n > 1; n >>= 1)
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) node[i] = __fadd_rn(node[2 * i], node[2 * i + 1]);
+  const float rr = quake_rsqrt(node[0]);
+  const float rs = __fmul_rn(__fmul_rn(rr, rr), p.scale);
+  if (lane < T) {
+    p.sel[m * T + lane] = my_sel;
+    p.sel_w[m * T + lane] = bf16_rne_bits(__fmul_rn(my_win, rs));
+    sel_s[lane] = my_sel;
   }
 }
 
-__device__ void router_union(const RouterParams& p) {
+// wide routers out of line, so their 32 keys per lane do not raise the kernel's register count
+__device__ __noinline__ void router_topk_token_wide(const RouterParams& p, int m, int* sel_s) {
+  router_topk_token_pl<32>(p, m, nullptr, sel_s);
+}
+
+// the score bias of this lane's experts (E <= 256: lane l holds [l*per, (l+1)*per)), loaded before
+// the cross-CTA hand-off so the top-k does not wait on it
+__device__ __forceinline__ void router_bias_pre(const RouterParams& p, float (&b)[8]) {
+  const int lane = threadIdx.x & 31, per = (p.E + 31) / 32;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = lane * per + j;
+    b[j] = (p.bias && j < per && e < p.E) ? __ldg(p.bias + e) : 0.f;
+  }
+}
+
+__device__ void router_topk_token(const RouterParams& p, int m, const float (&bias_pre)[8], int* sel_s) {
+  if (p.E <= 256)
+    router_topk_token_pl<8>(p, m, bias_pre, sel_s);
+  else
+    router_topk_token_wide(p, m, sel_s);
+}
+
+// sel_s: the selections in shared memory (one token block), or null (read p.sel from L2)
+__device__ void router_union(const RouterParams& p, const int* sel_s) {
   // one warp: mark selected experts, emit them in ascending expert order
   const int lane = threadIdx.x & 31;
   const int T = p.topk, M = p.M;
@@ -194,7 +251,7 @@ __device__ void router_union(const RouterParams& p) {
   mask[lane] = 0u;
   __syncwarp();
   for (int i = lane; i < M * T; i += 32) {
-    const int e = __ldcg(p.sel + i);
+    const int e = sel_s ? sel_s[i] : __ldcg(p.sel + i);
     atomicOr(&mask[e >> 5], 1u << (e & 31));
   }
   __syncwarp();
@@ -213,7 +270,7 @@ __device__ void router_union(const RouterParams& p) {
   if (lane == 31) *p.n_union = pre;
   __syncwarp();
   for (int i = lane; i < M * T; i += 32) {
-    const int e = __ldcg(p.sel + i);
+    const int e = sel_s ? sel_s[i] : __ldcg(p.sel + i);
     const int wd = e >> 5, bit = e & 31;
     // rank of e = (count of set bits in words < wd) + popcount(mask[wd] & ((1<<bit)-1))
     int rank = 0;
@@ -223,48 +280,74 @@ __device__ void router_union(const RouterParams& p) {
   }
 }
 
-// One CTA = 32 experts x a block of up to 8 tokens; one consumer warp per token (lane = expert),
-// each lane running the sequential fp32 chain of its (token, expert) logit. For the dense fp32
-// router ([K, E]) a producer warp streams 128-row x 32-expert chunks of W (and the matching
-// activation slices) into a shared-memory ring with 1-D bulk copies, so the chains never wait on
-// DRAM latency. GGUF-row routers dequantise each weight exactly in the chain.
+// One CTA = EG experts x a block of up to 8 tokens; one chain warp per token (lane = expert), each
+// lane running the sequential fp32 chain of its (token, expert) logit. For the dense fp32 router
+// ([K, E]) a producer warp streams 128-row x EG-expert boxes of W by tiled TMA (and the matching
+// activation slices by bulk copies) into a shared-memory ring, so the chains never wait on DRAM
+// latency. GGUF-row routers dequantise each weight exactly in the chain.
 constexpr int RT_CHUNK = 128;   // k rows per stage
 // experts per CTA: 8 for few tokens (lanes 0..7 run the chains, four times the CTAs stream the
 // router), 32 for many tokens (every lane runs a chain)
 constexpr int RT_MB = 8;        // tokens per CTA
+constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
+// EG = 8 (decode) splits each token over warps: product warps write the chunk's 1024 fp32 products
+// into a per-token shared ring, the chain warp runs only the dependent adds (one warp doing both is
+// issue-bound at ~10 cycles per k; the add chain alone runs near the add latency)
 template <int EG>
 struct RtCfg {
-  static constexpr int NST = (EG == 8) ? 16 : 6;  // ring depth
+  static constexpr bool SPLIT = (EG == 8);
+  static constexpr int NST = SPLIT ? 8 : 6;  // input ring depth
   static constexpr int WBYTES = RT_CHUNK * EG * 4;
+  static constexpr int NWARP = SPLIT ? 2 * RT_MB + 1 : RT_MB + 1;
+  static constexpr int PSTR = 132;            // floats per expert row of a product slot (padded)
+  static constexpr int PSLOT = EG * PSTR * 4;  // bytes of one product slot
+  static constexpr int NPS = 4;               // product slots per token at 8 tokens (fewer tokens: more)
+  static constexpr int OFF_RING = 1024;
+  static constexpr int OFF_PROD = OFF_RING + NST * (WBYTES + RT_XBYTES);
+  static constexpr int SMEM = OFF_PROD + (SPLIT ? RT_MB * NPS * PSLOT : 0);
 };
-constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
 
-#ifdef RT_TRACE
-__device__ long long g_rt_trace[4];
-extern "C" int aipu_debug_rt_trace(long long* out) {
-  cudaMemcpyFromSymbol(out, g_rt_trace, sizeof(g_rt_trace));
-  static const long long z[4] = {};
-  cudaMemcpyToSymbol(g_rt_trace, z, sizeof(z));
+// Debug builds only (-DRT_GT): globaltimer marks of one router call, read back by
+// aipu_debug_rt_gt (not part of the product library).
+#ifdef RT_GT
+// globaltimer marks of one call: ~min start, max chain end, top-k end, union end
+__device__ unsigned long long g_rt_gt[4];
+__device__ __forceinline__ unsigned long long rt_gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+extern "C" int aipu_debug_rt_gt(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, g_rt_gt, sizeof(g_rt_gt));
+  static const unsigned long long z[4] = {};
+  cudaMemcpyToSymbol(g_rt_gt, z, sizeof(z));
   return 0;
 }
 #endif
 template <int RT_EG>
-__global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const __grid_constant__ RouterParams p) {
-  constexpr int RT_NST = RtCfg<RT_EG>::NST;
-  constexpr int RT_WBYTES = RtCfg<RT_EG>::WBYTES;
-#ifdef RT_TRACE
-  const long long t_start = clock64();
+__global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(const __grid_constant__ RouterParams p) {
+  using RC = RtCfg<RT_EG>;
+  constexpr int RT_NST = RC::NST;
+  constexpr int RT_WBYTES = RC::WBYTES;
+#ifdef RT_GT
+  if (threadIdx.x == 0) atomicMax(&g_rt_gt[0], ~rt_gtime());
 #endif
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + RT_NST;
-  uint8_t* ring = smem + 256;  // barriers first (2 x RT_NST <= 32 of them); TMA destinations 128-byte aligned
+  uint8_t* ring = smem + RC::OFF_RING;  // barriers first; TMA destinations 128-byte aligned
   __shared__ int last_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = blockIdx.x * RT_EG, e = e0 + lane;
   const bool live = (lane < RT_EG) && (e < p.E);
   const int m0 = blockIdx.y * RT_MB;
   const int mb = min(RT_MB, p.M - m0);
+  // SPLIT: product slots per token (the RT_MB * NPS slots shared by the block's tokens, at most 16
+  // each; chunk c of token t in slot t * nps + c % nps), and per token the chunks whose products are
+  // written (pready[t]) and the chunks the chain has consumed (pdone[t])
+  const int nps = min(16, (RT_MB * RC::NPS) / mb);
+  uint32_t* pready = reinterpret_cast<uint32_t*>(empty + RT_NST);
+  uint32_t* pdone = pready + RT_MB;
   const int K = p.K, E = p.E;
   const bool dense = (p.wt == WT_F32);
   const int nchunk = (K + RT_CHUNK - 1) / RT_CHUNK;
@@ -273,36 +356,109 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const _
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], mb);
     }
+    for (int s = 0; s < 2 * RT_MB; ++s) pready[s] = 0u;  // pready and pdone
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_wait();
   if (warp == RT_MB) {
-    // producer: W[k0:k0+128, e0:e0+32] rows and x[m0+m, k0:k0+128] slices
-    if (!dense) return;
-    for (int c = 0; c < nchunk; ++c) {
+    // producer: W[k0:k0+128, e0:e0+EG] boxes and x[m0+m, k0:k0+128] slices. The first RT_NST W boxes
+    // are requested before griddepcontrol.wait (the router weights are not written by the kernel
+    // this launch may overlap), the activations after it.
+    if (!dense) {
+      pdl_wait();
+      return;
+    }
+    const int npre = min(RT_NST, nchunk);
+    auto issue_w = [&](int c) {
       const int slot = c % RT_NST;
-      if (c >= RT_NST) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((c / RT_NST) - 1) & 1, p.status, ST_TIMEOUT_EMPTY);
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
-      }
       const int k0 = c * RT_CHUNK, kl = min(RT_CHUNK, K - k0);
       const uint32_t xrow = static_cast<uint32_t>((kl * 2 + 15) & ~15);
       uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
-      if (lane == 0) {
-        // one tiled TMA request for the whole 128-row x 32-expert box (out-of-range parts read 0)
-        mbar_arrive_expect_tx(&full[slot], RT_WBYTES + xrow * mb);
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-                "r"(smem_u32(st)),
-            "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(e0), "r"(k0), "r"(smem_u32(&full[slot]))
-            : "memory");
-      }
-      __syncwarp();
+      // one tiled TMA request for the whole 128-row x EG-expert box (out-of-range parts read 0)
+      mbar_arrive_expect_tx(&full[slot], RT_WBYTES + xrow * mb);
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+              "r"(smem_u32(st)),
+          "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(e0), "r"(k0), "r"(smem_u32(&full[slot]))
+          : "memory");
+    };
+    auto issue_x = [&](int c) {
+      const int slot = c % RT_NST;
+      const int k0 = c * RT_CHUNK, kl = min(RT_CHUNK, K - k0);
+      const uint32_t xrow = static_cast<uint32_t>((kl * 2 + 15) & ~15);
+      uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
       if (lane < mb)
         bulk_g2s(st + RT_WBYTES + lane * RT_CHUNK * 2, p.x + static_cast<int64_t>(m0 + lane) * K + k0, xrow,
                  &full[slot]);
+    };
+    if (lane == 0)
+      for (int c = 0; c < npre; ++c) issue_w(c);
+    __syncwarp();
+    pdl_wait();
+    for (int c = 0; c < npre; ++c) issue_x(c);
+    for (int c = npre; c < nchunk; ++c) {
+      const int slot = c % RT_NST;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait_bounded(&empty[slot], ((c / RT_NST) - 1) & 1, p.status, ST_TIMEOUT_EMPTY);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
+      if (lane == 0) issue_w(c);
+      __syncwarp();
+      issue_x(c);
+    }
+    return;
+  }
+  pdl_wait();
+  if (RC::SPLIT && warp > RT_MB) {
+    // product warp of token m0 + pw: the products of each chunk into the token's product slots
+    const int pw = warp - RT_MB - 1;
+    if (pw >= mb || !dense) return;
+    uint32_t done_seen = 0u;
+    for (int c = 0; c < nchunk; ++c) {
+      const int slot = c % RT_NST, ps = pw * nps + c % nps;
+      const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
+      bool ok = mbar_wait_bounded(&full[slot], (c / RT_NST) & 1, p.status, ST_TIMEOUT_FULL);
+      if (!__all_sync(0xffffffffu, ok)) return;
+      // the slot's previous chunk (c - nps) must be consumed; re-read the chain's counter only when
+      // the last value seen does not cover it
+      if (c - nps + 1 > static_cast<int>(done_seen)) {
+        const uint32_t want = static_cast<uint32_t>(c - nps + 1);
+        done_seen = warp_wait_counter(&pdone[pw], want, p.status, ST_TIMEOUT_EMPTY);
+        if (static_cast<int32_t>(done_seen - want) < 0) return;
+      }
+      const uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
+      const float4* ws = reinterpret_cast<const float4*>(st);
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(st + RT_WBYTES + pw * RT_CHUNK * 2);
+      float* pb = reinterpret_cast<float*>(smem + RC::OFF_PROD + ps * RC::PSLOT);
+      // lane = k within each 32-row group: the row's 8 weights (two float4) times x[k], stored
+      // expert-major (bank (4 e + k) mod 32: conflict-free). All operands are loaded before the first
+      // store (the stores could alias the loads as far as the compiler knows).
+      constexpr int NJ = RT_CHUNK / 32;
+      float4 w0[NJ], w1[NJ];
+      float xv[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int k = lane + 32 * j;
+        w0[j] = ws[2 * k];
+        w1[j] = ws[2 * k + 1];
+        xv[j] = (k < kl) ? bf16_bits_to_f32(xs[k]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int k = lane + 32 * j;
+        pb[0 * RC::PSTR + k] = __fmul_rn(xv[j], w0[j].x);
+        pb[1 * RC::PSTR + k] = __fmul_rn(xv[j], w0[j].y);
+        pb[2 * RC::PSTR + k] = __fmul_rn(xv[j], w0[j].z);
+        pb[3 * RC::PSTR + k] = __fmul_rn(xv[j], w0[j].w);
+        pb[4 * RC::PSTR + k] = __fmul_rn(xv[j], w1[j].x);
+        pb[5 * RC::PSTR + k] = __fmul_rn(xv[j], w1[j].y);
+        pb[6 * RC::PSTR + k] = __fmul_rn(xv[j], w1[j].z);
+        pb[7 * RC::PSTR + k] = __fmul_rn(xv[j], w1[j].w);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[slot]);
+        st_release_cta_shared(&pready[pw], static_cast<uint32_t>(c + 1));
+      }
     }
     return;
   }
@@ -310,18 +466,62 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const _
   const int m = m0 + warp;
   if (warp < mb) {
     float acc = 0.f;
-    if (dense) {
+    if (RC::SPLIT && dense) {
+      // the chain over the products, in k order; 32 of them loaded ahead of the adds
+      bool ok = true;
+      uint32_t ready_seen = 0u;
+      for (int c = 0; c < nchunk && ok; ++c) {
+        const int ps = warp * nps + c % nps;
+        // the counter is re-read only when the chunks seen ready so far are used up (a hand-off costs
+        // a few hundred cycles on the critical chain; one read often covers several chunks)
+        if (c >= static_cast<int>(ready_seen)) {
+          const uint32_t want = static_cast<uint32_t>(c + 1);
+          ready_seen = warp_wait_counter(&pready[warp], want, p.status, ST_TIMEOUT_FULL);
+          ok = static_cast<int32_t>(ready_seen - want) >= 0;
+        }
+        if (!ok) break;
+        const float4* pr = reinterpret_cast<const float4*>(smem + RC::OFF_PROD + ps * RC::PSLOT +
+                                                           (lane & (RT_EG - 1)) * RC::PSTR * 4);
+        float4 a0[8], a1[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a0[i] = pr[i];
+#pragma unroll
+        for (int b = 0; b < RT_CHUNK / 32; b += 2) {
+          if (b + 1 < RT_CHUNK / 32) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a1[i] = pr[8 * (b + 1) + i];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            acc = __fadd_rn(acc, a0[i].x);
+            acc = __fadd_rn(acc, a0[i].y);
+            acc = __fadd_rn(acc, a0[i].z);
+            acc = __fadd_rn(acc, a0[i].w);
+          }
+          if (b + 2 < RT_CHUNK / 32) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a0[i] = pr[8 * (b + 2) + i];
+          }
+          if (b + 1 < RT_CHUNK / 32) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              acc = __fadd_rn(acc, a1[i].x);
+              acc = __fadd_rn(acc, a1[i].y);
+              acc = __fadd_rn(acc, a1[i].z);
+              acc = __fadd_rn(acc, a1[i].w);
+            }
+          }
+        }
+        // (a short last chunk has zero products past its end; adding them leaves the sum unchanged)
+        __syncwarp();
+        if (lane == 0) st_release_cta_shared(&pdone[warp], static_cast<uint32_t>(c + 1));
+      }
+    } else if (dense) {
       bool ok = true;
       for (int c = 0; c < nchunk; ++c) {
         const int slot = c % RT_NST;
         const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
-#ifdef RT_TRACE
-        const long long tw0 = clock64();
-#endif
         if (ok) ok = mbar_wait_bounded(&full[slot], (c / RT_NST) & 1, p.status, ST_TIMEOUT_FULL);
-#ifdef RT_TRACE
-        if (lane == 0 && blockIdx.x == 0 && blockIdx.y == 0 && warp == 0) g_rt_trace[0] += clock64() - tw0;
-#endif
         if (ok) {
           const uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
           const float* ws = reinterpret_cast<const float*>(st);
@@ -377,39 +577,46 @@ __global__ void __launch_bounds__(32 * (RT_MB + 1)) router_strict_kernel(const _
       if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
     }
   }
-#ifdef RT_TRACE
-  if (lane == 0 && blockIdx.x == 0 && blockIdx.y == 0 && warp == 0) g_rt_trace[1] += clock64() - t_start;
+#ifdef RT_GT
+  if (threadIdx.x == 0) atomicMax(&g_rt_gt[1], rt_gtime());
 #endif
   // the last CTA of this token block selects top-K for its tokens; the last block builds the union
+  __shared__ int sel_s[RT_MB * 16];
+  float bias_pre[8];
+  router_bias_pre(p, bias_pre);
   named_bar_sync(1, 32 * RT_MB);
-  if (threadIdx.x == 0) {
-    __threadfence();
-    last_flag = (atomicAdd(&p.counters[blockIdx.y], 1) == static_cast<int>(gridDim.x) - 1);
-  }
-  named_bar_sync(1, 32 * RT_MB);
-  if (!last_flag) return;
-  __threadfence();
-  if (warp < mb) router_topk_token(p, m);
-  named_bar_sync(1, 32 * RT_MB);
-  if (threadIdx.x == 0) {
-    p.counters[blockIdx.y] = 0;
-    __threadfence();
-    last_flag = (atomicAdd(&p.counters[gridDim.y], 1) == static_cast<int>(gridDim.y) - 1);
-  }
+  if (threadIdx.x == 0)
+    last_flag = (atom_add_acq_rel_gpu(&p.counters[blockIdx.y], 1) == static_cast<int>(gridDim.x) - 1);
   named_bar_sync(1, 32 * RT_MB);
   if (!last_flag) return;
-  __threadfence();
+  if (warp < mb) router_topk_token(p, m, bias_pre, sel_s + warp * p.topk);
+#ifdef RT_GT
+  if (threadIdx.x == 0) atomicMax(&g_rt_gt[2], rt_gtime());
+#endif
+  named_bar_sync(1, 32 * RT_MB);
+  if (gridDim.y > 1) {
+    if (threadIdx.x == 0) {
+      p.counters[blockIdx.y] = 0;
+      last_flag = (atom_add_acq_rel_gpu(&p.counters[gridDim.y], 1) == static_cast<int>(gridDim.y) - 1);
+    }
+    named_bar_sync(1, 32 * RT_MB);
+    if (!last_flag) return;
+  }
   if (warp == 0) {
-    if (lane == 0) p.counters[gridDim.y] = 0;
-    if (p.union_ids) router_union(p);
+    if (lane == 0) p.counters[gridDim.y > 1 ? gridDim.y : blockIdx.y] = 0;
+    if (p.union_ids) router_union(p, gridDim.y > 1 ? nullptr : sel_s);
+#ifdef RT_GT
+    if (lane == 0) atomicMax(&g_rt_gt[3], rt_gtime());
+#endif
   }
 }
 
 template <int EG>
 static int router_launch_eg(const RouterParams& p, cudaStream_t s, bool pdl) {
-  constexpr int NST = RtCfg<EG>::NST;
-  static_assert(2 * NST * 8 <= 256, "router barriers fit before the ring");
-  const int smem = 256 + NST * (RtCfg<EG>::WBYTES + RT_XBYTES);
+  using RC = RtCfg<EG>;
+  static_assert(2 * RC::NST * 8 + 2 * RT_MB * 4 <= RC::OFF_RING, "router barriers fit before the ring");
+  static_assert(RC::SMEM <= 227 * 1024, "router shared memory");
+  const int smem = RC::SMEM;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(router_strict_kernel<EG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -425,7 +632,7 @@ static int router_launch_eg(const RouterParams& p, cudaStream_t s, bool pdl) {
     if (rc) return rc;
   }
   return launch_kernel(reinterpret_cast<const void*>(router_strict_kernel<EG>),
-                       dim3((p.E + EG - 1) / EG, (p.M + RT_MB - 1) / RT_MB), dim3(32 * (RT_MB + 1)), smem, s, pdl, &q);
+                       dim3((p.E + EG - 1) / EG, (p.M + RT_MB - 1) / RT_MB), dim3(32 * RC::NWARP), smem, s, pdl, &q);
 }
 
 int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {

@@ -7,6 +7,7 @@ device at most, inputs larger than L2).
     python -m aipu_b200.profile_cases gemv --wtype 0 --m 1 --groups 8
     python -m aipu_b200.profile_cases tc --wtype 1 --n 49152 --k 2048 --m 64
     python -m aipu_b200.profile_cases moe --experts 64 --tokens 512
+    python -m aipu_b200.profile_cases router --tokens 1
 """
 from __future__ import annotations
 
@@ -59,6 +60,18 @@ def case_moe(experts: int, tokens: int, hidden: int = 6144, ffn: int = 2048, top
     print("moe ok", float(y.float().abs().mean()))
 
 
+def case_router(tokens: int, hidden: int = 6144, experts: int = 256, topk: int = 8) -> None:
+    d = torch.device("cuda", 0)
+    g = torch.Generator(device=d)
+    w = torch.randn((hidden, experts), device=d, generator=g.manual_seed(1)) * 0.02
+    b = torch.randn((experts,), device=d, generator=g.manual_seed(2)) * 0.01
+    x = torch.randn((tokens, hidden), device=d, generator=g.manual_seed(3)).to(torch.bfloat16)
+    for _ in range(4):
+        sel, _, _ = ops.moe_router(F.F32, w, x, experts, topk, bias=b)
+    torch.cuda.synchronize()
+    print("router ok", int(sel.sum()))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     sub = ap.add_subparsers(dest="case", required=True)
@@ -74,11 +87,15 @@ def main() -> None:
     a = sub.add_parser("moe")
     a.add_argument("--experts", type=int, default=64)
     a.add_argument("--tokens", type=int, default=512)
+    a = sub.add_parser("router")
+    a.add_argument("--tokens", type=int, default=1)
     args = ap.parse_args()
     if args.case == "gemv":
         case_gemv(args.wtype, args.m, args.groups)
     elif args.case == "tc":
         case_tc(args.wtype, args.n, args.k, args.m)
+    elif args.case == "router":
+        case_router(args.tokens)
     else:
         case_moe(args.experts, args.tokens)
 

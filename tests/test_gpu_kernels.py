@@ -212,7 +212,7 @@ def test_router_reference_fixture_bitexact(golden, name):
     assert np.array_equal(bf16_np(gate).view(np.uint32), g[f"{name}_gate"])
 
 
-@pytest.mark.parametrize("M", [1, 4])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 8])
 def test_router_fp32_bias_config3_bitexact(M):
     """BASELINE config 3 router: fp32 6144 x 256 ~ N(0, 0.02), bias ~ N(0, 0.01), top-8, x2.5."""
     H, E, T = 6144, 256, 8
@@ -224,6 +224,24 @@ def test_router_fp32_bias_config3_bitexact(M):
     sel, sw, gate, logits = ops.moe_router(F.F32, to_dev(wr), np_to_bf16_dev(x), E, T, bias=to_dev(bias),
                                            want_logits=True)
     assert np.array_equal(bf16_np(logits).view(np.uint32), mo.router_logits(x, wr.T.copy()).view(np.uint32))
+    assert np.array_equal(sel.cpu().numpy(), sel_r)
+    assert np.array_equal(bf16_np(sw).view(np.uint32), sw_r.view(np.uint32))
+    assert np.array_equal(bf16_np(gate).view(np.uint32), gate_r.view(np.uint32))
+
+
+@pytest.mark.parametrize("E,T,M", [(40, 8, 3), (512, 16, 2), (1024, 8, 5), (256, 16, 9)])
+def test_router_fp32_ties_and_widths_bitexact(E, T, M):
+    """Expert counts other than 256 (per-lane key lists of 2, 16 and 32 entries), top-16, and exact
+    ties: columns duplicated in pairs with equal biases, so the lower index must win every tie."""
+    H = 512
+    rng = np.random.default_rng(E + T + M)
+    wr = rng.normal(0, 0.05, (H, E)).astype(F32)
+    bias = rng.normal(0, 0.01, E).astype(F32)
+    wr[:, 1::2] = wr[:, 0::2]
+    bias[1::2] = bias[0::2]
+    x = qo.bf16_round(rng.standard_normal((M, H)).astype(F32))
+    sel_r, sw_r, gate_r = mo.moe_router(x, wr.T.copy(), T, bias=bias)
+    sel, sw, gate = ops.moe_router(F.F32, to_dev(wr), np_to_bf16_dev(x), E, T, bias=to_dev(bias))
     assert np.array_equal(sel.cpu().numpy(), sel_r)
     assert np.array_equal(bf16_np(sw).view(np.uint32), sw_r.view(np.uint32))
     assert np.array_equal(bf16_np(gate).view(np.uint32), gate_r.view(np.uint32))
