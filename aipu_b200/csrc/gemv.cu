@@ -200,6 +200,102 @@ __device__ __forceinline__ void unit_q6k(const uint8_t* rg, const uint8_t* rg8, 
   }
 }
 
+// 4 bytes at a shared-memory address known to be 4-byte aligned (A4) or 2 mod 4 (two aligned words
+// and a byte permute).
+template <bool A4>
+__device__ __forceinline__ uint32_t lds4(const uint8_t* p) {
+  if (A4) return *reinterpret_cast<const uint32_t*>(p);
+  const uint32_t w0 = *reinterpret_cast<const uint32_t*>(p - 2), w1 = *reinterpret_cast<const uint32_t*>(p + 2);
+  return __byte_perm(w0, w1, 0x5432);
+}
+
+// Q6_K unit for up to 4 live columns (MP = 1, 2 or 4 columns padded to a power of two): the MMA's
+// 8 output columns hold 8 / MP scale groups x MP columns, so the 16-weight groups of a super-block
+// accumulate in 2 MP sets of fp32 accumulators and are scaled once per unit (one multiply-add per
+// accumulator instead of one per group). Lane (g, t) feeds B column g: column g % MP, group slot
+// g / MP (zeros for the MMAs of other slots). acc holds per-lane partial sums over groups until
+// q6k_fold combines the lanes at the end of a tile.
+template <int MP, bool A4>
+__device__ __forceinline__ void unit_q6k_mp(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcolm, bool mok,
+                                            int gslot, int sb, int t, float (&acc)[4]) {
+  constexpr int NGM = 8 / MP;    // groups per accumulator set
+  constexpr int NSET = 16 / NGM;
+  float D[NSET][4];
+#pragma unroll
+  for (int i = 0; i < NSET; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
+  const uint8_t* xb = xcolm + 2 * (sb * 256 + 4 * t);
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+    for (int lh = 0; lh < 2; ++lh) {
+      const int off = 16 * lh + 4 * t;
+      const uint32_t qa = lds4<A4>(rg + 64 * hf + off), qb = lds4<A4>(rg + 64 * hf + 32 + off);
+      const uint32_t qh = lds4<A4>(rg + 128 + 32 * hf + off);
+      const uint32_t ra = lds4<A4>(rg8 + 64 * hf + off), rb = lds4<A4>(rg8 + 64 * hf + 32 + off);
+      const uint32_t rh = lds4<A4>(rg8 + 128 + 32 * hf + off);
+      uint32_t cg[4], c8[4];
+      cg[0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
+      cg[1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
+      cg[2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
+      cg[3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+      c8[0] = (ra & 0x0F0F0F0Fu) | ((rh << 4) & 0x30303030u);
+      c8[1] = (rb & 0x0F0F0F0Fu) | ((rh << 2) & 0x30303030u);
+      c8[2] = ((ra >> 4) & 0x0F0F0F0Fu) | (rh & 0x30303030u);
+      c8[3] = ((rb >> 4) & 0x0F0F0F0Fu) | ((rh >> 2) & 0x30303030u);
+#pragma unroll
+      for (int qi = 0; qi < 4; ++qi) {
+        const int grp = 8 * hf + 2 * qi + lh;
+        uint32_t a[4];
+        a[0] = hsub2_u32(lop3_and_or(cg[qi], 0x003F003Fu, H2_1024), H2_1056);
+        a[1] = hsub2_u32(lop3_and_or(c8[qi], 0x003F003Fu, H2_1024), H2_1056);
+        a[2] = hsub2_u32(lop3_and_or(cg[qi] >> 8, 0x003F003Fu, H2_1024), H2_1056);
+        a[3] = hsub2_u32(lop3_and_or(c8[qi] >> 8, 0x003F003Fu, H2_1024), H2_1056);
+        uint2 xv = make_uint2(0, 0);
+        if (mok && gslot == grp % NGM) xv = *reinterpret_cast<const uint2*>(xb + 2 * (128 * hf + 32 * qi + 16 * lh));
+        mma_f16_16816(D[grp / NGM], a, xv.x, xv.y);
+      }
+    }
+  }
+  const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg + 208));
+  const float d8 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg8 + 208));
+  const int8_t* scg = reinterpret_cast<const int8_t*>(rg + 192);
+  const int8_t* sc8 = reinterpret_cast<const int8_t*>(rg8 + 192);
+#pragma unroll
+  for (int st = 0; st < NSET; ++st) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int gc = st * NGM + (2 * t + h) / MP;  // the group of this lane's output column 2t + h
+      acc[h] = fmaf(__fmul_rn(dg, static_cast<float>(scg[gc])), D[st][h], acc[h]);
+      acc[2 + h] = fmaf(__fmul_rn(d8, static_cast<float>(sc8[gc])), D[st][2 + h], acc[2 + h]);
+    }
+  }
+}
+
+// End of a tile for unit_q6k_mp: sum each column's partials over the lanes holding its group slots
+// and leave column c in the standard layout (lane t = c / 2, element h = c % 2).
+template <int MP>
+__device__ __forceinline__ void q6k_fold(float (&acc)[4]) {
+  if (MP == 1) {
+    float v0 = __fadd_rn(acc[0], acc[1]), v2 = __fadd_rn(acc[2], acc[3]);
+    v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, 1));
+    v2 = __fadd_rn(v2, __shfl_xor_sync(0xffffffffu, v2, 1));
+    v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, 2));
+    v2 = __fadd_rn(v2, __shfl_xor_sync(0xffffffffu, v2, 2));
+    acc[0] = v0;
+    acc[2] = v2;
+    acc[1] = acc[3] = 0.f;
+  } else if (MP == 2) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[i] = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 1));
+      acc[i] = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 2));
+    }
+  } else if (MP == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 2));
+  }
+}
+
 __device__ __forceinline__ void unit_q80(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol, bool colok,
                                          int sb, int t, float (&acc)[4]) {
   const uint8_t* xb = xcol + 2 * (sb * 256 + 4 * t);
@@ -636,6 +732,13 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
   const int g = lane >> 2, t = lane & 3;
   const bool colok = g < ncols;
   const int gx = colok ? g : 0;  // lanes of dead columns read column 0 (their results are never stored)
+  // Q6_K with at most 4 columns: B column g = (group slot g / mp, column g % mp). Only with the tiled
+  // copies, where every row of a slot starts at the same offset, so the unit's alignment variant is
+  // the same for the whole warp (its MMAs must not diverge).
+  const int mp = (WT == WT_Q6K && p.use_tmap) ? (ncols == 1 ? 1 : ncols == 2 ? 2 : ncols <= 4 ? 4 : 8) : 8;
+  const int gslot = g / mp;
+  const bool mok = (g % mp) < ncols;
+  const int gxm = mok ? g % mp : 0;
   const int* misc0 = reinterpret_cast<const int*>(smem + L.off_misc);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
@@ -659,13 +762,27 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     const uint8_t* rg = st + g * p.pitch + hg;
     const uint8_t* r8 = st + (g + 8) * p.pitch + h8;
     const uint8_t* xcol = smem + L.off_xs + (xsl * ncols + gx) * p.xpitch;
+    const uint8_t* xcolm = smem + L.off_xs + (xsl * ncols + gxm) * p.xpitch;
     for (int i = 0; i < ch.n; ++i) {
       const int sb = ch.sb + i;
       if (WT == WT_Q4K) {
         const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
         unit_q4k(rg + i * UB, r8 + i * UB, xcol, sxcol, sb, t, acc);
       } else if (WT == WT_Q6K) {
-        unit_q6k(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
+        // warp-uniform (lane 0's row; all rows share the offset when mp < 8)
+        const bool a4 = __shfl_sync(0xffffffffu, ((reinterpret_cast<uintptr_t>(rg) + i * UB) & 3u) == 0u, 0);
+        if (mp == 1) {
+          if (a4) unit_q6k_mp<1, true>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+          else unit_q6k_mp<1, false>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+        } else if (mp == 2) {
+          if (a4) unit_q6k_mp<2, true>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+          else unit_q6k_mp<2, false>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+        } else if (mp == 4) {
+          if (a4) unit_q6k_mp<4, true>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+          else unit_q6k_mp<4, false>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+        } else {
+          unit_q6k(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
+        }
       } else if (WT == WT_Q80) {
         unit_q80(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
       } else {
@@ -682,6 +799,11 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     prefetch();  // refill the slot just freed
     if (ch.sb + ch.n == nsb || cc.u == b) {
       // ---------------- this worker's piece of `tile` is done
+      if (WT == WT_Q6K) {
+        if (mp == 1) q6k_fold<1>(acc);
+        else if (mp == 2) q6k_fold<2>(acc);
+        else if (mp == 4) q6k_fold<4>(acc);
+      }
       const int seg0 = max(a, ch.tile * nsb);
       const bool whole = (seg0 == ch.tile * nsb) && (cc.u == (ch.tile + 1) * nsb);
       const int* misc = misc0 + xsl * 8;

@@ -79,6 +79,8 @@ def main() -> None:
     a.add_argument("--wtype", type=int, default=F.Q4_K)
     a.add_argument("--m", type=int, default=1)
     a.add_argument("--groups", type=int, default=8)
+    a.add_argument("--n", type=int, default=2048)
+    a.add_argument("--k", type=int, default=6144)
     a = sub.add_parser("tc")
     a.add_argument("--wtype", type=int, default=F.Q4_K)
     a.add_argument("--n", type=int, default=32768)
@@ -91,7 +93,7 @@ def main() -> None:
     a.add_argument("--tokens", type=int, default=1)
     args = ap.parse_args()
     if args.case == "gemv":
-        case_gemv(args.wtype, args.m, args.groups)
+        case_gemv(args.wtype, args.m, args.groups, args.n, args.k)
     elif args.case == "tc":
         case_tc(args.wtype, args.n, args.k, args.m)
     elif args.case == "router":

@@ -170,6 +170,18 @@ def test_gemm_fast_config1_fp32_x():
     assert_close_bf16(bf16_np(y), ref)
 
 
+@pytest.mark.parametrize("wt", [F.Q6_K, F.Q8_0])
+@pytest.mark.parametrize("M", [1, 2, 3])
+def test_gemm_fast_fp32_x_small_m(wt, M):
+    """fp32 activations (two fp16 columns per token) at 1-3 tokens: 2, 4 and 6 live MMA columns."""
+    N, K = 1000, 2048
+    w = F.random_rows_np(wt, N, K, seed=200 + wt + M)
+    x = np.random.default_rng(70 + M).standard_normal((M, K)).astype(F32)
+    ref = qo.gemm(wt, w, N, K, x)
+    y = ops.gemm(wt, to_dev(w), N, K, to_dev(x))
+    assert_close_bf16(bf16_np(y), ref, f"wt={wt} M={M}")
+
+
 @pytest.mark.parametrize("N,K", [(1, 256), (5, 256), (17, 512), (40, 2048), (300, 768), (16, 6144)])
 def test_gemm_fast_ragged_and_streamk_splits(N, K):
     """Ragged N (partial tiles), tiny problems where one tile is cut across many CTAs."""
