@@ -391,10 +391,15 @@ static int moe_scratch(aipu_ctx* c, int64_t M, int64_t E, int T, int64_t H, int6
 }
 
 // SwiGLU on groups of experts: h[g] = bf16(silu(x Wg_e) * (x Wu_e)), y[g] = h[g] Wd_e
+// shared memory of one SM (bytes): two CTAs whose shared memory adds up to more never share an SM
+static const int kSmemPerSm = 233472;
+
 static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, const void* uw, int dwt, const void* dw,
                          int64_t H, int64_t F, int n_experts, const int* group_ids, const int* n_groups_dev,
                          int n_groups,
-                         const void* x, int64_t M, uint16_t* h, uint16_t* y, cudaStream_t s, bool pdl) {
+                         const void* x, int64_t M, uint16_t* h, uint16_t* y, cudaStream_t s, bool pdl,
+                         int num_sms = 0, int min_smem = 0) {
+  if (num_sms <= 0) num_sms = c->num_sms;
   const int64_t gstride = F * row_bytes_of(gwt, H), dstride = H * row_bytes_of(dwt, F);
   if (c->flags & AIPU_FLAG_STRICT) {
     // bit-exact chains (tools/glm_model_q4k_ref.py:702-708): gate into h, up into a temporary,
@@ -460,7 +465,7 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
     p.partials = ws.partials;
     p.counters = ws.counters;
     p.status = c->status;
-    int rc = gemv_launch(gwt, XT_BF16, EPI_SWIGLU, p, c->num_sms, s, pdl);
+    int rc = gemv_launch(gwt, XT_BF16, EPI_SWIGLU, p, num_sms, s, pdl, min_smem);
     if (rc) return rc;
     GemvParams q = p;
     q.w0 = static_cast<const uint8_t*>(dw);
@@ -473,7 +478,11 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
     q.x_group_stride = M * F;
     q.y = y + m0 * H;
     q.y_group_stride = M * H;
-    rc = gemv_launch(dwt, XT_BF16, EPI_STORE, q, c->num_sms, s, pdl);
+    // the group list was complete before the gate/up launch began (its producers do not trigger
+    // their dependents early), so the down projection may read it and prefetch weights while the
+    // gate/up launch drains
+    q.ids_ready = 1;
+    rc = gemv_launch(dwt, XT_BF16, EPI_STORE, q, num_sms, s, pdl, min_smem);
     if (rc) return rc;
   }
   return OK;
@@ -672,15 +681,11 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
   int rc = moe_scratch(c, M, E, T, H, F, sc);
   if (rc) return rc;
   const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
-  if (shared) {
-    // shared expert on the side stream, overlapping the (serial) router
-    if ((rc = set_cuda_error(cudaEventRecord(c->ev_fork, s), "eventRecord"))) return rc;
-    if ((rc = set_cuda_error(cudaStreamWaitEvent(c->side, c->ev_fork, 0), "streamWaitEvent"))) return rc;
-    rc = swiglu_groups(c, c->ws[1], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
-                       H, F, 1, nullptr, nullptr, 1, x, M, sc.h_sh, sc.y_sh, c->side, false);
-    if (rc) return rc;
-    if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
-  }
+  // the shared expert runs on the side stream beside the (serial, latency-bound) router: the fork
+  // point is recorded before the router, the side launches are submitted after it, on the SMs the
+  // router leaves free and with enough shared memory that they cannot share an SM with it (a
+  // co-resident GEMV would take issue slots from the router's dependent add chains)
+  if (shared && (rc = set_cuda_error(cudaEventRecord(c->ev_fork, s), "eventRecord"))) return rc;
   RouterParams rp = {};
   rp.wt = W->router_wtype;
   rp.w = static_cast<const uint8_t*>(W->router_w);
@@ -700,6 +705,16 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
   rp.counters = c->router_counters;
   rp.status = c->status;
   if ((rc = router_launch(rp, s, false))) return rc;
+  if (shared) {
+    const int router_ctas = router_grid_ctas(rp);
+    const int side_sms = std::max(1, c->num_sms - router_ctas);
+    if ((rc = set_cuda_error(cudaStreamWaitEvent(c->side, c->ev_fork, 0), "streamWaitEvent"))) return rc;
+    rc = swiglu_groups(c, c->ws[1], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
+                       H, F, 1, nullptr, nullptr, 1, x, M, sc.h_sh, sc.y_sh, c->side, false, side_sms,
+                       kSmemPerSm - router_smem_bytes(rp));
+    if (rc) return rc;
+    if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
+  }
   const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
   rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F, static_cast<int>(E), sc.union_ids,
                      sc.n_union, Umax, x, M, sc.h, sc.y, s, true);

@@ -708,12 +708,14 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
       ++issued;
     }
   };
-  if (!dyn) {
-    setup_range(p.n_groups);
+  // (a dynamic group list is read before the wait only when the host marks it as already complete)
+  const bool early = !dyn || p.ids_ready;
+  if (early) {
+    setup_range(p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
     prefetch();
   }
   pdl_wait();
-  if (dyn) {
+  if (!early) {
     setup_range(p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
     prefetch();
   }
@@ -881,7 +883,7 @@ static int launch_one(GemvParams p, int grid, int nw, int smem, cudaStream_t str
 // units per slot: rows of at least ~288 bytes per bulk copy keep the copy engine efficient
 static int gemv_upc(int wt) { return wt == WT_Q4K ? 2 : wt == WT_Q6K ? 2 : wt == WT_Q80 ? 2 : 1; }
 
-int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl) {
+int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl, int min_smem) {
   const int ncols = (xt == XT_F32) ? 2 * p.M : p.M;
   if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ncols > 8) return set_error(-1, "gemv: bad shape");
   if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
@@ -941,7 +943,7 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   }
   if (!nw) return set_error(-1, "gemv: activation block too large for shared memory");
   p.nslots = ns;
-  const int smem = gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch).total;
+  const int smem = std::min(limit, std::max(min_smem, gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch).total));
 #define AIPU_GEMV_CASE(W, X, E)                                              \
   if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, nw, smem, stream, pdl);
   AIPU_GEMV_CASE(WT_Q4K, XT_BF16, EPI_STORE)
@@ -1020,7 +1022,7 @@ extern "C" int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_
     p.partials = partials;
     p.counters = counters;
     p.status = nullptr;
-    const int rc = gemv_launch(wtype, x_dtype, EPI_STORE, p, sms[dev], s, false);
+    const int rc = gemv_launch(wtype, x_dtype, EPI_STORE, p, sms[dev], s, false, 0);
     if (rc) return rc;
   }
   return OK;

@@ -66,6 +66,9 @@ struct GemvParams {
   int xg;                    // activation groups staged per CTA (1 when x is shared by all groups)
   int n_experts;             // extent of the expert dimension of w0/w1 (tensor maps)
   int use_tmap;              // 1: each slot is filled by one tiled TMA request (two for EPI_SWIGLU)
+  int ids_ready;             // 1: group_ids / n_groups_dev were complete before the launch preceding this
+                             // one began, so they are read (and weights prefetched) before
+                             // griddepcontrol.wait
   int tm_esz;                // tensor-map element size (bytes)
   int tm_box;                // tensor-map box width (elements)
   alignas(64) CUtensorMap tmap0;  // [expert][row][row bytes / esz] over w0

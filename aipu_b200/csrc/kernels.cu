@@ -645,6 +645,15 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
   return (p.M <= 4 * RT_MB) ? router_launch_eg<8>(p, s, pdl) : router_launch_eg<32>(p, s, pdl);
 }
 
+int router_grid_ctas(const RouterParams& p) {
+  const int eg = (p.M <= 4 * RT_MB) ? 8 : 32;
+  return ((p.E + eg - 1) / eg) * ((p.M + RT_MB - 1) / RT_MB);
+}
+
+int router_smem_bytes(const RouterParams& p) {
+  return (p.M <= 4 * RT_MB) ? RtCfg<8>::SMEM : RtCfg<32>::SMEM;
+}
+
 // ------------------------------------------------------------------ combine
 // out[m, d] = bf16( (sum over slots in slot order of fmul(w_slot, y_slot[d])) + y_shared[d] )
 // (tools/glm_model_q4k_ref.py:799-809)

@@ -140,8 +140,12 @@ int swiglu_elem_launch(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t
 int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,
                        cudaStream_t s);
 int router_launch(const RouterParams& p, cudaStream_t s, bool pdl);
+int router_grid_ctas(const RouterParams& p);  // CTAs of the launch router_launch makes
+int router_smem_bytes(const RouterParams& p); // its dynamic shared memory per CTA
 int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl);
-int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl);
+// min_smem: dynamic shared memory of at least this many bytes per CTA (keeps CTAs off SMs whose
+// remaining shared memory is less, e.g. SMs running a concurrent latency-bound kernel)
+int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl, int min_smem = 0);
 int gemv_partials_floats(int num_sms);
 int act_launch(int kind, const void* x, int64_t n, void* out, cudaStream_t s);
 
