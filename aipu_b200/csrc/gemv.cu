@@ -765,7 +765,8 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     const uint8_t* r8 = st + (g + 8) * p.pitch + h8;
     const uint8_t* xcol = smem + L.off_xs + (xsl * ncols + gx) * p.xpitch;
     const uint8_t* xcolm = smem + L.off_xs + (xsl * ncols + gxm) * p.xpitch;
-    for (int i = 0; i < ch.n; ++i) {
+    // a chunk is one or two units (upc <= 2): straight-line calls, no loop over a runtime count
+    auto do_unit = [&](const int i) {
       const int sb = ch.sb + i;
       if (WT == WT_Q4K) {
         const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
@@ -790,7 +791,9 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
       } else {
         unit_f16(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
       }
-    }
+    };
+    do_unit(0);
+    if (ch.n > 1) do_unit(1);
     __syncwarp();
     ++consumed;
     if (++slot == S) {
@@ -881,6 +884,7 @@ static int launch_one(GemvParams p, int grid, int nw, int smem, cudaStream_t str
 }
 
 // units per slot: rows of at least ~288 bytes per bulk copy keep the copy engine efficient
+// (at most 2: the kernel processes a chunk as one or two straight-line units)
 static int gemv_upc(int wt) { return wt == WT_Q4K ? 2 : wt == WT_Q6K ? 2 : wt == WT_Q80 ? 2 : 1; }
 
 int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl, int min_smem) {
