@@ -909,7 +909,7 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   p.use_tmap = aligned ? 1 : 0;
   if (p.use_tmap) {
     p.tm_esz = (wt == WT_Q6K) ? 2 : 8;
-    p.tm_box = (wt == WT_Q4K) ? 36 : (wt == WT_Q6K) ? 240 : 68;
+    p.tm_box = (wt == WT_Q4K) ? 18 * p.upc : (wt == WT_Q6K) ? 240 : 68;
     p.pitch = p.tm_box * p.tm_esz;
     const int ne = ne_map;
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.row_bytes / p.tm_esz), static_cast<cuuint64_t>(p.N),
