@@ -470,8 +470,23 @@ __global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(con
       // the chain over the products, in k order; 32 of them loaded ahead of the adds
       bool ok = true;
       uint32_t ready_seen = 0u;
+      // the token's product slots, stepped without a division on the chain's path
+      const uint8_t* pbase = smem + RC::OFF_PROD + warp * nps * RC::PSLOT + (lane & (RT_EG - 1)) * RC::PSTR * 4;
+      const uint8_t* pend = pbase + nps * RC::PSLOT;
+      const uint8_t* pcur = pbase;
+      static_assert(RT_CHUNK == 128, "four batches of 32 products per chunk");
+      float4 a0[8], a1[8];
+      bool pre = false;  // a0 already holds the first 32 products of chunk c
+      auto add8 = [&](const float4 (&v)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          acc = __fadd_rn(acc, v[i].x);
+          acc = __fadd_rn(acc, v[i].y);
+          acc = __fadd_rn(acc, v[i].z);
+          acc = __fadd_rn(acc, v[i].w);
+        }
+      };
       for (int c = 0; c < nchunk && ok; ++c) {
-        const int ps = warp * nps + c % nps;
         // the counter is re-read only when the chunks seen ready so far are used up (a hand-off costs
         // a few hundred cycles on the critical chain; one read often covers several chunks)
         if (c >= static_cast<int>(ready_seen)) {
@@ -480,38 +495,30 @@ __global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(con
           ok = static_cast<int32_t>(ready_seen - want) >= 0;
         }
         if (!ok) break;
-        const float4* pr = reinterpret_cast<const float4*>(smem + RC::OFF_PROD + ps * RC::PSLOT +
-                                                           (lane & (RT_EG - 1)) * RC::PSTR * 4);
-        float4 a0[8], a1[8];
+        const float4* pr = reinterpret_cast<const float4*>(pcur);
+        pcur += RC::PSLOT;
+        if (pcur == pend) pcur = pbase;
+        // batches of 32 products, the next batch loaded while the current one is added
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a0[i] = pr[i];
+        for (int i = 0; i < 8; ++i)
+          if (!pre) a0[i] = pr[i];
 #pragma unroll
-        for (int b = 0; b < RT_CHUNK / 32; b += 2) {
-          if (b + 1 < RT_CHUNK / 32) {
+        for (int i = 0; i < 8; ++i) a1[i] = pr[8 + i];
+        add8(a0);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) a1[i] = pr[8 * (b + 1) + i];
-          }
+        for (int i = 0; i < 8; ++i) a0[i] = pr[16 + i];
+        add8(a1);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            acc = __fadd_rn(acc, a0[i].x);
-            acc = __fadd_rn(acc, a0[i].y);
-            acc = __fadd_rn(acc, a0[i].z);
-            acc = __fadd_rn(acc, a0[i].w);
-          }
-          if (b + 2 < RT_CHUNK / 32) {
+        for (int i = 0; i < 8; ++i) a1[i] = pr[24 + i];
+        add8(a0);
+        // the next chunk's first batch, when its products are already known to be written
+        pre = (c + 1 < nchunk) && (c + 1 < static_cast<int>(ready_seen));
+        if (pre) {
+          const float4* pn = reinterpret_cast<const float4*>(pcur);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) a0[i] = pr[8 * (b + 2) + i];
-          }
-          if (b + 1 < RT_CHUNK / 32) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              acc = __fadd_rn(acc, a1[i].x);
-              acc = __fadd_rn(acc, a1[i].y);
-              acc = __fadd_rn(acc, a1[i].z);
-              acc = __fadd_rn(acc, a1[i].w);
-            }
-          }
+          for (int i = 0; i < 8; ++i) a0[i] = pn[i];
         }
+        add8(a1);
         // (a short last chunk has zero products past its end; adding them leaves the sum unchanged)
         __syncwarp();
         if (lane == 0) st_release_cta_shared(&pdone[warp], static_cast<uint32_t>(c + 1));
