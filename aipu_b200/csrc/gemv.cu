@@ -72,10 +72,30 @@ __device__ __forceinline__ uint32_t imad_u32(uint32_t a, uint32_t b, uint32_t c)
 __device__ __forceinline__ float half_lo_f(uint32_t h2) { return __half2float(__ushort_as_half(h2 & 0xFFFFu)); }
 __device__ __forceinline__ float half_hi_f(uint32_t h2) { return __half2float(__ushort_as_half(h2 >> 16)); }
 
-__device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcol,
-                                         const uint32_t* sxcol, int sb, int t, float (&acc)[4]) {
-  const uint4 hg = *reinterpret_cast<const uint4*>(rg);
-  const uint4 h8 = *reinterpret_cast<const uint4*>(rg8);
+// Shared-memory operands addressed by 32-bit shared-window addresses (no 64-bit generic address
+// arithmetic per load). The loads are volatile so they stay behind the slot's mbarrier wait.
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_v1(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+
+// rg, rg8: shared addresses of the unit's bytes in rows g and g + 8; xcol: of the lane's activation
+// column; sxcol: of the column's sub-block sums (64 bytes per super-block)
+__device__ __forceinline__ void unit_q4k(uint32_t rg, uint32_t rg8, uint32_t xcol, uint32_t sxcol, int sb, int t,
+                                         float (&acc)[4]) {
+  const uint4 hg = lds_v4(rg);
+  const uint4 h8 = lds_v4(rg8);
   // 8 six-bit scales / mins per row, as packed bytes (get_scale_min_k4 for j = 0..7 at once)
   const uint32_t sc03g = hg.y & 0x3F3F3F3Fu, m03g = hg.z & 0x3F3F3F3Fu;
   const uint32_t sc47g = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
@@ -95,13 +115,13 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
   }
 
   float P[4] = {0.f, 0.f, 0.f, 0.f};
-  const uint8_t* xb = xcol + 2 * (sb * 256 + 8 * t);
+  const uint32_t xb = xcol + 2 * (sb * 256 + 8 * t);
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const uint2 qg = *reinterpret_cast<const uint2*>(rg + 16 + 32 * p + 8 * t);
-    const uint2 q8 = *reinterpret_cast<const uint2*>(rg8 + 16 + 32 * p + 8 * t);
-    const uint4 xl = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p));
-    const uint4 xh = *reinterpret_cast<const uint4*>(xb + 2 * (64 * p + 32));
+    const uint2 qg = lds_v2(rg + 16 + 32 * p + 8 * t);
+    const uint2 q8 = lds_v2(rg8 + 16 + 32 * p + 8 * t);
+    const uint4 xl = lds_v4(xb + 2 * (64 * p));
+    const uint4 xh = lds_v4(xb + 2 * (64 * p + 32));
     float Dlo[4] = {0.f, 0.f, 0.f, 0.f}, Dhi[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -133,7 +153,8 @@ __device__ __forceinline__ void unit_q4k(const uint8_t* rg, const uint8_t* rg8, 
     const uint32_t sel = (t & 1) ? 0x4342u : 0x4140u;
     const uint32_t mg = hsub2_u32(prmt((t < 2) ? m03g : m47g, 0x64u, sel), H2_1024);
     const uint32_t m8 = hsub2_u32(prmt((t < 2) ? m038 : m478, 0x64u, sel), H2_1024);
-    const uint32_t b0 = sxcol[sb * 16 + t], b1 = sxcol[sb * 16 + 4 + t], b2 = sxcol[sb * 16 + 8 + t];
+    const uint32_t sx = sxcol + 4 * (sb * 16 + t);
+    const uint32_t b0 = lds_v1(sx), b1 = lds_v1(sx + 16), b2 = lds_v1(sx + 32);
     const uint32_t am[4] = {mg, m8, mg, m8};
     mma_f16_16816(Cm, am, b0, b1);
     const uint32_t sgt = (t & 2) ? ((t & 1) ? sg[3] : sg[2]) : ((t & 1) ? sg[1] : sg[0]);
@@ -200,13 +221,22 @@ __device__ __forceinline__ void unit_q6k(const uint8_t* rg, const uint8_t* rg8, 
   }
 }
 
-// 4 bytes at a shared-memory address known to be 4-byte aligned (A4) or 2 mod 4 (two aligned words
-// and a byte permute).
+// 4 bytes at a shared address known to be 4-byte aligned (A4) or 2 mod 4 (two aligned words and a
+// byte permute).
 template <bool A4>
-__device__ __forceinline__ uint32_t lds4(const uint8_t* p) {
-  if (A4) return *reinterpret_cast<const uint32_t*>(p);
-  const uint32_t w0 = *reinterpret_cast<const uint32_t*>(p - 2), w1 = *reinterpret_cast<const uint32_t*>(p + 2);
-  return __byte_perm(w0, w1, 0x5432);
+__device__ __forceinline__ uint32_t lds4(uint32_t a) {
+  if (A4) return lds_v1(a);
+  return __byte_perm(lds_v1(a - 2), lds_v1(a + 2), 0x5432);
+}
+__device__ __forceinline__ int lds_s8(uint32_t a) {
+  int v;
+  asm volatile("ld.shared.s8 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
 }
 
 // Q6_K unit for up to 4 live columns (MP = 1, 2 or 4 columns padded to a power of two): the MMA's
@@ -214,16 +244,16 @@ __device__ __forceinline__ uint32_t lds4(const uint8_t* p) {
 // accumulate in 2 MP sets of fp32 accumulators and are scaled once per unit (one multiply-add per
 // accumulator instead of one per group). Lane (g, t) feeds B column g: column g % MP, group slot
 // g / MP (zeros for the MMAs of other slots). acc holds per-lane partial sums over groups until
-// q6k_fold combines the lanes at the end of a tile.
+// q6k_fold combines the lanes at the end of a tile. rg, rg8, xcolm: shared addresses.
 template <int MP, bool A4>
-__device__ __forceinline__ void unit_q6k_mp(const uint8_t* rg, const uint8_t* rg8, const uint8_t* xcolm, bool mok,
-                                            int gslot, int sb, int t, float (&acc)[4]) {
+__device__ __forceinline__ void unit_q6k_mp(uint32_t rg, uint32_t rg8, uint32_t xcolm, bool mok, int gslot, int sb,
+                                            int t, float (&acc)[4]) {
   constexpr int NGM = 8 / MP;    // groups per accumulator set
   constexpr int NSET = 16 / NGM;
   float D[NSET][4];
 #pragma unroll
   for (int i = 0; i < NSET; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0.f;
-  const uint8_t* xb = xcolm + 2 * (sb * 256 + 4 * t);
+  const uint32_t xb = xcolm + 2 * (sb * 256 + 4 * t);
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
 #pragma unroll
@@ -251,22 +281,20 @@ __device__ __forceinline__ void unit_q6k_mp(const uint8_t* rg, const uint8_t* rg
         a[2] = hsub2_u32(lop3_and_or(cg[qi] >> 8, 0x003F003Fu, H2_1024), H2_1056);
         a[3] = hsub2_u32(lop3_and_or(c8[qi] >> 8, 0x003F003Fu, H2_1024), H2_1056);
         uint2 xv = make_uint2(0, 0);
-        if (mok && gslot == grp % NGM) xv = *reinterpret_cast<const uint2*>(xb + 2 * (128 * hf + 32 * qi + 16 * lh));
+        if (mok && gslot == grp % NGM) xv = lds_v2(xb + 2 * (128 * hf + 32 * qi + 16 * lh));
         mma_f16_16816(D[grp / NGM], a, xv.x, xv.y);
       }
     }
   }
-  const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg + 208));
-  const float d8 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg8 + 208));
-  const int8_t* scg = reinterpret_cast<const int8_t*>(rg + 192);
-  const int8_t* sc8 = reinterpret_cast<const int8_t*>(rg8 + 192);
+  const float dg = f16_bits_to_f32(lds_u16(rg + 208));
+  const float d8 = f16_bits_to_f32(lds_u16(rg8 + 208));
 #pragma unroll
   for (int st = 0; st < NSET; ++st) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int gc = st * NGM + (2 * t + h) / MP;  // the group of this lane's output column 2t + h
-      acc[h] = fmaf(__fmul_rn(dg, static_cast<float>(scg[gc])), D[st][h], acc[h]);
-      acc[2 + h] = fmaf(__fmul_rn(d8, static_cast<float>(sc8[gc])), D[st][2 + h], acc[2 + h]);
+      acc[h] = fmaf(__fmul_rn(dg, static_cast<float>(lds_s8(rg + 192 + gc))), D[st][h], acc[h]);
+      acc[2 + h] = fmaf(__fmul_rn(d8, static_cast<float>(lds_s8(rg8 + 192 + gc))), D[st][2 + h], acc[2 + h]);
     }
   }
 }
@@ -769,20 +797,20 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
     auto do_unit = [&](const int i) {
       const int sb = ch.sb + i;
       if (WT == WT_Q4K) {
-        const uint32_t* sxcol = reinterpret_cast<const uint32_t*>(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
-        unit_q4k(rg + i * UB, r8 + i * UB, xcol, sxcol, sb, t, acc);
+        const uint32_t sxcol = smem_u32(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
+        unit_q4k(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcol), sxcol, sb, t, acc);
       } else if (WT == WT_Q6K) {
         // warp-uniform (lane 0's row; all rows share the offset when mp < 8)
         const bool a4 = __shfl_sync(0xffffffffu, ((reinterpret_cast<uintptr_t>(rg) + i * UB) & 3u) == 0u, 0);
         if (mp == 1) {
-          if (a4) unit_q6k_mp<1, true>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
-          else unit_q6k_mp<1, false>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+          if (a4) unit_q6k_mp<1, true>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcolm), mok, gslot, sb, t, acc);
+          else unit_q6k_mp<1, false>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcolm), mok, gslot, sb, t, acc);
         } else if (mp == 2) {
-          if (a4) unit_q6k_mp<2, true>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
-          else unit_q6k_mp<2, false>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+          if (a4) unit_q6k_mp<2, true>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcolm), mok, gslot, sb, t, acc);
+          else unit_q6k_mp<2, false>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcolm), mok, gslot, sb, t, acc);
         } else if (mp == 4) {
-          if (a4) unit_q6k_mp<4, true>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
-          else unit_q6k_mp<4, false>(rg + i * UB, r8 + i * UB, xcolm, mok, gslot, sb, t, acc);
+          if (a4) unit_q6k_mp<4, true>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcolm), mok, gslot, sb, t, acc);
+          else unit_q6k_mp<4, false>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcolm), mok, gslot, sb, t, acc);
         } else {
           unit_q6k(rg + i * UB, r8 + i * UB, xcol, colok, sb, t, acc);
         }
