@@ -21,7 +21,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
-from typing import Optional
+from typing import Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -160,3 +160,75 @@ class PeerExpertParallelMoE:
         if self._ep:
             L.lib().aipu_ep_destroy(self._ep)
             self._ep = None
+
+
+class DecodeStream:
+    """Full-depth expert-parallel decode: L MoE layers run back to back for this rank's M tokens, the
+    output of layer l feeding layer l + 1 (the MoE branch of every decoder block; the attention and
+    norms between blocks are outside this library's path).
+
+    ``layers``: one ShardedMoeWeights per layer (same hidden size, top-k and expert split on every
+    layer). ``exchange``: "peer" (one NVLink peer-memory exchange buffer shared by all layers, like
+    PeerExpertParallelMoE) or "nccl" (ExpertParallelMoE per layer). Every rank calls with the same M.
+    """
+
+    def __init__(self, layers: Sequence[ShardedMoeWeights], exchange: str = "peer", max_tokens: int = 8,
+                 group=None, ctx: Optional[ops.Context] = None, backend=None):
+        if not layers:
+            raise ValueError("a decode stream needs at least one layer")
+        H, T = layers[0].hidden, layers[0].topk
+        for S in layers:
+            if S.hidden != H or S.topk != T or S.n_experts_total != layers[0].n_experts_total \
+                    or S.expert_lo != layers[0].expert_lo or S.local.n_experts != layers[0].local.n_experts:
+                raise ValueError("all layers of a decode stream must share hidden size, top-k and expert split")
+        self.layers = list(layers)
+        self.exchange = exchange
+        self.hidden = H
+        self._bufs = {}
+        if exchange == "peer":
+            self._peer = PeerExpertParallelMoE(self.layers[0], max_tokens=max_tokens, group=group, ctx=ctx)
+            self._cs = []
+            for S in self.layers:
+                cs = S.local.cstruct()
+                cs.n_experts = S.local.n_experts
+                self._cs.append(cs)
+        elif exchange == "nccl":
+            self._peer = None
+            self._nccl = [ExpertParallelMoE(S, group=group, backend=backend) for S in self.layers]
+        else:
+            raise ValueError("exchange must be 'peer' or 'nccl'")
+
+    def _pingpong(self, x: torch.Tensor):
+        key = (x.shape[0], x.device)
+        if key not in self._bufs:
+            self._bufs[key] = [torch.empty((x.shape[0], self.hidden), dtype=torch.bfloat16, device=x.device)
+                               for _ in range(2)]
+        return self._bufs[key]
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.exchange == "nccl":
+            for layer in self._nccl:
+                x = layer(x)
+            if out is not None:
+                out.copy_(x)
+                return out
+            return x
+        if x.dtype != torch.bfloat16 or not x.is_cuda:
+            raise ValueError("tokens must be bf16 on the GPU")
+        M = x.shape[0]
+        bufs = self._pingpong(x)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        cur = x
+        for i, cs in enumerate(self._cs):
+            dst = out if (out is not None and i == len(self._cs) - 1) else bufs[i & 1]
+            if dst is cur:  # never write the tokens being read
+                dst = bufs[(i + 1) & 1]
+            L.check(L.lib().aipu_ep_moe_layer(self._peer._ep, ctypes.byref(cs), self.layers[i].expert_lo,
+                                              cur.data_ptr(), M, dst.data_ptr(), stream))
+            cur = dst
+        return cur
+
+    def close(self):
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None

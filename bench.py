@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--matrices", type=int, default=256, help="distinct weight matrices per step")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--stream-layers", type=int, default=75,
+                    help="layers of the full-depth expert-parallel decode stream (BASELINE config 5) at N > 1, "
+                         "capped by device memory; 0 skips it")
     return ap.parse_args()
 
 
@@ -145,8 +148,12 @@ def dist_setup(n_gpus):
     if world > 1:
         import torch.distributed as dist
 
+        import datetime
+
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # a rank that fails leaves the others blocked in their next collective until this expires
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=300))
     else:
         torch.cuda.set_device(0)
     return world, rank, local
@@ -394,6 +401,63 @@ def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
     return out
 
 
+def moe_decode_stream(world, rank, layers_req=75, M_list=(1, 4), reps=10):
+    """the full-depth decode weight stream, `layers_req` MoE layers (256 routed
+    experts + 1 shared each, hidden 6144, FFN 2048) with the routed experts sharded over the N ranks,
+    run back to back for M tokens per rank (each layer's output feeds the next), over the NVLink
+    peer exchange and over NCCL. The layer count is capped by free device memory (reported).
+    tokens/s = N * M / (max-over-ranks device time of one pass through all layers)."""
+    import torch
+    import torch.distributed as dist
+
+    from aipu_b200 import ep
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    H, Fd, E, T = 6144, 2048, 256, 8
+    n = E // world
+    expert_bytes = 2 * Fd * F.row_bytes(F.Q4_K, H) + H * F.row_bytes(F.Q6_K, Fd)
+    per_layer = (n + 1) * expert_bytes + H * E * 4 + E * 4
+    torch.cuda.empty_cache()
+    free = torch.cuda.mem_get_info(d)[0]
+    cap = torch.tensor([max(0, int((free - 8e9) // per_layer))], device=d, dtype=torch.int64)
+    dist.all_reduce(cap, op=dist.ReduceOp.MIN)
+    L = min(layers_req, int(cap.item()))
+    if L < 1:
+        return {"skipped": f"not enough device memory for one layer ({per_layer / 1e9:.1f} GB per layer per GPU)"}
+    g = torch.Generator(device=d)
+    layers = []
+    for l in range(L):
+        s0 = 100000 * (l + 1)
+        local = ops.MoeLayerWeights(
+            hidden=H, ffn=Fd, n_experts=n, topk=T, router_wtype=F.F32,
+            router_w=torch.randn((H, E), device=d, generator=g.manual_seed(s0 + 1)) * 0.02,
+            router_bias=torch.randn((E,), device=d, generator=g.manual_seed(s0 + 2)) * 0.01,
+            gate_w=F.random_rows_dev(F.Q4_K, n * Fd, H, seed=s0 + 11 + 100 * rank, device=d),
+            up_w=F.random_rows_dev(F.Q4_K, n * Fd, H, seed=s0 + 12 + 100 * rank, device=d),
+            down_w=F.random_rows_dev(F.Q6_K, n * H, Fd, seed=s0 + 13 + 100 * rank, device=d),
+            shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=s0 + 14, device=d),
+            shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=s0 + 15, device=d),
+            shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=s0 + 16, device=d))
+        layers.append(ep.ShardedMoeWeights(local, rank * n, E))
+    out = {"layers": L, "full_depth": L == 75, "experts_per_gpu": n,
+           "weights_gb_per_gpu": round(L * per_layer / 1e9, 1)}
+    for kind in ("peer", "nccl"):
+        stream = ep.DecodeStream(layers, exchange=kind, max_tokens=max(M_list),
+                                 backend=ep.CudaBackend(ops.Context(d)) if kind == "nccl" else None)
+        for M in M_list:
+            x = torch.randn((M, H), device=d, generator=g.manual_seed(7 + M + 31 * rank)).to(torch.bfloat16)
+            r = _time_ep_layer(stream, x, reps)
+            t = r["t"]
+            out[f"{kind}_M{M}"] = {"ms_per_pass": round(t * 1e3, 3), "us_per_layer": round(t / L * 1e6, 2),
+                                   "tokens_per_s": round(world * M / t, 1), "cuda_graph": r["graphed"]}
+        stream.close()
+    del layers
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -503,8 +567,14 @@ def main():
     if rank == 0 and world == 1 and not args.no_moe:
         moe = moe_decode()
     moe_ep = None
+    moe_stream = None
     if world > 1 and not args.no_moe:
         moe_ep = moe_decode_ep(world, rank)
+        if args.stream_layers > 0:
+            try:
+                moe_stream = moe_decode_stream(world, rank, args.stream_layers)
+            except Exception as e:  # reported in the line; the GEMV metric above stands
+                moe_stream = {"error": f"{type(e).__name__}: {e}"[:300]}
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu_base = cpu_baseline_gemv()
@@ -525,6 +595,7 @@ def main():
             "single_launch": single,
             "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,
             "clocks": clk.summary(), "moe_decode": moe, "moe_decode_ep": moe_ep,
+            "moe_decode_stream": moe_stream,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

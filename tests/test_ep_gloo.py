@@ -124,3 +124,50 @@ def test_expert_parallel_two_gloo_ranks_match_one_process_layer():
     for r in range(2):
         ref, _, _ = mo.moe_layer(xs[r], wr_t, deq, shared, T, bias=W.router_bias.numpy())
         assert np.array_equal(got[r].view(np.uint32), ref.view(np.uint32)), f"rank {r}"
+
+
+def _stream_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        Ws = [_weights(7 + 10 * l)[0] for l in range(3)]
+        _, xs = _weights(7)
+        stream = ep.DecodeStream([ep.shard(W, rank, world) for W in Ws], exchange="nccl", backend=OracleBackend())
+        out = stream(_bf16_t(xs[rank]))
+        q.put((rank, _np(out)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_decode_stream_two_gloo_ranks_three_layers():
+    """Three expert-parallel layers back to back (each layer's output is the next one's input)
+    equal the one-process oracle layers applied in turn."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_stream_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    Ws = [_weights(7 + 10 * l)[0] for l in range(3)]
+    _, xs = _weights(7)
+    for r in range(2):
+        x = xs[r]
+        for W in Ws:
+            wr_t = W.router_w.numpy().view(F32).reshape(H, E).T.copy()
+            gv, uv, dv = (W.gate_w.numpy().reshape(E, FD, -1), W.up_w.numpy().reshape(E, FD, -1),
+                          W.down_w.numpy().reshape(E, H, -1))
+
+            def deq(e, gv=gv, uv=uv, dv=dv):
+                return (qo.dequant_rows(F.Q4_K, gv[e], FD, H), qo.dequant_rows(F.Q4_K, uv[e], FD, H),
+                        qo.dequant_rows(F.Q6_K, dv[e], H, FD))
+
+            shared = (qo.dequant_rows(F.Q4_K, W.shared_gate_w.numpy(), FD, H),
+                      qo.dequant_rows(F.Q4_K, W.shared_up_w.numpy(), FD, H),
+                      qo.dequant_rows(F.Q6_K, W.shared_down_w.numpy(), H, FD))
+            x, _, _ = mo.moe_layer(x, wr_t, deq, shared, T, bias=W.router_bias.numpy())
+        assert np.array_equal(got[r].view(np.uint32), x.view(np.uint32)), f"rank {r}"

@@ -201,3 +201,56 @@ def test_expert_parallel_two_gpus_peer_memory():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert res == {0: {"strict": True, "fast": True}, 1: {"strict": True, "fast": True}}
+
+
+def _stream_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from aipu_b200 import ep
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    res = {}
+    try:
+        d = torch.device("cuda", rank)
+        Ws = [_layer(d, 512, 256, 16, 4, seed=300 + 10 * l) for l in range(3)]
+        ctx = ops.Context(d).set_flags(strict=True)
+        rng = np.random.default_rng(4000 + rank)
+        x = torch.from_numpy(qo.bf16_round(rng.standard_normal((2, 512)).astype(F32))).to(d).to(torch.bfloat16)
+        ref = x
+        for W in Ws:
+            ref = ops.moe_layer(W, ref, ctx=ctx)
+        for kind in ("peer", "nccl"):
+            stream = ep.DecodeStream([ep.shard(W, rank, world) for W in Ws], exchange=kind, max_tokens=2, ctx=ctx,
+                                     backend=ep.CudaBackend(ctx))
+            out = stream(x)
+            out2 = stream(x)  # a second call through the same exchange state
+            torch.cuda.synchronize()
+            res[kind] = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))) and \
+                bool(torch.equal(out2.view(torch.int16), ref.view(torch.int16)))
+            stream.close()
+        res["status"] = ctx.status()
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_decode_stream_two_gpus_strict():
+    """Three expert-parallel layers back to back, over the peer exchange and over NCCL, equal the
+    one-GPU layers applied in turn (strict mode, bit for bit), on two successive calls."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_stream_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res == {0: {"peer": True, "nccl": True, "status": 0}, 1: {"peer": True, "nccl": True, "status": 0}}
