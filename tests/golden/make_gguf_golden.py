@@ -17,7 +17,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("AIPU_REFERENCE", "/root/reference")
+REF = os.environ.get("AIPU_REFERENCE")
+if not REF:
+    sys.exit("set AIPU_REFERENCE to the root of the Wick-Lim/AIPU tree")
 sys.path.insert(0, os.path.join(REF, "tools"))
 
 import ckpt_pack_q4k as CP  # noqa: E402  (reference module, unchanged)
