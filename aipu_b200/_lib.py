@@ -59,6 +59,7 @@ SIGNATURES = {
                                       c_void_p]),
     "aipu_q4k_gemm_tc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                                  c_void_p]),
+    "aipu_bf16_dot_gemv": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p]),
     "aipu_q4k_gemm_grouped": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
                                       c_int, c_int64, c_void_p, c_void_p]),
     "aipu_moe_router": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaipu_q4k.so")
 
-SOURCES = ["capi.cu", "ep.cu", "gemv.cu", "kernels.cu", "tc_gemm.cu"]
+SOURCES = ["capi.cu", "ep.cu", "gemv.cu", "kernels.cu", "lmhead.cu", "tc_gemm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # No --use_fast_math and no -ftz: the exact kernels depend on IEEE fp32 with subnormals.
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",

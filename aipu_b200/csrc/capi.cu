@@ -976,6 +976,15 @@ extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt,
   return rc;
 }
 
+extern "C" int aipu_bf16_dot_gemv(aipu_ctx* c, const void* w, int64_t V, int64_t K, const void* x, int64_t M,
+                                  void* y, void* stream) {
+  if (!c || !w || !x || !y || V <= 0 || K <= 0 || M <= 0) return set_error(EINVAL_, "bf16_dot_gemv: bad arguments");
+  DeviceGuard dg(c->device);
+  return bf16_dot7_launch(static_cast<const uint16_t*>(w), V, K, static_cast<const uint16_t*>(x), M,
+                          static_cast<uint16_t*>(y), c->num_sms, static_cast<cudaStream_t>(stream),
+                          (c->flags & AIPU_FLAG_PDL) != 0);
+}
+
 extern "C" int aipu_q4k_gemm_tc(aipu_ctx* c, int wtype, const void* w, int64_t N, int64_t K, const void* x, int64_t M,
                                 void* y, void* stream) {
   if (!c || !w || !x || !y || N <= 0 || M <= 0 || K <= 0 || K % 256 || (wtype != AIPU_Q4_K && wtype != AIPU_Q6_K) ||

@@ -140,6 +140,9 @@ int swiglu_elem_launch(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t
 int strict_gemm_launch(int wt, const void* w, int N, int K, const void* x, int xt, int M, uint16_t* y, float* y_f32,
                        cudaStream_t s);
 int router_launch(const RouterParams& p, cudaStream_t s, bool pdl);
+// bf16 GEMV under the reference's bf16 dot contract (lmhead.cu): y[m, v] = dot7(x[m], w[v])
+int bf16_dot7_launch(const uint16_t* w, int64_t V, int64_t K, const uint16_t* x, int64_t M, uint16_t* y, int num_sms,
+                     cudaStream_t s, bool pdl);
 int router_grid_ctas(const RouterParams& p);  // CTAs of the launch router_launch makes
 int router_smem_bytes(const RouterParams& p); // its dynamic shared memory per CTA
 int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl);

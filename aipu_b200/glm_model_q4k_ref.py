@@ -139,6 +139,18 @@ def matmul_q4k(a_row, wdeq_cols):
     return [F32(v) for v in _bf16_host(y)[0]]
 
 
+def matmul_bf16_dot(a_bf, w_bf):
+    """One bf16 dot product under the reference's 7-partial-sum contract
+    (tools/glm_model_q4k_ref.py:474-486) on the GPU. Both vectors are zero padded to a multiple of 8
+    (the padding adds +0 products, which leave every partial sum unchanged: a sum that starts at +0
+    never becomes -0 under round-to-nearest)."""
+    K = len(a_bf)
+    kp = (K + 7) // 8 * 8
+    x = _bf16_dev(list(np.asarray(a_bf, F32).reshape(-1)), kp).view(1, kp)
+    w = _bf16_dev(list(np.asarray(w_bf, F32).reshape(-1)), kp).view(1, kp)
+    return F32(_bf16_host(ops.bf16_dot_gemv(w, x))[0, 0])
+
+
 # ---------------------------------------------------------------- Q4_K weight container
 class QW:
     """Q4_K weight matrix: NOUT output columns x NIN reduction (tools/glm_model_q4k_ref.py:491-519),

@@ -137,6 +137,23 @@ def gemm_tc(wtype: int, w: torch.Tensor, N: int, K: int, x: torch.Tensor, ctx: O
     return out
 
 
+def bf16_dot_gemv(w: torch.Tensor, x: torch.Tensor, ctx: Optional[Context] = None,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LM-head style GEMV: y[M, V] bf16 = the reference's bf16 dot (7 interleaved fp32 partial sums
+    and a fixed add tree) of every token row x[M, K] with every weight row w[V, K] (both bf16)."""
+    _need_cuda(w, x, out)
+    if w.dtype != torch.bfloat16 or x.dtype != torch.bfloat16 or w.dim() != 2 or x.dim() != 2 or x.shape[1] != w.shape[1]:
+        raise ValueError("w [V, K] and x [M, K] must be bf16 with the same K")
+    ctx = ctx or Context.default(w.device)
+    w, x = w.contiguous(), x.contiguous()  # held until the launch is queued
+    V, K = w.shape
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, V), dtype=torch.bfloat16, device=w.device)
+    check(lib().aipu_bf16_dot_gemv(ctx.handle, _ptr(w), V, K, _ptr(x), M, _ptr(out), _stream(w.device)))
+    return out
+
+
 def gemm_grouped(wtype: int, w: torch.Tensor, n_mats: int, N: int, K: int, x: torch.Tensor,
                  mat_stride: Optional[int] = None, ctx: Optional[Context] = None,
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -122,6 +122,14 @@ int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_t K, const 
 int aipu_q4k_gemm_tc(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K, const void* x, int64_t M, void* y,
                      void* stream);
 
+/* bf16 GEMV under the reference's bf16 dot-product contract (the LM head): y[m, v] (bf16) =
+ * bf16((fl(p0 + p1) + fl(p2 + p3)) + (fl(p4 + p5) + fl(p6 + 0))) where p_l is the sequential fp32 sum
+ * of fl(x[m, k] * w[v, k]) over k = l, l + 7, ... (bit-exact). w: V rows of K bf16 (16-byte
+ * aligned, K % 8 == 0, K <= 14336); x: M rows of K bf16; y: [M, V] bf16.
+ * Replaces: tools/glm_model_q4k_ref.py:474-486 matmul_bf16_dot (LM head use at :826). */
+int aipu_bf16_dot_gemv(aipu_ctx* ctx, const void* w, int64_t V, int64_t K, const void* x, int64_t M, void* y,
+                       void* stream);
+
 /* Grouped fast GEMM: n_mats independent matrices of N rows x K (matrix g at w + g * mat_stride
  * bytes) applied to the same activations x[M, K] in ONE launch; y[g, M, N] (bf16). This is the
  * decode pattern of several projections or experts fed by the same token rows (e.g. all experts of

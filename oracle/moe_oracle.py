@@ -12,6 +12,7 @@ Restates, vectorised with numpy, the reference's numpy golden of the MoE branch
   * _sum_tree balanced fp32 add tree                          glm_model_q4k_ref.py:691-699
   * swiglu_expert                                              glm_model_q4k_ref.py:702-708
   * MoE combine inside decoder_block (slot order, then shared) glm_model_q4k_ref.py:797-809
+  * matmul_bf16_dot (7 interleaved partial sums + add tree)   glm_model_q4k_ref.py:474-486
 
 Router extension (not in the reference): a dense fp32 router W_r [K, E] plus a per-expert fp32
 bias. Logits follow the same sequential fp32 MAC contract (fp32 weights instead of dequantised
@@ -260,3 +261,19 @@ def moe_layer(x_bf, wr_t, experts_deq, shared_deq, topk: int, bias=None, scale=R
             mag += swiglu_magnitude(h, wd)
     out = combine(sel_w, y_slots, y_sh)
     return (out, sel, sel_w, mag) if want_mag else (out, sel, sel_w)
+
+
+def bf16_dot7(x_bf: np.ndarray, w_bf: np.ndarray) -> np.ndarray:
+    """matmul_bf16_dot (glm_model_q4k_ref.py:474-486) for every (token, row): x_bf [M, K], w_bf [V, K]
+    bf16-valued fp32 -> bf16-valued fp32 [M, V]. Partial sum l (0..6) adds fl(x_k * w_k) for
+    k = l, l + 7, ... in order; then a01 = p0 + p1, a23 = p2 + p3, a45 = p4 + p5, a6 = p6 + 0,
+    b0 = a01 + a23, b1 = a45 + a6, out = bf16(b0 + b1)."""
+    x = np.asarray(x_bf, F32)
+    w = np.asarray(w_bf, F32)
+    M, K = x.shape
+    ps = np.zeros((7, M, w.shape[0]), F32)
+    for k in range(K):
+        ps[k % 7] = ps[k % 7] + x[:, k:k + 1] * w[None, :, k]
+    z = F32(0.0)
+    a01, a23, a45, a6 = ps[0] + ps[1], ps[2] + ps[3], ps[4] + ps[5], ps[6] + z
+    return qo.bf16_round((a01 + a23) + (a45 + a6))

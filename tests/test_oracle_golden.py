@@ -157,3 +157,13 @@ def test_c_oracle_dequant_edge_blocks(golden):
         assert np.array_equal(bits(y), g[f"{name}_y"])
     y = cpu.dequant_row(3, g["f16_bits"].view(np.uint8), g["f16_bits"].size)
     assert np.array_equal(bits(y), g["f16_y"])
+
+
+def test_bf16_dot7_oracle_matches_reference_fixture(golden):
+    """The vectorised bf16 dot (LM-head contract) equals the reference's matmul_bf16_dot."""
+    g = golden("lmhead_golden")
+    for c in ("a", "b", "c"):
+        x = (g[f"{c}_x"].astype(np.uint32) << 16).view(np.float32)
+        w = (g[f"{c}_w"].astype(np.uint32) << 16).view(np.float32)
+        y = mo.bf16_dot7(x, w)
+        assert np.array_equal((y.view(np.uint32) >> 16).astype(np.uint16), g[f"{c}_y"]), c
