@@ -171,3 +171,13 @@ def test_decode_stream_two_gloo_ranks_three_layers():
                       qo.dequant_rows(F.Q6_K, W.shared_down_w.numpy(), H, FD))
             x, _, _ = mo.moe_layer(x, wr_t, deq, shared, T, bias=W.router_bias.numpy())
         assert np.array_equal(got[r].view(np.uint32), x.view(np.uint32)), f"rank {r}"
+
+
+def test_decode_stream_rejects_mismatched_layers():
+    W1, _ = _weights(7)
+    W2, _ = _weights(8)
+    W2.topk = 1
+    with pytest.raises(ValueError):
+        ep.DecodeStream([ep.shard(W1, 0, 2), ep.shard(W2, 0, 2)], exchange="nccl")
+    with pytest.raises(ValueError):
+        ep.DecodeStream([], exchange="nccl")
