@@ -405,7 +405,8 @@ def moe_decode_stream(world, rank, layers_req=75, M_list=(1, 4), reps=10):
     """the full-depth decode weight stream, `layers_req` MoE layers (256 routed
     experts + 1 shared each, hidden 6144, FFN 2048) with the routed experts sharded over the N ranks,
     run back to back for M tokens per rank (each layer's output feeds the next), over the NVLink
-    peer exchange and over NCCL. The layer count is capped by free device memory (reported).
+    peer exchange and over NCCL. The layer count is capped by free device memory and by ~64 GB of
+    weights per GPU (75 layers fit at N = 8; fewer at N < 8, reported).
     tokens/s = N * M / (max-over-ranks device time of one pass through all layers)."""
     import torch
     import torch.distributed as dist
@@ -423,7 +424,8 @@ def moe_decode_stream(world, rank, layers_req=75, M_list=(1, 4), reps=10):
     free = torch.cuda.mem_get_info(d)[0]
     cap = torch.tensor([max(0, int((free - 8e9) // per_layer))], device=d, dtype=torch.int64)
     dist.all_reduce(cap, op=dist.ReduceOp.MIN)
-    L = min(layers_req, int(cap.item()))
+    # at most ~64 GB of weights per GPU (the config-5 share at N = 8), so every N takes similar time
+    L = min(layers_req, int(cap.item()), int(64e9 // per_layer))
     if L < 1:
         return {"skipped": f"not enough device memory for one layer ({per_layer / 1e9:.1f} GB per layer per GPU)"}
     g = torch.Generator(device=d)
