@@ -402,7 +402,8 @@ def test_moe_layer_reference_fixture_strict(golden):
     assert np.array_equal(bf16_np(y).view(np.uint32), g["moe_y"])
 
 
-@pytest.mark.parametrize("M,H,Fd,E", [(1, 6144, 2048, 256), (4, 6144, 2048, 256), (70, 512, 256, 16)])
+@pytest.mark.parametrize("M,H,Fd,E", [(1, 6144, 2048, 256), (4, 6144, 2048, 256), (5, 6144, 2048, 256),
+                                      (70, 512, 256, 16)])
 def test_moe_layer_config3_strict_bitexact(M, H, Fd, E):
     """Strict mode at BASELINE config-3 dims (and 70 tokens, past the tensor-core threshold, at
     reduced dims): outputs bit-identical to the oracle's sequential restatement of the reference."""
