@@ -47,3 +47,12 @@ def test_errors_do_not_need_a_gpu():
     assert b"bad arguments" in L.aipu_last_error()
     with pytest.raises(_lib.AipuError):
         _lib.check(rc)
+
+
+def test_argument_errors_of_newer_entry_points_do_not_need_a_gpu():
+    """Null contexts and bad shapes are rejected before any device work, with a message."""
+    L = _lib.lib()
+    assert L.aipu_bf16_dot_gemv(None, None, 16, 64, None, 1, None, None) == _lib.AIPU_EINVAL
+    assert b"bf16_dot_gemv" in L.aipu_last_error()
+    assert L.aipu_moe_layer(None, None, None, 1, None, None, None, None) == _lib.AIPU_EINVAL
+    assert L.aipu_ep_moe_layer(None, None, 0, None, 1, None, None) != 0
