@@ -132,3 +132,18 @@ def test_dropin_swiglu_expert_fixture(golden):
             Wdown = _qw_from_rows(g["moe_down_w"][e][:D], Fd)
             y = G.swiglu_expert(cfg, x, Wgate, Wup, Wdown)
             assert np.array_equal(np.array(y, F32).view(np.uint32), g["moe_yslots"][t, idx])
+
+
+@pytest.mark.gpu
+def test_dropin_matmul_bf16_dot_fixture(golden):
+    """matmul_bf16_dot(a_bf, w_bf) as the reference calls it (LM head), against its own outputs."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    g = golden("lmhead_golden")
+    for c in ("b", "c"):
+        x = (g[f"{c}_x"].astype(np.uint32) << 16).view(F32)
+        w = (g[f"{c}_w"].astype(np.uint32) << 16).view(F32)
+        y = (g[f"{c}_y"].astype(np.uint32) << 16).view(F32)
+        for v in range(min(4, w.shape[0])):
+            got = G.matmul_bf16_dot(list(x[0]), list(w[v]))
+            assert np.float32(got).view(np.uint32) == y[0, v].view(np.uint32), (c, v)
