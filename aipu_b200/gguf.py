@@ -263,6 +263,26 @@ def write_gguf(path: str, tensors: Sequence[TensorSpec], metadata: Optional[Dict
         f.write(bytes(blob))
 
 
+# -------------------------------------------------------------------- matrices
+@dataclass
+class Matrix:
+    """A 2-D GGUF weight on the device as the GEMV consumes it: N rows of K weights of `wtype`."""
+    wtype: int
+    N: int
+    K: int
+    rows: object  # torch uint8 [N, row bytes]
+
+
+def load_matrix(gf: GGUFFile, name: str, device) -> Matrix:
+    """A 2-D tensor (ne = [K, N]) for ops.gemm / ops.gemm_grouped: e.g. the attention projections
+    blk.{i}.attn_{q_a,q_b,kv_a_mqa,kv_b,output}.weight, whatever their per-tensor type."""
+    t = gf.info(name)
+    if len(t.ne) != 2:
+        raise GGUFError(f"{name}: expected a 2-D tensor, got ne = {list(t.ne)}")
+    K, N = t.ne
+    return Matrix(t.wtype, N, K, gf.to_device(name, device))
+
+
 # -------------------------------------------------------------------- MoE layers
 def moe_names(layer: int) -> Dict[str, str]:
     b = f"blk.{layer}."

@@ -96,3 +96,13 @@ def test_moe_layer_loads_with_kernel_layouts(tmp_path):
         assert W.shared_down_w.shape == (H, F.row_bytes(F.Q6_K, Fd)) and W.router_bias.shape == (E,)
         with pytest.raises(KeyError):
             gguf.load_moe_layer(gf, 2, "cpu")
+
+
+def test_load_matrix_keeps_rows_and_type():
+    with gguf.GGUFFile(os.path.join(GOLDEN, "ref_synthetic.gguf")) as gf:
+        m = gguf.load_matrix(gf, "blk.0.ffn_down.weight", "cpu")
+        assert (m.wtype, m.N, m.K) == (F.Q4_K, 8, 512)
+        assert m.rows.shape == (8, F.row_bytes(F.Q4_K, 512))
+        assert np.array_equal(m.rows.numpy(), np.array(gf.raw("blk.0.ffn_down.weight")))
+        with pytest.raises(gguf.GGUFError):
+            gguf.load_matrix(gf, "blk.0.attn_norm.weight", "cpu")
