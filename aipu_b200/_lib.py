@@ -18,6 +18,7 @@ DT_F32, DT_BF16 = 0, 1
 MODE_FAST, MODE_STRICT = 0, 1
 FLAG_PDL = 1
 FLAG_STRICT = 2
+FLAG_TC_DECODE = 4
 
 c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 
@@ -57,6 +58,7 @@ SIGNATURES = {
                               c_void_p, c_int, c_void_p]),
     "aipu_q4k_gemm_noalloc": (c_int, [c_int, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p,
                                       c_void_p]),
+    "aipu_q4k_gemm_noalloc_status": (c_int, [ctypes.POINTER(c_int)]),
     "aipu_q4k_gemm_tc": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                                  c_void_p]),
     "aipu_bf16_dot_gemv": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p]),

@@ -15,9 +15,12 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaipu_q4k.so")
 
-SOURCES = ["capi.cu", "ep.cu", "gemv.cu", "kernels.cu", "lmhead.cu", "tc_gemm.cu"]
+SOURCES = ["capi.cu", "chain.cu", "ep.cu", "gemv.cu", "kernels.cu", "lmhead.cu", "tc_gemm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # No --use_fast_math and no -ftz: the exact kernels depend on IEEE fp32 with subnormals.
+# Per-file flags. chain.cu: its packed fp32 products and sums must round separately (the reference's
+# contract), and ptxas would otherwise contract a packed multiply and add into a packed fma.
+FILE_FLAGS = {"chain.cu": ["-fmad=false"]}
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
 
@@ -42,16 +45,22 @@ def build(verbose: bool = False, force: bool = False, extra: list[str] | None = 
     os.makedirs(objdir, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     headers.append(os.path.join(ROOT, "include", "aipu_q4k.h"))
-    objs = []
+    objs, jobs = [], []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
         o = os.path.join(objdir, src.replace(".cu", ".o"))
         objs.append(o)
         if force or _stale(o, [s] + headers):
-            cmd = [nvcc()] + ARCH + FLAGS + (extra or []) + ["-c", s, "-o", o]
-            if verbose:
-                print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+            jobs.append([nvcc()] + ARCH + FLAGS + FILE_FLAGS.get(src, []) + (extra or []) + ["-c", s, "-o", o])
+    # the translation units are independent: compile them concurrently
+    procs = []
+    for cmd in jobs:
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        procs.append((cmd, subprocess.Popen(cmd)))
+    failed = [cmd for cmd, pr in procs if pr.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     if force or _stale(LIB, objs):
         cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs
         if verbose:

@@ -64,6 +64,18 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const vo
   return OK;
 }
 
+int set_smem_attr_once(const void* kern, int bytes, bool* done, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, what);
+  if (dev < 0 || dev >= 64) return set_error(EINVAL_, "device index out of range (at most 64 devices)");
+  if (done[dev]) return OK;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return set_cuda_error(e, what);
+  done[dev] = true;
+  return OK;
+}
+
 int num_sms_of_current_device() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
@@ -80,6 +92,8 @@ struct Workspace {
   float* partials = nullptr;
   int* counters = nullptr;
   int max_tiles = 0;
+  void* aux = nullptr;  // strict SwiGLU up-projection rows (grown on demand)
+  size_t aux_bytes = 0;
 };
 
 struct aipu_ctx {
@@ -99,6 +113,8 @@ struct aipu_ctx {
   size_t pre_bytes = 0;
   void* rt = nullptr;     // router outputs of the many-token path
   size_t rt_bytes = 0;
+  void* tmp = nullptr;    // gate rows of aipu_moe_router / h rows of aipu_swiglu_expert when the caller passes none
+  size_t tmp_bytes = 0;
 };
 
 static int grow(void** buf, size_t* have, size_t need, const char* what) {
@@ -184,7 +200,9 @@ int aipu_ctx_destroy(aipu_ctx* c) {
   for (auto& w : c->ws) {
     cudaFree(w.partials);
     cudaFree(w.counters);
+    cudaFree(w.aux);
   }
+  cudaFree(c->tmp);
   cudaFree(c->status);
   cudaFree(c->router_counters);
   cudaFree(c->moe);
@@ -198,7 +216,7 @@ int aipu_ctx_destroy(aipu_ctx* c) {
 }
 
 int aipu_ctx_set_flags(aipu_ctx* c, int flags) {
-  if (!c || (flags & ~(AIPU_FLAG_PDL | AIPU_FLAG_STRICT))) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
+  if (!c || (flags & ~(AIPU_FLAG_PDL | AIPU_FLAG_STRICT | AIPU_FLAG_TC_DECODE))) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
   c->flags = flags;
   return OK;
 }
@@ -262,6 +280,22 @@ extern "C" int aipu_q4k_gemm(aipu_ctx* c, int wtype, const void* w, int64_t N, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int xt = x_dtype == AIPU_DT_F32 ? XT_F32 : XT_BF16;
   if (mode == AIPU_MODE_STRICT || wtype == AIPU_F32 || y_f32) {
+    if (wtype != AIPU_F32 && chain_supported(wtype, K, row_bytes_of(wtype, K))) {
+      ChainParams p = {};
+      p.w0 = static_cast<const uint8_t*>(w);
+      p.row_bytes = row_bytes_of(wtype, K);
+      p.n_groups = 1;
+      p.N = static_cast<int>(N);
+      p.K = static_cast<int>(K);
+      p.x = x;
+      p.x_f32 = (xt == XT_F32) ? 1 : 0;
+      p.M = static_cast<int>(std::min<int64_t>(M, INT32_MAX));
+      p.y = static_cast<uint16_t*>(y);
+      p.y_f32 = y_f32;
+      p.status = c->status;
+      const int rc = chain_launch(wtype, CHAIN_STORE, p, c->num_sms, s, (c->flags & AIPU_FLAG_PDL) != 0);
+      if (rc != CHAIN_UNSUPPORTED) return rc;
+    }
     return strict_gemm_launch(wtype, w, static_cast<int>(N), static_cast<int>(K), x, xt, static_cast<int>(M),
                               static_cast<uint16_t*>(y), y_f32, s);
   }
@@ -315,11 +349,11 @@ extern "C" int aipu_moe_router(aipu_ctx* c, int wt, const void* w, const float* 
   DeviceGuard dg(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint16_t* gbuf = static_cast<uint16_t*>(gate);
-  uint16_t* tmp = nullptr;
   if (!gbuf) {
-    if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), sizeof(uint16_t) * M * E, s) != cudaSuccess)
-      return set_error(ENOMEM_, "router: gate scratch");
-    gbuf = tmp;
+    // context workspace, grown on demand (make a first call before capturing a CUDA graph)
+    const int grc = grow(&c->tmp, &c->tmp_bytes, sizeof(uint16_t) * M * E, "router: gate scratch");
+    if (grc) return grc;
+    gbuf = static_cast<uint16_t*>(c->tmp);
   }
   RouterParams p = {};
   p.wt = wt;
@@ -337,9 +371,7 @@ extern "C" int aipu_moe_router(aipu_ctx* c, int wt, const void* w, const float* 
   p.sel_w = static_cast<uint16_t*>(sel_w);
   p.counters = c->router_counters;
   p.status = c->status;
-  int rc = router_launch(p, s, false);
-  if (tmp) cudaFreeAsync(tmp, s);
-  return rc;
+  return router_launch(p, s, false);
 }
 
 // ------------------------------------------------------------------ MoE decode layer
@@ -396,18 +428,61 @@ static const int kSmemPerSm = 233472;
 
 static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, const void* uw, int dwt, const void* dw,
                          int64_t H, int64_t F, int n_experts, const int* group_ids, const int* n_groups_dev,
-                         int n_groups,
+                         int n_groups, const int32_t* slot_map, int topk,
                          const void* x, int64_t M, uint16_t* h, uint16_t* y, cudaStream_t s, bool pdl,
                          int num_sms = 0, int min_smem = 0) {
   if (num_sms <= 0) num_sms = c->num_sms;
   const int64_t gstride = F * row_bytes_of(gwt, H), dstride = H * row_bytes_of(dwt, F);
+  if (!(c->flags & AIPU_FLAG_TC_DECODE) && chain_supported(gwt, H, row_bytes_of(gwt, H)) &&
+      chain_supported(dwt, F, row_bytes_of(dwt, F)) && gwt == WT_Q4K && (!slot_map || M <= 32)) {
+    // the bit-exact sequential chains (tools/glm_model_q4k_ref.py:702-708 op for op), each expert on
+    // the tokens that selected it: gate/up with the SwiGLU product fused, then the down projection
+    ChainParams g = {};
+    g.w0 = static_cast<const uint8_t*>(gw);
+    g.w1 = static_cast<const uint8_t*>(uw);
+    g.row_bytes = row_bytes_of(gwt, H);
+    g.expert_stride = gstride;
+    g.group_ids = group_ids;
+    g.n_groups_dev = n_groups_dev;
+    g.n_groups = n_groups;
+    g.n_experts = n_experts;
+    g.N = static_cast<int>(F);
+    g.K = static_cast<int>(H);
+    g.x = static_cast<const uint16_t*>(x);
+    g.x_group_stride = 0;
+    g.M = static_cast<int>(M);
+    g.slot_map = slot_map;
+    g.topk = topk;
+    g.y = h;
+    g.y_group_stride = M * F;
+    g.status = c->status;
+    int rc = chain_launch(gwt, CHAIN_SWIGLU, g, num_sms, s, pdl);
+    if (rc == OK) {
+      ChainParams d = g;
+      d.w0 = static_cast<const uint8_t*>(dw);
+      d.w1 = nullptr;
+      d.row_bytes = row_bytes_of(dwt, F);
+      d.expert_stride = dstride;
+      d.N = static_cast<int>(H);
+      d.K = static_cast<int>(F);
+      d.x = h;
+      d.x_group_stride = M * F;
+      d.y = y;
+      d.y_group_stride = M * H;
+      rc = chain_launch(dwt, CHAIN_STORE, d, num_sms, s, true);
+      if (rc == CHAIN_UNSUPPORTED) rc = set_error(EINVAL_, "swiglu: down projection not supported by the chain kernel");
+      return rc;
+    }
+    if (rc != CHAIN_UNSUPPORTED) return rc;
+  }
   if (c->flags & AIPU_FLAG_STRICT) {
     // bit-exact chains (tools/glm_model_q4k_ref.py:702-708): gate into h, up into a temporary,
     // h = bf16(silu(gate) * up) in place, then the down projection of h
     const int64_t n = static_cast<int64_t>(n_groups) * M * F;
-    uint16_t* up = nullptr;
-    if (cudaMallocAsync(reinterpret_cast<void**>(&up), 2 * n, s) != cudaSuccess)
-      return set_error(ENOMEM_, "swiglu (strict): scratch");
+    // up-projection rows in the workspace of this stream (grown on demand, before any capture)
+    const int grc = grow(&ws.aux, &ws.aux_bytes, 2 * n, "swiglu (strict): scratch");
+    if (grc) return grc;
+    uint16_t* up = static_cast<uint16_t*>(ws.aux);
     StrictParams p = {};
     p.wt = gwt;
     p.w = static_cast<const uint8_t*>(gw);
@@ -441,7 +516,6 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
       q.y_group_stride = M * H;
       rc = strict_gemm_grouped_launch(q, n_groups, s);
     }
-    cudaFreeAsync(up, s);
     return rc;
   }
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
@@ -656,6 +730,169 @@ static int moe_prefill(aipu_ctx* c, const aipu_moe_weights* W, const void* x, in
   return rc;
 }
 
+// Many-token MoE experts, bit-exact: the tokens of every local expert (perm_kernel lists, 8 tokens per
+// tile) run through the chain kernel -- gate/up with the SwiGLU product, then down, rows by position --
+// and the shared expert over tokens [shared_t0, shared_t0 + shared_n) as dense chains. Outputs (in
+// c->pre): y_perm rows by position, pos_of[M * T] (-1: expert not local), y_sh [shared_n, H].
+struct ExactExperts {
+  uint16_t* y_perm;
+  int32_t* pos_of;
+  uint16_t* y_sh;
+};
+static int moe_experts_exact(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, const int32_t* sel,
+                             int64_t expert_lo, int64_t shared_t0, int64_t shared_n, ExactExperts& out, cudaStream_t s) {
+  const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
+  const int T = W->topk;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w && shared_n > 0;
+  const int64_t Pmax = perm_max_positions(M, T, static_cast<int>(E), 0);
+  const int64_t max_tiles = perm_max_tiles(M, T, static_cast<int>(E), 0, 8);
+  const int64_t Sn = shared ? shared_n : 0;
+  size_t sz[8] = {al256x(4 * M * T), al256x(4 * Pmax), al256x(16 * max_tiles), al256x(16), al256x(2 * Pmax * F),
+                  al256x(2 * Pmax * H), al256x(2 * std::max<int64_t>(Sn, 1) * F), al256x(2 * std::max<int64_t>(Sn, 1) * H)};
+  size_t total = 0;
+  for (size_t v : sz) total += v;
+  int rc = grow(&c->pre, &c->pre_bytes, total, "moe (exact): scratch");
+  if (rc) return rc;
+  uint8_t* b = static_cast<uint8_t*>(c->pre);
+  void* ptr[8];
+  for (int i = 0; i < 8; ++i) {
+    ptr[i] = b;
+    b += sz[i];
+  }
+  out.pos_of = static_cast<int32_t*>(ptr[0]);
+  int32_t* perm_tok = static_cast<int32_t*>(ptr[1]);
+  int4* tiles = static_cast<int4*>(ptr[2]);
+  int32_t* counts = static_cast<int32_t*>(ptr[3]);
+  uint16_t* h_perm = static_cast<uint16_t*>(ptr[4]);
+  out.y_perm = static_cast<uint16_t*>(ptr[5]);
+  uint16_t* h_sh = static_cast<uint16_t*>(ptr[6]);
+  out.y_sh = static_cast<uint16_t*>(ptr[7]);
+  PermParams pp = {};
+  pp.sel = sel;
+  pp.T = static_cast<int>(M);
+  pp.topk = T;
+  pp.E = static_cast<int>(E);
+  pp.nt = 8;
+  pp.expert_lo = static_cast<int>(expert_lo);
+  pp.perm_tok = perm_tok;
+  pp.pos_of = out.pos_of;
+  pp.tiles = tiles;
+  pp.n_tiles = counts;
+  pp.n_pos = counts + 1;
+  if ((rc = perm_launch(pp, s))) return rc;
+  ChainParams g = {};
+  g.w0 = static_cast<const uint8_t*>(W->gate_w);
+  g.w1 = static_cast<const uint8_t*>(W->up_w);
+  g.row_bytes = row_bytes_of(W->gate_wtype, H);
+  g.expert_stride = F * g.row_bytes;
+  g.n_experts = static_cast<int>(E);
+  g.N = static_cast<int>(F);
+  g.K = static_cast<int>(H);
+  g.x = x;
+  g.M = static_cast<int>(M);
+  g.tiles = tiles;
+  g.n_tiles_dev = counts;
+  g.max_tiles = static_cast<int>(max_tiles);
+  g.perm_tok = perm_tok;
+  g.y = h_perm;
+  g.status = c->status;
+  if ((rc = chain_launch(W->gate_wtype, CHAIN_SWIGLU, g, c->num_sms, s, true)))
+    return rc == CHAIN_UNSUPPORTED ? set_error(EINVAL_, "moe (exact): gate/up type or shape not supported") : rc;
+  ChainParams d = g;
+  d.w0 = static_cast<const uint8_t*>(W->down_w);
+  d.w1 = nullptr;
+  d.row_bytes = row_bytes_of(W->down_wtype, F);
+  d.expert_stride = H * d.row_bytes;
+  d.N = static_cast<int>(H);
+  d.K = static_cast<int>(F);
+  d.x = h_perm;
+  d.x_by_pos = 1;
+  d.M = static_cast<int>(Pmax);
+  d.y = out.y_perm;
+  if ((rc = chain_launch(W->down_wtype, CHAIN_STORE, d, c->num_sms, s, true)))
+    return rc == CHAIN_UNSUPPORTED ? set_error(EINVAL_, "moe (exact): down type or shape not supported") : rc;
+  if (shared) {
+    ChainParams sg = {};
+    sg.w0 = static_cast<const uint8_t*>(W->shared_gate_w);
+    sg.w1 = static_cast<const uint8_t*>(W->shared_up_w);
+    sg.row_bytes = g.row_bytes;
+    sg.n_groups = 1;
+    sg.N = static_cast<int>(F);
+    sg.K = static_cast<int>(H);
+    sg.x = static_cast<const uint16_t*>(x) + shared_t0 * H;
+    sg.M = static_cast<int>(Sn);
+    sg.y = h_sh;
+    sg.status = c->status;
+    if ((rc = chain_launch(W->gate_wtype, CHAIN_SWIGLU, sg, c->num_sms, s, true))) return rc;
+    ChainParams sd = sg;
+    sd.w0 = static_cast<const uint8_t*>(W->shared_down_w);
+    sd.w1 = nullptr;
+    sd.row_bytes = d.row_bytes;
+    sd.N = static_cast<int>(H);
+    sd.K = static_cast<int>(F);
+    sd.x = h_sh;
+    sd.y = out.y_sh;
+    if ((rc = chain_launch(W->down_wtype, CHAIN_STORE, sd, c->num_sms, s, true))) return rc;
+  }
+  return OK;
+}
+
+// Many-token MoE layer, bit-exact: router -> moe_experts_exact -> slot-order combine from positions.
+static int moe_exact_many(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y, int32_t* sel_out,
+                          void* sel_w_out, cudaStream_t s) {
+  const int64_t E = W->n_experts;
+  const int T = W->topk;
+  const int64_t P = M * T;
+  const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w;
+  const size_t aux = al256x(2 * M * E) + al256x(4 * P) + al256x(2 * P);
+  int rc = grow(&c->rt, &c->rt_bytes, aux, "moe (exact): router scratch");
+  if (rc) return rc;
+  uint16_t* gate = static_cast<uint16_t*>(c->rt);
+  int32_t* sel = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(gate) + al256x(2 * M * E));
+  uint16_t* sel_w = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(sel) + al256x(4 * P));
+  RouterParams rp = {};
+  rp.wt = W->router_wtype;
+  rp.w = static_cast<const uint8_t*>(W->router_w);
+  rp.bias = W->router_bias;
+  rp.x = static_cast<const uint16_t*>(x);
+  rp.M = static_cast<int>(M);
+  rp.K = static_cast<int>(W->hidden);
+  rp.E = static_cast<int>(E);
+  rp.topk = T;
+  rp.scale = W->scale;
+  rp.gate = gate;
+  rp.sel = sel;
+  rp.sel_w = sel_w;
+  rp.counters = c->router_counters;
+  rp.status = c->status;
+  if ((rc = router_launch(rp, s, false))) return rc;
+  ExactExperts ex = {};
+  if ((rc = moe_experts_exact(c, W, x, M, sel, 0, 0, shared ? M : 0, ex, s))) return rc;
+  CombineParams cp = {};
+  cp.M = static_cast<int>(M);
+  cp.H = static_cast<int>(W->hidden);
+  cp.topk = T;
+  cp.slot_map = ex.pos_of;
+  cp.sel_w = sel_w;
+  cp.y_union = ex.y_perm;
+  cp.y_shared = shared ? ex.y_sh : nullptr;
+  cp.out = static_cast<uint16_t*>(y);
+  cp.rows_are_positions = 1;
+  if ((rc = combine_launch(cp, s, true))) return rc;
+  if (sel_out && (rc = set_cuda_error(cudaMemcpyAsync(sel_out, sel, 4 * P, cudaMemcpyDeviceToDevice, s), "copy sel")))
+    return rc;
+  if (sel_w_out &&
+      (rc = set_cuda_error(cudaMemcpyAsync(sel_w_out, sel_w, 2 * P, cudaMemcpyDeviceToDevice, s), "copy sel_w")))
+    return rc;
+  return OK;
+}
+
+static bool exact_many_ok(const aipu_moe_weights* W, const void* x) {
+  return W->gate_wtype == AIPU_Q4_K && chain_supported(W->gate_wtype, W->hidden, row_bytes_of(W->gate_wtype, W->hidden)) &&
+         chain_supported(W->down_wtype, W->ffn, row_bytes_of(W->down_wtype, W->ffn)) &&
+         (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (W->n_experts * W->ffn * row_bytes_of(W->gate_wtype, W->hidden)) > 0;
+}
+
 static const int64_t kPrefillMinTokens = 64;
 
 extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void* x, int64_t M, void* y,
@@ -674,6 +911,10 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
   if (!strict && M >= kPrefillMinTokens && W->gate_wtype == AIPU_Q4_K &&
       (W->down_wtype == AIPU_Q4_K || W->down_wtype == AIPU_Q6_K) && (reinterpret_cast<uintptr_t>(x) & 15u) == 0)
     return moe_prefill(c, W, x, M, y, sel_out, sel_w_out, s);
+  // more tokens than the decode union path takes (its per-expert token masks hold 32 tokens): the
+  // bit-exact chains over per-expert token lists
+  if (M > 32 && !(c->flags & AIPU_FLAG_TC_DECODE) && exact_many_ok(W, x))
+    return moe_exact_many(c, W, x, M, y, sel_out, sel_w_out, s);
   if (M > 1024)
     return set_error(EINVAL_, strict ? "moe_layer (strict): at most 1024 tokens per call"
                                      : "moe_layer: more than 1024 tokens need Q4_K gate/up and Q4_K/Q6_K down");
@@ -710,14 +951,14 @@ extern "C" int aipu_moe_layer(aipu_ctx* c, const aipu_moe_weights* W, const void
     const int side_sms = std::max(1, c->num_sms - router_ctas);
     if ((rc = set_cuda_error(cudaStreamWaitEvent(c->side, c->ev_fork, 0), "streamWaitEvent"))) return rc;
     rc = swiglu_groups(c, c->ws[1], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
-                       H, F, 1, nullptr, nullptr, 1, x, M, sc.h_sh, sc.y_sh, c->side, false, side_sms,
+                       H, F, 1, nullptr, nullptr, 1, nullptr, 0, x, M, sc.h_sh, sc.y_sh, c->side, false, side_sms,
                        kSmemPerSm - router_smem_bytes(rp));
     if (rc) return rc;
     if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
   }
   const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
   rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F, static_cast<int>(E), sc.union_ids,
-                     sc.n_union, Umax, x, M, sc.h, sc.y, s, true);
+                     sc.n_union, Umax, sc.slot_map, T, x, M, sc.h, sc.y, s, true);
   if (rc) return rc;
   if (shared && (rc = set_cuda_error(cudaStreamWaitEvent(s, c->ev_join, 0), "streamWaitEvent"))) return rc;
   CombineParams cp = {};
@@ -775,12 +1016,12 @@ extern "C" int aipu_moe_experts(aipu_ctx* c, const aipu_moe_weights* W, int64_t 
     return rc;
   const int Umax = static_cast<int>(std::min<int64_t>(E, M * T));
   rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F,
-                     static_cast<int>(E), sc.union_ids, sc.n_union, Umax, x, M, sc.h, sc.y, s, false);
+                     static_cast<int>(E), sc.union_ids, sc.n_union, Umax, sc.slot_map, T, x, M, sc.h, sc.y, s, false);
   if (!rc)
     rc = gather_slots_launch(sc.slot_map, static_cast<int>(M), T, H, sc.y, M, 1, static_cast<uint16_t*>(y_slots), s);
   if (!rc && shared)
     rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
-                       H, F, 1, nullptr, nullptr, 1, static_cast<const uint16_t*>(x) + shared_t0 * H, shared_n,
+                       H, F, 1, nullptr, nullptr, 1, nullptr, 0, static_cast<const uint16_t*>(x) + shared_t0 * H, shared_n,
                        sc.h_sh, static_cast<uint16_t*>(y_shared), s, false);
   return rc;
 }
@@ -932,7 +1173,8 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
   if ((rc = ep_dispatch_launch(e->p, static_cast<const uint16_t*>(x), sel, static_cast<int>(M), s))) return rc;
   // 3. shared expert on the local tokens while the peers' tokens arrive
   if (shared && (rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype,
-                                    W->shared_down_w, H, F, 1, nullptr, nullptr, 1, x, M, sc.h_sh, y_sh, s, false)))
+                                    W->shared_down_w, H, F, 1, nullptr, nullptr, 1, nullptr, 0, x, M, sc.h_sh, y_sh, s,
+                                    false)))
     return rc;
   // 4. every rank's tokens: local experts
   if ((rc = ep_wait_launch(e->p, 0, s))) return rc;
@@ -944,7 +1186,8 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
     return rc;
   const int Umax = static_cast<int>(std::min<int64_t>(El, Gtok * T));
   if ((rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F,
-                          static_cast<int>(El), sc.union_ids, sc.n_union, Umax, in_x, Gtok, sc.h, sc.y, s, false)))
+                          static_cast<int>(El), sc.union_ids, sc.n_union, Umax, sc.slot_map, T, in_x, Gtok, sc.h, sc.y,
+                          s, false)))
     return rc;
   // 5. per-slot outputs into the owners' outboxes
   if ((rc = ep_return_launch(e->p, sc.slot_map, sc.y, static_cast<int>(M), static_cast<int>(Gtok), s))) return rc;
@@ -964,16 +1207,13 @@ extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt,
   DeviceGuard dg(c->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint16_t* hb = static_cast<uint16_t*>(h);
-  uint16_t* tmp = nullptr;
   if (!hb) {
-    if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), 2 * M * F, s) != cudaSuccess)
-      return set_error(ENOMEM_, "swiglu: scratch");
-    hb = tmp;
+    const int grc = grow(&c->tmp, &c->tmp_bytes, 2 * M * F, "swiglu: scratch");
+    if (grc) return grc;
+    hb = static_cast<uint16_t*>(c->tmp);
   }
-  int rc = swiglu_groups(c, c->ws[0], gwt, gw, uw, dwt, dw, H, F, 1, nullptr, nullptr, 1, x, M, hb,
-                         static_cast<uint16_t*>(y), s, false);
-  if (tmp) cudaFreeAsync(tmp, s);
-  return rc;
+  return swiglu_groups(c, c->ws[0], gwt, gw, uw, dwt, dw, H, F, 1, nullptr, nullptr, 1, nullptr, 0, x, M, hb,
+                       static_cast<uint16_t*>(y), s, false);
 }
 
 extern "C" int aipu_bf16_dot_gemv(aipu_ctx* c, const void* w, int64_t V, int64_t K, const void* x, int64_t M,

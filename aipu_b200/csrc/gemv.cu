@@ -1,6 +1,7 @@
 // Decode dequant GEMV kernel bodies and host launchers (design notes in gemv.cuh).
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "deq.cuh"
 #include "gemv.cuh"
@@ -693,7 +694,7 @@ __device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch
 }
 
 template <int WT, int XT, int EPI>
-__global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
   constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
@@ -899,15 +900,10 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) gemv_kernel(const __grid_co
 // ------------------------------------------------------------------ host launch
 template <int WT, int XT, int EPI>
 static int launch_one(GemvParams p, int grid, int nw, int smem, cudaStream_t stream, bool pdl) {
-  auto kern = gemv_kernel<WT, XT, EPI>;
+  auto kern = aipu_kq_gemv_kernel<WT, XT, EPI>;
   static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(gemv)");
-    attr_set[dev & 63] = true;
-  }
+  const int arc = set_smem_attr_once(reinterpret_cast<const void*>(kern), 232448 - 1024, attr_set, "cudaFuncSetAttribute(gemv)");
+  if (arc) return arc;
   return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(nw * 32), smem, stream, pdl, &p);
 }
 
@@ -994,13 +990,44 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
 
 // ------------------------------------------------------------------ allocation-free variant
 // Scratch for aipu_q4k_gemm_noalloc, owned by the library for the lifetime of the process on every
-// device that loads it: stream-K partials for up to kNoAllocSms CTAs of GEMV_MAXW workers, then one
-// arrival counter per 16-row tile for up to kNoAllocTiles tiles (N <= 65536 rows).
+// device that loads it: stream-K partials for up to kNoAllocSms CTAs of GEMV_MAXW workers, one
+// arrival counter per 16-row tile for up to kNoAllocTiles tiles (N <= 65536 rows), then one status
+// word (set when a bounded wait in the kernel gave up).
 constexpr int kNoAllocSms = 160;
 constexpr int kNoAllocTiles = 4096;
 constexpr size_t kNoAllocPartialBytes = sizeof(float) * kNoAllocSms * GEMV_MAXW * 2 * 128;  // 2.5 MiB
-constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + sizeof(int) * kNoAllocTiles;        // + 16 KiB
+constexpr size_t kNoAllocCounterBytes = sizeof(int) * kNoAllocTiles;                        // 16 KiB
+constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + kNoAllocCounterBytes + 256;        // + status word
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of the scratch array and SM count, looked up once per device with that device
+// current (in host code the array's name is only a host-side stand-in, never a device address).
+// The lookup is guarded by a mutex, so first calls from several threads do not race.
+struct NoAllocDev {
+  unsigned char* ptr = nullptr;
+  int sms = 0;
+};
+static int noalloc_device(NoAllocDev& out) {
+  static std::mutex mu;
+  static NoAllocDev table[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(EINVAL_, "gemm_noalloc: device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!table[dev].ptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaGetSymbolAddress");
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaDeviceGetAttribute");
+    table[dev].sms = n < kNoAllocSms ? n : kNoAllocSms;
+    table[dev].ptr = static_cast<unsigned char*>(ptr);
+  }
+  out = table[dev];
+  return OK;
+}
 
 }  // namespace aipu
 
@@ -1014,33 +1041,19 @@ extern "C" int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_
   if ((N + 15) / 16 > kNoAllocTiles)
     return set_error(EINVAL_, "gemm_noalloc: N exceeds the static scratch limit of 65536 rows");
   if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0) return set_error(EINVAL_, "gemm_noalloc: weights must be 16-byte aligned");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaGetDevice");
-  // device address of the scratch array, resolved once per device with that device current (in
-  // host code the array's name is only a host-side stand-in, never a device address)
-  static unsigned char* scratch_ptr[64] = {nullptr};
-  static int sms[64] = {0};
-  if (dev < 0 || dev >= 64) return set_error(EINVAL_, "gemm_noalloc: device index out of range");
-  if (!scratch_ptr[dev]) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaGetSymbolAddress");
-    int n = 0;
-    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaDeviceGetAttribute");
-    sms[dev] = n < kNoAllocSms ? n : kNoAllocSms;
-    scratch_ptr[dev] = static_cast<unsigned char*>(ptr);
-  }
+  NoAllocDev nd;
+  int rc = noalloc_device(nd);
+  if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  float* partials = reinterpret_cast<float*>(scratch_ptr[dev]);
-  int* counters = reinterpret_cast<int*>(scratch_ptr[dev] + kNoAllocPartialBytes);
+  float* partials = reinterpret_cast<float*>(nd.ptr);
+  int* counters = reinterpret_cast<int*>(nd.ptr + kNoAllocPartialBytes);
+  int* status = reinterpret_cast<int*>(nd.ptr + kNoAllocPartialBytes + kNoAllocCounterBytes);
   const int mb = (x_dtype == XT_F32) ? 4 : 8;
   const int esz = (x_dtype == XT_F32) ? 4 : 2;
   for (int64_t m0 = 0; m0 < M; m0 += mb) {
     // the counters must start at zero; an earlier call that gave up a bounded wait may have left
     // some set, so clear them before every launch (no allocation involved)
-    e = cudaMemsetAsync(counters, 0, sizeof(int) * ((N + 15) / 16), s);
+    cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int) * ((N + 15) / 16), s);
     if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc: cudaMemsetAsync");
     GemvParams p = {};
     p.w0 = static_cast<const uint8_t*>(w);
@@ -1053,10 +1066,27 @@ extern "C" int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_
     p.y = static_cast<uint16_t*>(y) + m0 * N;
     p.partials = partials;
     p.counters = counters;
-    p.status = nullptr;
-    const int rc = gemv_launch(wtype, x_dtype, EPI_STORE, p, sms[dev], s, false, 0);
+    p.status = status;
+    rc = gemv_launch(wtype, x_dtype, EPI_STORE, p, nd.sms, s, false, 0);
     if (rc) return rc;
   }
+  return OK;
+}
+
+extern "C" int aipu_q4k_gemm_noalloc_status(int* status) {
+  using namespace aipu;
+  if (!status) return set_error(EINVAL_, "gemm_noalloc_status: null pointer");
+  NoAllocDev nd;
+  int rc = noalloc_device(nd);
+  if (rc) return rc;
+  int* dst = reinterpret_cast<int*>(nd.ptr + kNoAllocPartialBytes + kNoAllocCounterBytes);
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, dst, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc_status: read");
+  const int zero = 0;
+  e = cudaMemcpy(dst, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return set_cuda_error(e, "gemm_noalloc_status: clear");
+  *status = v;
   return OK;
 }
 

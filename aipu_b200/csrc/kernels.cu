@@ -624,11 +624,10 @@ static int router_launch_eg(const RouterParams& p, cudaStream_t s, bool pdl) {
   static_assert(2 * RC::NST * 8 + 2 * RT_MB * 4 <= RC::OFF_RING, "router barriers fit before the ring");
   static_assert(RC::SMEM <= 227 * 1024, "router shared memory");
   const int smem = RC::SMEM;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(router_strict_kernel<EG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(router)");
-    attr = true;
+  static bool attr[64] = {false};
+  {
+    const int arc = set_smem_attr_once(reinterpret_cast<const void*>(router_strict_kernel<EG>), smem, attr, "cudaFuncSetAttribute(router)");
+    if (arc) return arc;
   }
   RouterParams q = p;
   if (p.wt == WT_F32) {

@@ -152,4 +152,48 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
 int gemv_partials_floats(int num_sms);
 int act_launch(int kind, const void* x, int64_t n, void* out, cudaStream_t s);
 
+// Bit-exact sequential-chain GEMV (chain.cu): every output is the reference's sequential fp32 chain
+// over k (tools/q4k_ref.py:86-92), computed for many rows at once. Groups (experts) g use weights
+// w + group_ids[g] * expert_stride; the tokens of group g are the x rows m with some slot
+// slot_map[m * topk + s] == g (all M rows when slot_map is null). x rows of group g start at
+// x + g * x_group_stride (elements; 0 = shared rows); outputs y[g * y_group_stride + m * N + n].
+enum ChainEpi : int { CHAIN_STORE = 0, CHAIN_SWIGLU = 1 };
+struct ChainParams {
+  const uint8_t* w0;         // rows (CHAIN_SWIGLU: gate rows)
+  const uint8_t* w1;         // up rows (CHAIN_SWIGLU)
+  int64_t row_bytes, expert_stride;
+  const int* group_ids;      // nullable: group g = expert g
+  const int* n_groups_dev;   // nullable: n_groups groups
+  int n_groups, n_experts;
+  int N, K;
+  const void* x;             // activations (bf16, or fp32 when x_f32)
+  int x_f32;
+  int64_t x_group_stride;
+  int M;                     // token rows
+  const int32_t* slot_map;   // [M, topk] group index of each (token, slot), -1 none (nullable)
+  int topk;
+  // tile mode (many tokens, tiles != null): the token lists of perm_kernel with 8 tokens per tile --
+  // item rows come from tile t = (expert, first position p0, tokens c): tokens perm_tok[p0 .. p0 + c),
+  // x row = perm_tok[p0 + j] (or p0 + j when x_by_pos), output row y[(p0 + j) * N + n]
+  const int4* tiles;
+  const int* n_tiles_dev;
+  int max_tiles;
+  const int32_t* perm_tok;
+  int x_by_pos;
+  uint16_t* y;               // bf16 out (CHAIN_SWIGLU: h = bf16(silu(bf16 g) * bf16 u))
+  float* y_f32;              // fp32 accumulators (CHAIN_STORE, nullable)
+  int64_t y_group_stride;
+  int* status;
+  // set by chain_launch
+  float neg_zero;            // -0.0f (the addend that forms exact products; see chain.cu)
+  int tiles_per_group, nstages, stage_bytes, w_bytes, mt;
+  alignas(64) CUtensorMap tmap0;
+  alignas(64) CUtensorMap tmap1;
+};
+// Returns OK, an error, or CHAIN_UNSUPPORTED (shape/type the kernel does not take: use the generic
+// strict kernel).
+constexpr int CHAIN_UNSUPPORTED = 1;
+int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bool pdl);
+bool chain_supported(int wt, int64_t K, int64_t row_bytes);
+
 }  // namespace aipu

@@ -21,6 +21,11 @@ int launch_kernel(const void* kern, dim3 grid, dim3 block, int smem, cudaStream_
 
 int num_sms_of_current_device();
 
+// Raise a kernel's dynamic shared-memory limit once per device (the attribute is per device, so a
+// process with contexts on several devices sets it on each). `done` is the caller's per-kernel
+// table of 64 device flags.
+int set_smem_attr_once(const void* kern, int bytes, bool* done, const char* what);
+
 // Encode a tiled TMA tensor map (no swizzle, no interleave, OOB reads return 0). The driver entry
 // point is looked up through the runtime, so the library does not link libcuda.
 // dims/box in elements (innermost first); strides in bytes for dims 1..rank-1.

@@ -102,12 +102,10 @@ template <int MT>
 static int bf16_dot7_launch_mt(const uint16_t* w, int64_t V, int K, const uint16_t* x, int M, uint16_t* y,
                                int num_sms, cudaStream_t s, bool pdl) {
   const int smem = MT * K * 4;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(bf16_dot7_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(bf16_dot7)");
-    attr = true;
+  static bool attr[64] = {false};
+  {
+    const int arc = set_smem_attr_once(reinterpret_cast<const void*>(bf16_dot7_kernel<MT>), 227 * 1024, attr, "cudaFuncSetAttribute(bf16_dot7)");
+    if (arc) return arc;
   }
   int per_sm = 0;
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bf16_dot7_kernel<MT>, 256, smem);

@@ -306,7 +306,7 @@ __device__ __forceinline__ bool tc_wait_stage_done(TcBars* bars, uint32_t k, int
 }
 
 template <int WT, int NT, bool SWIGLU>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(TC_THREADS, 1) aipu_tc_gemm_kernel(const __grid_constant__ TcParams p) {
   using C = TcCfg<WT, NT>;
   extern __shared__ __align__(1024) uint8_t smem[];
   TcBars* bars = reinterpret_cast<TcBars*>(smem);
@@ -762,12 +762,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 template <int WT, int NT, bool SW>
 static int tc_launch_one(const TcParams& p, int grid, cudaStream_t s, bool pdl) {
   constexpr int smem = TcCfg<WT, NT>::TOTAL;
-  auto kern = tc_gemm_kernel<WT, NT, SW>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(tc_gemm)");
-    attr = true;
+  auto kern = aipu_tc_gemm_kernel<WT, NT, SW>;
+  static bool attr[64] = {false};
+  {
+    const int arc = set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, attr, "cudaFuncSetAttribute(tc_gemm)");
+    if (arc) return arc;
   }
   TcParams q = p;
   return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(TC_THREADS), smem, s, pdl, &q);

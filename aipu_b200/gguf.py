@@ -280,6 +280,10 @@ def load_matrix(gf: GGUFFile, name: str, device) -> Matrix:
     if len(t.ne) != 2:
         raise GGUFError(f"{name}: expected a 2-D tensor, got ne = {list(t.ne)}")
     K, N = t.ne
+    if t.wtype not in (F.Q4_K, F.Q6_K, F.Q8_0, F.F16):
+        raise GGUFError(f"{name}: type {t.ggml_type} is not a GEMM weight type (Q4_K, Q6_K, Q8_0 or F16)")
+    if K % 256:
+        raise GGUFError(f"{name}: K = {K} is not a multiple of 256 (the fast GEMM streams 256-weight columns)")
     return Matrix(t.wtype, N, K, gf.to_device(name, device))
 
 

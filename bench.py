@@ -592,7 +592,7 @@ def main():
                        "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic_from_profile(),
-                         "peak_source": peak_kind, "kernel": "gemv_kernel<Q4_K,bf16,store> (grouped launch)",
+                         "peak_source": peak_kind, "kernel": "aipu_kq_gemv_kernel<Q4_K,bf16,store> (grouped launch)",
                          "us_per_launch": round(step * 1e6, 3)},
             "single_launch": single,
             "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,

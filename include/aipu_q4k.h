@@ -71,6 +71,10 @@ int aipu_ctx_destroy(aipu_ctx* ctx);
  * and the combine in the reference's op order, so outputs equal tools/glm_model_q4k_ref.py
  * swiglu_expert / the decoder block's MoE branch bit for bit (slower: no tensor cores). */
 #define AIPU_FLAG_STRICT 2
+/* AIPU_FLAG_TC_DECODE: run the SwiGLU experts of the decode MoE path (aipu_moe_layer with few tokens,
+ * aipu_moe_experts, aipu_swiglu_expert, aipu_ep_moe_layer) on the tensor-core GEMV (each GEMM within
+ * 1 bf16 ulp, the layer not bit-exact) instead of the default bit-exact chain kernel. */
+#define AIPU_FLAG_TC_DECODE 4
 int aipu_ctx_set_flags(aipu_ctx* ctx, int flags);
 /* device status word of the context (0 = no bounded wait ever gave up); resets it to 0 */
 int aipu_ctx_status(aipu_ctx* ctx, int* status);
@@ -101,15 +105,21 @@ int aipu_q4k_gemm(aipu_ctx* ctx, int wtype, const void* w, int64_t N, int64_t K,
  * plug-ins that must not create or keep a context object, and latency-critical paths where the
  * device-wide synchronisation of cudaMalloc/cudaFree is unacceptable. Same inputs, outputs and
  * numerics as aipu_q4k_gemm in AIPU_MODE_FAST (x_dtype AIPU_DT_F32 or AIPU_DT_BF16; wtype Q4_K,
- * Q6_K, Q8_0 or F16; K a multiple of 256), but its scratch (stream-K partial sums and arrival
- * counters, about 2.5 MiB) is a static array inside the library, held by every GPU that loads the
- * library until the process exits. Limit: N <= 65536 rows (larger N is rejected with
- * AIPU_EINVAL). The first call on a device looks up the array's device address (make that first
- * call before any stream capture). All calls share the one array: calls that overlap on the GPU
- * (different streams, or other threads) race and corrupt each other; serialise them. No
- * counterpart in the reference. */
+ * Q6_K, Q8_0 or F16; K a multiple of 256), but its scratch (stream-K partial sums, arrival
+ * counters and a status word, about 2.5 MiB) is a static array inside the library, held by every
+ * GPU that loads the library until the process exits. Limit: N <= 65536 rows (larger N is
+ * rejected with AIPU_EINVAL). The first call on a device looks up the array's device address
+ * (guarded by a lock; make that first call before any stream capture). All calls share the one
+ * array: calls that overlap on the GPU (different streams, or other threads) race and corrupt each
+ * other; serialise them. The call is asynchronous, so its return code cannot report a bounded
+ * device wait that gave up (its outputs are then left partly unwritten): the kernel records that in
+ * the array's status word, which aipu_q4k_gemm_noalloc_status reads. No counterpart in the
+ * reference. */
 int aipu_q4k_gemm_noalloc(int wtype, const void* w, int64_t N, int64_t K, const void* x, int x_dtype, int64_t M,
                           void* y, void* stream);
+/* Status word of aipu_q4k_gemm_noalloc on the current device (0 = no bounded wait gave up since the
+ * last read), read synchronously and reset to 0; allocates nothing. No counterpart in the reference. */
+int aipu_q4k_gemm_noalloc_status(int* status);
 
 /* Prefill GEMM on the 5th-generation tensor cores (tcgen05 MMA, fp32 accumulators in TMEM):
  * y[M, N] (bf16) = x[M, K] (bf16, 16-byte aligned) x W[N rows, K]^T for Q4_K or Q6_K weights and many

@@ -277,3 +277,37 @@ def bf16_dot7(x_bf: np.ndarray, w_bf: np.ndarray) -> np.ndarray:
     z = F32(0.0)
     a01, a23, a45, a6 = ps[0] + ps[1], ps[2] + ps[3], ps[4] + ps[5], ps[6] + z
     return qo.bf16_round((a01 + a23) + (a45 + a6))
+
+
+def moe_layer_packed(x_bf, router_rows_f32, experts, shared, topk: int, bias=None, scale=RSCALE_DEFAULT,
+                     gate_wtype: int = 0, down_wtype: int = 1):
+    """moe_layer on packed GGUF rows, with every GEMM done by the C restatement of the sequential
+    contract (oracle/q4k_oracle.c; bit-identical to qo.matmul_seq), for full-size layers.
+    x_bf [M, H] bf16-valued fp32; router_rows_f32 [E, H] fp32 (router rows); experts: callable
+    e -> (gate rows, up rows, down rows) as uint8 [rows, row bytes]; shared: same tuple or None.
+    Returns (out [M, H], sel, sel_w) exactly as moe_layer (glm_model_q4k_ref.py:797-809)."""
+    from . import cpu
+
+    x = np.ascontiguousarray(np.asarray(x_bf, F32))
+    M, H = x.shape
+    E = router_rows_f32.shape[0]
+    logits = cpu.gemm(4, np.ascontiguousarray(router_rows_f32, F32).view(np.uint8), E, H, x)
+    sel, sel_w, _ = route_from_logits(logits, topk, bias, scale)
+
+    def expert_rows(wg, wu, wd, xr):
+        Fd = wg.shape[0]
+        g = cpu.gemm(gate_wtype, wg, Fd, H, xr)
+        u = cpu.gemm(gate_wtype, wu, Fd, H, xr)
+        h = qo.bf16_round(glm_silu(g) * u)
+        return cpu.gemm(down_wtype, wd, H, Fd, h)
+
+    y_slots = np.empty((M, topk, H), F32)
+    for e in sorted(set(int(v) for v in sel.reshape(-1))):
+        rows = np.nonzero((sel == e).any(axis=1))[0]
+        ye = expert_rows(*experts(e), x[rows])
+        for i, m in enumerate(rows):
+            for s in range(topk):
+                if sel[m, s] == e:
+                    y_slots[m, s] = ye[i]
+    y_sh = expert_rows(*shared, x) if shared is not None else None
+    return combine(sel_w, y_slots, y_sh), sel, sel_w

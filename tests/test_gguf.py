@@ -106,3 +106,18 @@ def test_load_matrix_keeps_rows_and_type():
         assert np.array_equal(m.rows.numpy(), np.array(gf.raw("blk.0.ffn_down.weight")))
         with pytest.raises(gguf.GGUFError):
             gguf.load_matrix(gf, "blk.0.attn_norm.weight", "cpu")
+
+
+def test_load_matrix_rejects_non_gemm_tensors(tmp_path):
+    """A 2-D F32 tensor, or one whose K is not a multiple of 256, is refused at load time with its name."""
+    p = str(tmp_path / "m.gguf")
+    gguf.write_gguf(p, [gguf.TensorSpec("f32w", gguf.GGML_F32, (256, 4), np.zeros(1024, np.float32).tobytes()),
+                        gguf.TensorSpec("q8w", gguf.GGML_Q8_0, (96, 4), F.random_rows_np(F.Q8_0, 4, 96, seed=1).tobytes()),
+                        gguf.TensorSpec("okw", gguf.GGML_Q8_0, (256, 4), F.random_rows_np(F.Q8_0, 4, 256, seed=2).tobytes())])
+    with gguf.GGUFFile(p) as gf:
+        with pytest.raises(gguf.GGUFError, match="f32w"):
+            gguf.load_matrix(gf, "f32w", "cpu")
+        with pytest.raises(gguf.GGUFError, match="q8w.*256"):
+            gguf.load_matrix(gf, "q8w", "cpu")
+        m = gguf.load_matrix(gf, "okw", "cpu")
+        assert (m.wtype, m.N, m.K) == (F.Q8_0, 4, 256)

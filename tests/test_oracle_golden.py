@@ -167,3 +167,23 @@ def test_bf16_dot7_oracle_matches_reference_fixture(golden):
         w = (g[f"{c}_w"].astype(np.uint32) << 16).view(np.float32)
         y = mo.bf16_dot7(x, w)
         assert np.array_equal((y.view(np.uint32) >> 16).astype(np.uint16), g[f"{c}_y"]), c
+
+
+def test_moe_layer_packed_reference(golden):
+    """The full-size oracle layer (C-restatement GEMMs on packed rows) equals the reference's MoE
+    branch bit for bit (F padded to 256 with zero gate/up rows, which leave h and y unchanged)."""
+    g = golden("moe_golden")
+    E, T, D, Fd = (int(v) for v in g["moe_meta"])
+    Fp = 256
+    gate = np.zeros((E + 1, Fp, 144), np.uint8)
+    up = np.zeros((E + 1, Fp, 144), np.uint8)
+    gate[:, :Fd] = g["moe_gate_w"]
+    up[:, :Fd] = g["moe_up_w"]
+    down = g["moe_down_w"]
+    x = g["moe_x"].view(F32)
+    rrows = qo.dequant_rows(0, g["moe_router_w"], E, 256)
+    out, sel, sw = mo.moe_layer_packed(x, rrows, lambda e: (gate[e], up[e], down[e]), (gate[E], up[E], down[E]), T,
+                                       gate_wtype=0, down_wtype=0)
+    assert np.array_equal(sel, g["moe_sel"])
+    assert np.array_equal(bits(sw), g["moe_sw"])
+    assert np.array_equal(bits(out), g["moe_y"])
