@@ -27,7 +27,6 @@
 
 namespace aipu {
 
-constexpr int CH_NT = 128;       // consumer threads per CTA
 constexpr int CH_MAXS = 6;       // ring stages
 constexpr uint32_t MAG = 0x4B000000u;   // 2^23
 constexpr float MAGF = 8388608.0f;
@@ -88,12 +87,6 @@ __device__ __forceinline__ float4 ch_ldsf4(uint32_t a) {
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
   return v;
 }
-// 4 bytes at a shared address that is 4-byte aligned (A4) or 2 mod 4
-template <bool A4>
-__device__ __forceinline__ uint32_t ch_ld4(uint32_t a) {
-  if (A4) return ch_lds1(a);
-  return __byte_perm(ch_lds1(a - 2), ch_lds1(a + 2), 0x5432);
-}
 __device__ __forceinline__ uint32_t lop_mag(uint32_t w, uint32_t mask) {
   uint32_t d;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w), "r"(mask), "r"(MAG));
@@ -136,18 +129,19 @@ __device__ __forceinline__ void q4k_sb(uint32_t ra, uint32_t rb, uint32_t xs, fl
   const uint32_t sb47 = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
   const uint32_t mb47 = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
   const float2 nmag = f2s(-MAGF);
-#pragma unroll
+  // one 64-weight group per iteration, not unrolled: the fully unrolled 256-weight body overflowed the
+  // instruction cache (measured: instruction-fetch stalls dominated)
+#pragma unroll 1
   for (int g = 0; g < 4; ++g) {
     // sub-blocks 2g (low nibbles) and 2g + 1 (high nibbles): d1 = d*sc, m1 = dmin*m, both exact
-    const int jl = 2 * g, jh = 2 * g + 1;
-    const uint32_t tsa_l = jl < 4 ? sa03 : sa47, tsb_l = jl < 4 ? sb03 : sb47;
-    const uint32_t tma_l = jl < 4 ? ma03 : ma47, tmb_l = jl < 4 ? mb03 : mb47;
-    const uint32_t tsa_h = jh < 4 ? sa03 : sa47, tsb_h = jh < 4 ? sb03 : sb47;
-    const uint32_t tma_h = jh < 4 ? ma03 : ma47, tmb_h = jh < 4 ? mb03 : mb47;
-    const float2 scl = add2(f2(byte_mag(tsa_l, jl & 3), byte_mag(tsb_l, jl & 3)), nmag);
-    const float2 mnl = add2(f2(byte_mag(tma_l, jl & 3), byte_mag(tmb_l, jl & 3)), nmag);
-    const float2 sch = add2(f2(byte_mag(tsa_h, jh & 3), byte_mag(tsb_h, jh & 3)), nmag);
-    const float2 mnh = add2(f2(byte_mag(tma_h, jh & 3), byte_mag(tmb_h, jh & 3)), nmag);
+    const bool hi4 = g >= 2;
+    const uint32_t tsa = hi4 ? sa47 : sa03, tsb = hi4 ? sb47 : sb03;
+    const uint32_t tma = hi4 ? ma47 : ma03, tmb = hi4 ? mb47 : mb03;
+    const int bl = (2 * g) & 3, bh = (2 * g + 1) & 3;
+    const float2 scl = add2(f2(byte_mag(tsa, bl), byte_mag(tsb, bl)), nmag);
+    const float2 mnl = add2(f2(byte_mag(tma, bl), byte_mag(tmb, bl)), nmag);
+    const float2 sch = add2(f2(byte_mag(tsa, bh), byte_mag(tsb, bh)), nmag);
+    const float2 mnh = add2(f2(byte_mag(tma, bh), byte_mag(tmb, bh)), nmag);
     const float2 d1l = mul2(d, scl), d1h = mul2(d, sch);
     const float2 nm1l = mul2(dm, make_float2(-mnl.x, -mnl.y));
     const float2 nm1h = mul2(dm, make_float2(-mnh.x, -mnh.y));
@@ -214,34 +208,75 @@ __device__ __forceinline__ uint32_t sext_byte(uint32_t w, int b) {
   const uint32_t s = 8u | static_cast<uint32_t>(b);
   return prmt(w, 0u, static_cast<uint32_t>(b) | (s << 4) | (s << 8) | (s << 12));
 }
-template <int CNT, bool A4>
-__device__ __forceinline__ void q6k_sb(uint32_t ra, uint32_t rb, uint32_t xs, float2 (&acc)[8], const float2 nz) {
-  const float2 d = make_float2(f16_bits_to_f32(__byte_perm(ch_ld4<A4>(ra + 208), 0, 0x3210)),
-                               f16_bits_to_f32(__byte_perm(ch_ld4<A4>(rb + 208), 0, 0x3210)));
+// Words i = 0..n-1 starting `head` bytes (even, < 16) into a window of 16-byte chunks loaded with
+// conflict-free LDS.128 from a 16-byte-aligned row address (rows 240 bytes apart: an odd number of
+// 16-byte units, so the 8 lanes of each LDS.128 phase hit distinct banks).
+template <int NW, int NCH>
+__device__ __forceinline__ void q6k_words(uint32_t row16, int head, uint32_t (&out)[NW]) {
+  uint32_t win[4 * NCH];
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    const uint4 v = ch_lds4(row16 + 16 * j);
+    win[4 * j] = v.x;
+    win[4 * j + 1] = v.y;
+    win[4 * j + 2] = v.z;
+    win[4 * j + 3] = v.w;
+  }
+  // realign by head bytes: word offset head >> 2 (warp-uniform, 4 cases), then half-word shift
+  const uint32_t sel = (head & 2) ? 0x5432u : 0x3210u;
+  switch (head >> 2) {
+#define AIPU_Q6W(O)                                                                               \
+  case O:                                                                                         \
+    _Pragma("unroll") for (int i = 0; i < NW; ++i) out[i] = __byte_perm(win[i + O], win[i + O + 1], sel); \
+    break;
+    AIPU_Q6W(0)
+    AIPU_Q6W(1)
+    AIPU_Q6W(2)
+    default:
+      _Pragma("unroll") for (int i = 0; i < NW; ++i) out[i] = __byte_perm(win[i + 3], win[i + 4], sel);
+      break;
+#undef AIPU_Q6W
+  }
+}
+
+template <int CNT>
+__device__ __forceinline__ void q6k_sb(uint32_t ra16, uint32_t rb16, int head, uint32_t xs, float2 (&acc)[8],
+                                       const float2 nz) {
+  // scales and d: bytes 192..209 of the super-block
+  uint32_t ta[5], tb[5];
+  q6k_words<5, 3>(ra16 + 192, head, ta);
+  q6k_words<5, 3>(rb16 + 192, head, tb);
+  const float2 d = make_float2(f16_bits_to_f32(ta[4]), f16_bits_to_f32(tb[4]));
   const float2 c0 = f2s(-(MAGF + 32.f)), c1 = f2s(-(MAGF + 8192.f)), c2 = f2s(-(MAGF + 2097152.f));
-#pragma unroll
+#pragma unroll 1
   for (int h = 0; h < 2; ++h) {
-    // scales of this half: sc[8h .. 8h + 7] as exact floats d * sc (sign-extended bytes)
-    const uint32_t sca0 = ch_ld4<A4>(ra + 192 + 8 * h), sca1 = ch_ld4<A4>(ra + 196 + 8 * h);
-    const uint32_t scb0 = ch_ld4<A4>(rb + 192 + 8 * h), scb1 = ch_ld4<A4>(rb + 196 + 8 * h);
-    float2 ds[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int ia = static_cast<int>(sext_byte(i < 4 ? sca0 : sca1, i & 3));
-      const int ib = static_cast<int>(sext_byte(i < 4 ? scb0 : scb1, i & 3));
-      // int8 -> float via 1.5 * 2^23 + v (exact for |v| < 2^22)
-      const float2 sv = add2(f2(0x4B400000u + static_cast<uint32_t>(ia), 0x4B400000u + static_cast<uint32_t>(ib)),
-                                   f2s(-12582912.0f));
-      ds[i] = mul2(d, sv);
-    }
+    // ql[64h .. 64h + 64) and qh[32h .. 32h + 32) of both rows, realigned into registers
+    uint32_t A[16], Q[8], B2[16], Q2[8];
+    q6k_words<16, 5>(ra16 + 64 * h, head, A);
+    q6k_words<8, 3>(ra16 + 128 + 32 * h, head, Q);
+    q6k_words<16, 5>(rb16 + 64 * h, head, B2);
+    q6k_words<8, 3>(rb16 + 128 + 32 * h, head, Q2);
+    const uint32_t sa_lo = h ? ta[2] : ta[0], sa_hi = h ? ta[3] : ta[1];
+    const uint32_t sb_lo = h ? tb[2] : tb[0], sb_hi = h ? tb[3] : tb[1];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const uint32_t qbase = (c & 1) ? 32u : 0u;
+      // sub-block scales sc[8h + 2c + l/16], l/16 = 0 (words 0..3) and 1 (words 4..7): exact d * sc
+      float2 dsc[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int i = 2 * c + hh;
+        const int ia = static_cast<int>(sext_byte(i < 4 ? sa_lo : sa_hi, i & 3));
+        const int ib = static_cast<int>(sext_byte(i < 4 ? sb_lo : sb_hi, i & 3));
+        // int8 -> float via 1.5 * 2^23 + v (exact for |v| < 2^22)
+        const float2 sv = add2(f2(0x4B400000u + static_cast<uint32_t>(ia), 0x4B400000u + static_cast<uint32_t>(ib)),
+                               f2s(-12582912.0f));
+        dsc[hh] = mul2(d, sv);
+      }
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
-        const int k = 128 * h + 32 * c + 4 * w;
-        const uint32_t qla = ch_ld4<A4>(ra + 64 * h + qbase + 4 * w), qlb = ch_ld4<A4>(rb + 64 * h + qbase + 4 * w);
-        const uint32_t qha = ch_ld4<A4>(ra + 128 + 32 * h + 4 * w), qhb = ch_ld4<A4>(rb + 128 + 32 * h + 4 * w);
+        const int k = 128 * h + 32 * c + 4 * w;  // h is a loop variable: k is an offset into xs
+        const uint32_t qla = A[8 * (c & 1) + w], qlb = B2[8 * (c & 1) + w];
+        const uint32_t qha = Q[w], qhb = Q2[w];
         uint32_t ca, cb;
         if (c == 0) {
           ca = (qla & 0x0F0F0F0Fu) | ((qha << 4) & 0x30303030u);
@@ -257,7 +292,7 @@ __device__ __forceinline__ void q6k_sb(uint32_t ra, uint32_t rb, uint32_t xs, fl
           cb = ((qlb >> 4) & 0x0F0F0F0Fu) | ((qhb >> 2) & 0x30303030u);
         }
         const uint32_t cas = ca >> 16, cbs = cb >> 16;
-        const float2 s0 = ds[2 * c + (w >> 2)];
+        const float2 s0 = dsc[w >> 2];
         const float2 s8 = mul2(s0, f2s(0x1p-8f)), s16 = mul2(s0, f2s(0x1p-16f));
         float2 x0[8], x1[8], x2[8], x3[8];
         load_x2<CNT>(xs, k, x0, x1);
@@ -349,8 +384,8 @@ __device__ __forceinline__ void item_at(const ChainParams& p, int idx, int lane,
   }
 }
 
-template <int WT, int EPI, int MT>
-__global__ void __launch_bounds__(CH_NT + 32, 1) aipu_chain_kernel(const __grid_constant__ ChainParams p) {
+template <int WT, int EPI, int MT, int CH_NT>
+__global__ void __launch_bounds__(CH_NT + 32) aipu_chain_kernel(const __grid_constant__ ChainParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int PITCH = ChainGeom<WT>::PITCH;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -366,8 +401,10 @@ __global__ void __launch_bounds__(CH_NT + 32, 1) aipu_chain_kernel(const __grid_
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_launch_dependents();
-  pdl_wait();  // the token lists and activations come from the preceding kernels
+  // the token lists and activations come from the preceding kernels (launched without programmatic
+  // dependent launch: a persistent CTA of this kernel fills an SM, and one that waited early for its
+  // predecessor would hold the SM idle)
+  pdl_wait();
   const int ngroups = p.tiles ? min(*p.n_tiles_dev, p.max_tiles)
                               : (p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
   const int n_items = ngroups * p.tiles_per_group * chain_passes(p);
@@ -472,12 +509,9 @@ __global__ void __launch_bounds__(CH_NT + 32, 1) aipu_chain_kernel(const __grid_
         }
       } else {
         const int head = (210 * sb) & 15;
-        const uint32_t ra = smem_u32(st + tid * PITCH + head);
+        const uint32_t ra = smem_u32(st + tid * PITCH);
         const uint32_t rb = ra + CH_NT * PITCH;
-        const bool a4 = (head & 3) == 0;
-#define AIPU_Q6(C)                                   \
-  if (a4) q6k_sb<C, true>(ra, rb, xs, acc, nz);          \
-  else q6k_sb<C, false>(ra, rb, xs, acc, nz);
+#define AIPU_Q6(C) q6k_sb<C>(ra, rb, head, xs, acc, nz);
         switch (ci.cnt) {
           case 1: AIPU_Q6(1) break;
           case 2: if (MT >= 2) { AIPU_Q6((MT >= 2 ? 2 : 1)) } break;
@@ -532,13 +566,13 @@ bool chain_supported(int wt, int64_t K, int64_t row_bytes) {
   return (wt == WT_Q4K || wt == WT_Q6K) && K > 0 && K % 256 == 0 && row_bytes % 16 == 0;
 }
 
-template <int WT, int EPI, int MT>
-static int chain_launch_t(ChainParams& p, int grid, int smem, cudaStream_t s, bool pdl) {
-  auto kern = aipu_chain_kernel<WT, EPI, MT>;
+template <int WT, int EPI, int MT, int NT>
+static int chain_launch_t(ChainParams& p, int grid, int smem, cudaStream_t s) {
+  auto kern = aipu_chain_kernel<WT, EPI, MT, NT>;
   static bool attr[64] = {false};
   const int rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, attr, "cudaFuncSetAttribute(chain)");
   if (rc) return rc;
-  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(CH_NT + 32), smem, s, pdl, &p);
+  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NT + 32), smem, s, false, &p);
 }
 
 int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bool pdl) {
@@ -555,17 +589,31 @@ int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bo
   if (ne > 1 && p.expert_stride % 16) return CHAIN_UNSUPPORTED;
   const int pitch = (wt == WT_Q4K) ? ChainGeom<WT_Q4K>::PITCH : ChainGeom<WT_Q6K>::PITCH;
   const int box = pitch / 8;
-  const int rows_tile = (epi == CHAIN_SWIGLU) ? CH_NT : 2 * CH_NT;
-  const int box_rows = (epi == CHAIN_SWIGLU) ? CH_NT : 2 * CH_NT;
-  p.tiles_per_group = (p.N + rows_tile - 1) / rows_tile;
   const int mneed = p.tiles ? 8 : std::min(p.M, 8);
   const int mt = mneed <= 1 ? 1 : mneed <= 2 ? 2 : mneed <= 4 ? 4 : 8;
   p.mt = mt;
-  p.w_bytes = 2 * CH_NT * pitch;
+  const int64_t passes = p.tiles ? 1 : ((p.slot_map ? std::min(p.M, 32) : p.M) + mt - 1) / mt;
+  const int64_t ngr = p.tiles ? p.max_tiles : p.n_groups;
+  // 128 consumer threads (one CTA per SM), or 64 with several CTAs per SM when 128-thread tiles would
+  // leave SMs idle or need a second round (the Q6_K down projection of a decode layer)
+  auto items_of = [&](int nt) {
+    const int rt = (epi == CHAIN_SWIGLU) ? nt : 2 * nt;
+    return ngr * ((p.N + rt - 1) / rt) * passes;
+  };
+  const int NT = (epi == CHAIN_STORE && items_of(128) > num_sms / 2) ? 64 : 128;
+  const int rows_tile = (epi == CHAIN_SWIGLU) ? NT : 2 * NT;
+  const int box_rows = rows_tile;
+  p.tiles_per_group = (p.N + rows_tile - 1) / rows_tile;
+  p.w_bytes = 2 * NT * pitch;
   p.stage_bytes = p.w_bytes + mt * 256 * 8;
   const int limit = 232448 - 1024;
-  p.nstages = std::min(CH_MAXS, (limit - 128) / p.stage_bytes);
-  if (p.nstages < 2) return set_error(EINVAL_, "chain: stage too large for shared memory");
+  // NT = 64: at most three CTAs per SM, two stages each when that fits
+  const int per_cta = (NT == 64) ? std::max(2 * p.stage_bytes + 128, (limit - 3 * 1024) / 3) : limit;
+  p.nstages = std::min(CH_MAXS, (std::min(per_cta, limit) - 128) / p.stage_bytes);
+  if (p.nstages < 2) {
+    p.nstages = std::min(CH_MAXS, (limit - 128) / p.stage_bytes);
+    if (p.nstages < 2) return set_error(EINVAL_, "chain: stage too large for shared memory");
+  }
   const int smem = 128 + p.nstages * p.stage_bytes;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(p.row_bytes / 8), static_cast<cuuint64_t>(p.N),
                               static_cast<cuuint64_t>(ne)};
@@ -575,24 +623,20 @@ int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bo
   int rc = encode_tiled(&p.tmap0, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, p.w0, dims, strides, boxd);
   if (!rc && epi == CHAIN_SWIGLU) rc = encode_tiled(&p.tmap1, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, p.w1, dims, strides, boxd);
   if (rc) return rc;
-  const int64_t passes = p.tiles ? 1 : ((p.slot_map ? std::min(p.M, 32) : p.M) + mt - 1) / mt;
-  const int64_t items = static_cast<int64_t>(p.tiles ? p.max_tiles : p.n_groups) * p.tiles_per_group * passes;
+  const int64_t items = items_of(NT);
   if (items > (1ll << 30)) return set_error(EINVAL_, "chain: too many items");
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, items)));
-#define AIPU_CHAIN_CASE(W, E, M_)                                  \
-  if (wt == W && epi == E && mt == M_) return chain_launch_t<W, E, M_>(p, grid, smem, s, pdl);
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_STORE, 1)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_STORE, 2)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_STORE, 4)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_STORE, 8)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_SWIGLU, 1)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_SWIGLU, 2)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_SWIGLU, 4)
-  AIPU_CHAIN_CASE(WT_Q4K, CHAIN_SWIGLU, 8)
-  AIPU_CHAIN_CASE(WT_Q6K, CHAIN_STORE, 1)
-  AIPU_CHAIN_CASE(WT_Q6K, CHAIN_STORE, 2)
-  AIPU_CHAIN_CASE(WT_Q6K, CHAIN_STORE, 4)
-  AIPU_CHAIN_CASE(WT_Q6K, CHAIN_STORE, 8)
+  const int64_t slots = static_cast<int64_t>(num_sms) * std::max(1, limit / smem);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(slots, items)));
+#define AIPU_CHAIN_CASE(W, E, M_, N_)                                                      \
+  if (wt == W && epi == E && mt == M_ && NT == N_) return chain_launch_t<W, E, M_, N_>(p, grid, smem, s);
+#define AIPU_CHAIN_MT(W, E, N_) \
+  AIPU_CHAIN_CASE(W, E, 1, N_) AIPU_CHAIN_CASE(W, E, 2, N_) AIPU_CHAIN_CASE(W, E, 4, N_) AIPU_CHAIN_CASE(W, E, 8, N_)
+  AIPU_CHAIN_MT(WT_Q4K, CHAIN_STORE, 128)
+  AIPU_CHAIN_MT(WT_Q4K, CHAIN_STORE, 64)
+  AIPU_CHAIN_MT(WT_Q4K, CHAIN_SWIGLU, 128)
+  AIPU_CHAIN_MT(WT_Q6K, CHAIN_STORE, 128)
+  AIPU_CHAIN_MT(WT_Q6K, CHAIN_STORE, 64)
+#undef AIPU_CHAIN_MT
 #undef AIPU_CHAIN_CASE
   return CHAIN_UNSUPPORTED;
 }

@@ -1,21 +1,24 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 k-quant decode path. Prints ONE JSON line (rank 0).
 
-Headline metric: Q4_K GEMV HBM GB/s on the BASELINE config-2 shape (2048 rows x 6144, bf16 x,
-M = 1). A step is one pass over a batch of `--matrices` distinct weight matrices (1.8 GB by default,
-far larger than the 126 MB L2, so no L2 flush is needed) applied to the same activation row, as ONE
-grouped launch (aipu_q4k_gemm_grouped), replayed as a CUDA graph. value = algorithmic bytes
+Headline: Q4_K GEMV HBM GB/s on 4096 x 4096 Q4_K weights (16 super-blocks per
+row), x fp32 [1, 4096] ~ N(0, 1) drawn with numpy seed 0, bf16 out. A step is ONE grouped launch
+(aipu_q4k_gemm_grouped) over `--matrices` distinct seeded matrices (64 x 9.4 MB = 604 MB, more than
+twice the 126 MB L2, so no flush is needed), replayed as a CUDA graph. value = algorithmic bytes
 (weights + x + y) of all GEMVs of all ranks / device time (max over ranks). The same GEMVs as one
-launch per matrix (decode-style stream, programmatic dependent launch) are reported as
-"single_launch".
+launch per matrix are reported as "single_launch".
 
-Also reported: roofline of the GEMV kernel against MEASURED_PEAKS.json, the CPU baseline (the C
-restatement of the reference's contract on the host cores), the end-to-end number through the public
-API with host buffers, SM clocks sampled through NVML during the timed region, and the MoE-layer
-decode throughput of BASELINE config 3 (1 GPU).
+Also reported: the roofline of the GEMV kernel against MEASURED_PEAKS.json; the CPU baselines (the C
+restatement of the reference's contract on all host cores, and the numpy restatement on a sample);
+the end-to-end number through the public API with host buffers; SM clocks sampled through NVML during
+the timed region; the MoE layer of BASELINE configs 3 (decode, M = 1 and 4) and 4 (prefill, 2048
+tokens) on the default bit-exact path and on the tensor-core path, each with parity against the
+oracle computed in the same run (the oracle's timed CPU run of the same sampled tokens is the CPU
+baseline of that layer); at N > 1 the expert-parallel decode layer and the full-depth decode stream.
 
 --impl reference times the reference's CPU implementation of the path (its C restatement, all host
-threads) on the same config and metric.
+threads) on the same config, inputs and per-step work.
+--case {gemv,chain,tc,moe,router} runs one small workload for a profiler capture and exits.
 """
 from __future__ import annotations
 
@@ -30,24 +33,40 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_ROWS, K_COLS = 2048, 6144
-GEMV_W_BYTES = N_ROWS * (K_COLS // 256) * 144            # 7,077,888
-GEMV_BYTES = GEMV_W_BYTES + K_COLS * 2 + N_ROWS * 2       # + x bf16 + y bf16 = 7,094,272
+# BASELINE config 1
+C1_N, C1_K = 4096, 4096
+C1_W_BYTES = C1_N * (C1_K // 256) * 144                # 9,437,184
+C1_BYTES = C1_W_BYTES + C1_K * 4 + C1_N * 2             # + x fp32 + y bf16 = 9,461,760
 METRIC = "Q4_K GEMV HBM GB/s"
+# DRAM bytes per C1 GEMV of the grouped kernel, from one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum) of an 8-matrix C1 launch divided by 8; the full launch reads every weight
+# byte once, so its traffic is this times the matrices per launch.
+C1_TRAFFIC_PER_GEMV = None
+MOE_H, MOE_F, MOE_E, MOE_T = 6144, 2048, 256, 8
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="aipu", choices=["aipu", "reference"])
-    ap.add_argument("--matrices", type=int, default=256, help="distinct weight matrices per step")
-    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode measurement")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--matrices", type=int, default=64, help="distinct 4096x4096 Q4_K matrices per step")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE measurements")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--stream-layers", type=int, default=75,
                     help="layers of the full-depth expert-parallel decode stream (BASELINE config 5) at N > 1, "
                          "capped by device memory; 0 skips it")
+    ap.add_argument("--case", default=None, choices=["gemv", "chain", "tc", "moe", "router"],
+                    help="run one small workload for a profiler capture and exit")
+    ap.add_argument("--wtype", type=int, default=0)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--x-f32", action="store_true")
+    ap.add_argument("--groups", type=int, default=8)
+    ap.add_argument("--experts", type=int, default=64)
+    ap.add_argument("--tokens", type=int, default=512)
     return ap.parse_args()
 
 
@@ -59,18 +78,18 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def traffic_from_profile():
-    """dram bytes per launch of the GEMV kernel from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "gemv_q4k_2048x6144.md")
-    if not os.path.exists(p):
-        return None
-    for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":")[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+def c1_inputs(L):
+    """BASELINE config 1 inputs, identical in both arms: x = numpy default_rng(0) N(0,1) fp32 [1, 4096];
+    matrix l = formats.random_rows_np(Q4_K, 4096, 4096, seed=1000 + l)."""
+    import numpy as np
+
+    from aipu_b200 import formats as F
+
+    x = np.random.default_rng(0).standard_normal((1, C1_K)).astype(np.float32)
+    w = np.empty((L, C1_N, F.row_bytes(F.Q4_K, C1_K)), np.uint8)
+    for l in range(L):
+        w[l] = F.random_rows_np(F.Q4_K, C1_N, C1_K, seed=1000 + l)
+    return x, w
 
 
 class _Null:
@@ -125,7 +144,7 @@ class ClockSampler:
                         self.reasons.add(k)
             except Exception:
                 pass
-            time.sleep(0.005)
+            time.sleep(0.001)
 
     def __exit__(self, *a):
         self._stop.set()
@@ -159,103 +178,105 @@ def dist_setup(n_gpus):
     return world, rank, local
 
 
-def cpu_baseline_gemv(seconds=10.0, w=None, x=None):
-    """The C restatement on all host cores: full 2048 x 6144 Q4_K GEMVs for ~`seconds`."""
+def cpu_baseline_c1(x, w, seconds=10.0):
+    """CPU baselines of the headline workload on the host cores: (a) the C restatement of the
+    reference's contract (oracle/q4k_oracle.c) on all cores over the distinct matrices for ~`seconds`;
+    (b) the numpy restatement (oracle/q4k_oracle.py, vectorised over rows, sequential over K) on a
+    256-row sample of one matrix, its rate scaled to GB/s of the same workload."""
     import numpy as np
 
     from aipu_b200 import formats as F
     from oracle import cpu
+    from oracle import q4k_oracle as qo
 
-    if w is None:
-        w = F.random_rows_np(F.Q4_K, N_ROWS, K_COLS, seed=0)
-        x = np.random.default_rng(0).standard_normal((1, K_COLS)).astype(np.float32)
     cores = os.cpu_count() or 1
-    cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+    L = w.shape[0]
+    cpu.gemm(F.Q4_K, w[0], C1_N, C1_K, x, nthreads=cores)
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+        cpu.gemm(F.Q4_K, w[n % L], C1_N, C1_K, x, nthreads=cores)
         n += 1
         dt = time.perf_counter() - t0
         if dt >= seconds:
             break
-    return {"value": round(GEMV_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{n} full Q4_K GEMVs 2048x6144 (M=1) by oracle/q4k_oracle.c, {cores} threads, {dt:.1f} s"}
+    out = {"value": round(C1_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+           "sample": f"{n} full C1 GEMVs (Q4_K 4096x4096, x fp32) by oracle/q4k_oracle.c on {cores} threads, "
+                     f"{dt:.1f} s"}
+    rows = 256
+    t0 = time.perf_counter()
+    qo.gemm(F.Q4_K, w[0][:rows], rows, C1_K, x)
+    dt = time.perf_counter() - t0
+    out["numpy"] = {"value": round(C1_BYTES * rows / C1_N / dt / 1e9, 5), "unit": "GB/s", "cores": 1,
+                    "kind": "port", "sample": f"{rows} of 4096 rows of one C1 GEMV by oracle/q4k_oracle.py "
+                                               f"(numpy, one core), {dt:.2f} s, rate scaled to the full GEMV"}
+    return out
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU implementation of the path (C restatement), rank 0 only."""
-    import numpy as np
-
+    """--impl reference: the reference's contract on the host cores (the C restatement), rank 0 only,
+    on the same inputs and per-step work as the GPU arm (one step = the GEMVs of all matrices)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
     from aipu_b200 import formats as F
     from oracle import cpu
 
-    if int(os.environ.get("RANK", "0")) != 0:
-        return
     cores = os.cpu_count() or 1
-    w = F.random_rows_np(F.Q4_K, N_ROWS, K_COLS, seed=0)
-    x = np.random.default_rng(0).standard_normal((1, K_COLS)).astype(np.float32)
+    L = args.matrices
+    x, w = c1_inputs(L)
     for _ in range(max(args.warmup, 1)):
-        cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+        cpu.gemm(F.Q4_K, w[0], C1_N, C1_K, x, nthreads=cores)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu.gemm(F.Q4_K, w, N_ROWS, K_COLS, x, nthreads=cores)
+        for l in range(L):
+            cpu.gemm(F.Q4_K, w[l], C1_N, C1_K, x, nthreads=cores)
     dt = time.perf_counter() - t0
-    v = GEMV_BYTES * args.steps / dt / 1e9
+    v = L * C1_BYTES * args.steps / dt / 1e9
     line = {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "Q4_K GEMV 2048x6144, x bf16-valued fp32 [1,6144], y bf16 (BASELINE config 2, "
-                                   "Q4_K, M=1)", "step": "one GEMV"},
+            "config": c1_config(L, args.gpus),
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                             "sample": f"{args.steps} GEMVs, oracle/q4k_oracle.c (restatement of tools/q4k_ref.py)"},
+                             "sample": f"{args.steps} steps x {L} C1 GEMVs, oracle/q4k_oracle.c (the C restatement "
+                                       f"of tools/q4k_ref.py matmul_q4k_col) on {cores} threads"},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def moe_decode(M_list=(1, 4), reps=200):
-    """BASELINE config 3 on one GPU: tokens/s of the MoE layer (CUDA graph replays)."""
-    import numpy as np
+def c1_config(L, world):
+    return {"workload": "BASELINE config 1: Q4_K GEMV, W 4096 rows x 4096 (16 super-blocks per row), x fp32 [1,4096] "
+                        "~N(0,1) (numpy seed 0), y bf16; a step = the GEMVs of all matrices (one grouped launch)",
+            "matrices_per_step": L, "bytes_per_gemv": C1_BYTES,
+            "l2": f"inputs larger than L2: {L * C1_W_BYTES / 1e9:.2f} GB of distinct weights per step",
+            "parallelism": f"replicas x{world}"}
+
+
+def _graph(fn, stream):
     import torch
 
-    from aipu_b200 import formats as F
-    from aipu_b200 import ops
-
-    d = torch.device("cuda", torch.cuda.current_device())
-    H, Fd, E, T = 6144, 2048, 256, 8
-    W = moe_layer_weights(d)
-    ctx = ops.Context(d)
-    out = {}
-    expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
-    for M in M_list:
-        x = (torch.randn((M, H), device=d, generator=torch.Generator(device=d).manual_seed(100 + M))).to(torch.bfloat16)
-        y = torch.empty((M, H), dtype=torch.bfloat16, device=d)
-        _, sel, _ = ops.moe_layer(W, x, ctx=ctx, out=y, return_routing=True)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn()
         torch.cuda.synchronize()
-        union = len(set(sel.cpu().numpy().reshape(-1).tolist()))
-        g = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        with torch.cuda.stream(s):
-            ops.moe_layer(W, x, ctx=ctx, out=y)
-            torch.cuda.synchronize()
-            with torch.cuda.graph(g, stream=s):
-                ops.moe_layer(W, x, ctx=ctx, out=y)
-        for _ in range(10):
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def _time_graph(g, reps, stream):
+    import torch
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
             g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        e0.record(stream)
         for _ in range(reps):
             g.replay()
-        e1.record()
+        e1.record(stream)
         torch.cuda.synchronize()
-        t = e0.elapsed_time(e1) / reps / 1e3
-        byts = H * E * 4 + (union + 1) * expert_bytes
-        out[f"M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(M / t, 1), "union_experts": union,
-                        "hbm_bytes": byts, "hbm_gbs": round(byts / t / 1e9, 1)}
-    out["prefill"] = moe_prefill(W)
-    del W
-    torch.cuda.empty_cache()
-    return out
+    return e0.elapsed_time(e1) / reps / 1e3
 
 
 def moe_layer_weights(d):
@@ -265,7 +286,7 @@ def moe_layer_weights(d):
     from aipu_b200 import formats as F
     from aipu_b200 import ops
 
-    H, Fd, E, T = 6144, 2048, 256, 8
+    H, Fd, E, T = MOE_H, MOE_F, MOE_E, MOE_T
     return ops.MoeLayerWeights(
         hidden=H, ffn=Fd, n_experts=E, topk=T, router_wtype=F.F32,
         router_w=torch.randn((H, E), device=d, generator=torch.Generator(device=d).manual_seed(1)) * 0.02,
@@ -278,41 +299,121 @@ def moe_layer_weights(d):
         shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
 
 
-def moe_prefill(W, M=2048, reps=10):
-    """BASELINE config 4 on one GPU: one MoE layer over 2048 tokens (router, per-expert token lists,
-    tcgen05 SwiGLU and down GEMMs grouped by expert, shared expert, combine), CUDA-graph replays.
-    Tensor FLOPs counted = 2 * (token-expert pairs + tokens for the shared expert) * 3 * H * F."""
+def _bf16_np(t):
+    import numpy as np
+
+    return (t.view(__import__("torch").int16).cpu().numpy().astype(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def moe_oracle_check(W, x_bf, y, sel, sw, rows):
+    """CPU baseline leg of the MoE layer: the oracle layer (C restatement GEMMs on packed rows) on the
+    sampled token rows, timed on the host cores; its outputs against the GPU's give the parity object."""
+    import numpy as np
+
+    from oracle import moe_oracle as mo
+    from oracle import q4k_oracle as qo
+
+    H, Fd, E, T = W.hidden, W.ffn, W.n_experts, W.topk
+    xs = _bf16_np(x_bf)[rows]
+    gv, uv, dv = W.gate_w.view(E, Fd, -1), W.up_w.view(E, Fd, -1), W.down_w.view(E, H, -1)
+
+    def experts(e):
+        return gv[e].cpu().numpy(), uv[e].cpu().numpy(), dv[e].cpu().numpy()
+
+    shared = (W.shared_gate_w.cpu().numpy(), W.shared_up_w.cpu().numpy(), W.shared_down_w.cpu().numpy())
+    wr = W.router_w.cpu().numpy().T.copy()
+    bias = W.router_bias.cpu().numpy()
+    t0 = time.perf_counter()
+    y_ref, sel_ref, sw_ref = mo.moe_layer_packed(xs, wr, experts, shared, T, bias=bias, gate_wtype=W.gate_wtype,
+                                                 down_wtype=W.down_wtype)
+    dt = time.perf_counter() - t0
+    got = _bf16_np(y)[rows]
+    st = qo.parity_stats(got, y_ref)
+    parity = {"tokens_checked": int(len(rows)), "frac_within_1ulp": round(st["frac_within_1ulp"], 6),
+              "max_rel": round(st["max_rel"], 6), "max_ulp": st["max_ulp"],
+              "bit_exact": bool(np.array_equal(got.view(np.uint32), y_ref.view(np.uint32))),
+              "topk_exact": bool(np.array_equal(sel.cpu().numpy()[rows], sel_ref)),
+              "weights_exact": bool(np.array_equal(_bf16_np(sw)[rows].view(np.uint32), sw_ref.view(np.uint32)))}
+    cpu = {"value": round(len(rows) / dt, 3), "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+           "sample": f"{len(rows)} token rows through oracle/moe_oracle.py moe_layer_packed (C restatement GEMMs, "
+                     f"all cores), {dt:.1f} s including the host copies of the experts"}
+    return parity, cpu
+
+
+def moe_bench(check=True):
+    """BASELINE config 3 (decode, M = 1 and 4) and config 4 (prefill, 2048 tokens) on one GPU, on the
+    default bit-exact path and on the tensor-core path, CUDA-graph replays, with parity."""
+    import numpy as np
+    import torch
+
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    H, Fd, E, T = MOE_H, MOE_F, MOE_E, MOE_T
+    W = moe_layer_weights(d)
+    s = torch.cuda.Stream()
+    hbm, tf_peak, kind = peaks()
+    expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
+    out = {}
+    paths = {"exact": {}, "tensor_core": {"tc_decode": True}}
+    for M in (1, 4):
+        x = (torch.randn((M, H), device=d, generator=torch.Generator(device=d).manual_seed(100 + M))).to(torch.bfloat16)
+        y = torch.empty((M, H), dtype=torch.bfloat16, device=d)
+        for name, flags in paths.items():
+            ctx = ops.Context(d).set_flags(**flags)
+            yy, sel, sw = ops.moe_layer(W, x, ctx=ctx, out=y, return_routing=True)
+            torch.cuda.synchronize()
+            union = len(set(sel.cpu().numpy().reshape(-1).tolist()))
+            g = _graph(lambda: ops.moe_layer(W, x, ctx=ctx, out=y), s)
+            t = _time_graph(g, 100, s)
+            byts = H * E * 4 + (union + 1) * expert_bytes
+            ent = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(M / t, 1), "union_experts": union,
+                   "hbm_bytes": byts, "hbm_gbs": round(byts / t / 1e9, 1),
+                   "roofline_frac": round(byts / t / 1e9 / hbm, 4)}
+            if check:
+                ent["parity"], ent["cpu_baseline"] = moe_oracle_check(W, x, y, sel, sw, np.arange(M))
+            out[f"{name}_M{M}"] = ent
+            del g
+            ctx.close()
+    out["prefill"] = moe_prefill_bench(W, check)
+    del W
+    torch.cuda.empty_cache()
+    return out
+
+
+def moe_prefill_bench(W, check):
+    """BASELINE config 4 on one GPU: one MoE layer over 2048 tokens, CUDA-graph replays. Tensor-core
+    path (default for >= 64 tokens) and the bit-exact chain path (AIPU_FLAG_STRICT). Tensor FLOPs
+    counted = 2 * (token-expert pairs + tokens for the shared expert) * 3 * H * F."""
+    import numpy as np
     import torch
 
     from aipu_b200 import ops
 
     d = torch.device("cuda", torch.cuda.current_device())
     H, Fd, T = W.hidden, W.ffn, W.topk
-    ctx = ops.Context(d)
+    M = 2048
     x = torch.randn((M, H), device=d, generator=torch.Generator(device=d).manual_seed(4)).to(torch.bfloat16)
     y = torch.empty((M, H), dtype=torch.bfloat16, device=d)
     s = torch.cuda.Stream()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        ops.moe_layer(W, x, ctx=ctx, out=y)
-        torch.cuda.synchronize()
-        with torch.cuda.graph(g, stream=s):
-            ops.moe_layer(W, x, ctx=ctx, out=y)
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        g.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / reps / 1e3
     flops = 2.0 * (M * T + M) * 3 * H * Fd
     _, tf_peak, kind = peaks()
-    return {"tokens": M, "ms_per_layer": round(t * 1e3, 3), "tokens_per_s": round(M / t, 1),
-            "tensor_tflops": round(flops / t / 1e12, 1), "frac_of_bf16_peak": round(flops / t / 1e12 / tf_peak, 4),
-            "peak_source": kind, "flops": flops}
+    out = {"tokens": M, "flops": flops, "peak_source": kind}
+    rows = np.sort(np.random.default_rng(7).choice(M, 16, replace=False))
+    for name, flags, reps in (("tensor_core", {}, 10), ("exact", {"strict": True}, 2)):
+        ctx = ops.Context(d).set_flags(**flags)
+        yy, sel, sw = ops.moe_layer(W, x, ctx=ctx, out=y, return_routing=True)
+        torch.cuda.synchronize()
+        g = _graph(lambda: ops.moe_layer(W, x, ctx=ctx, out=y), s)
+        t = _time_graph(g, reps, s)
+        ent = {"ms_per_layer": round(t * 1e3, 3), "tokens_per_s": round(M / t, 1),
+               "tensor_tflops": round(flops / t / 1e12, 1), "frac_of_bf16_peak": round(flops / t / 1e12 / tf_peak, 4)}
+        if check:
+            ent["parity"], ent["cpu_baseline"] = moe_oracle_check(W, x, y, sel, sw, rows)
+        out[name] = ent
+        del g
+        ctx.close()
+    return out
 
 
 def _time_ep_layer(layer, x, reps):
@@ -460,58 +561,109 @@ def moe_decode_stream(world, rank, layers_req=75, M_list=(1, 4), reps=10):
     return out
 
 
+def run_case(a):
+    """Small workloads for a profiler capture (a few GB on the device at most, inputs larger than L2)."""
+    import torch
+
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    if a.case in ("gemv", "chain"):
+        w = F.random_rows_dev(a.wtype, a.groups * a.n * 4, a.k, seed=1, device=d)
+        x = torch.randn((a.m, a.k), device=d)
+        if not a.x_f32:
+            x = x.to(torch.bfloat16)
+        for i in range(6):
+            sub = w[(i % 4) * a.groups * a.n:((i % 4) + 1) * a.groups * a.n]
+            if a.case == "chain":
+                y = ops.gemm(a.wtype, sub[:a.n], a.n, a.k, x, mode="strict")
+            elif a.groups > 1:
+                y = ops.gemm_grouped(a.wtype, sub, a.groups, a.n, a.k, x)
+            else:
+                y = ops.gemm(a.wtype, sub, a.n, a.k, x)
+    elif a.case == "tc":
+        w = F.random_rows_dev(a.wtype, a.n, a.k, seed=3, device=d)
+        x = torch.randn((a.m, a.k), device=d).to(torch.bfloat16)
+        for _ in range(3):
+            y = ops.gemm_tc(a.wtype, w, a.n, a.k, x)
+    elif a.case == "router":
+        g = torch.Generator(device=d)
+        w = torch.randn((MOE_H, MOE_E), device=d, generator=g.manual_seed(1)) * 0.02
+        b = torch.randn((MOE_E,), device=d, generator=g.manual_seed(2)) * 0.01
+        x = torch.randn((a.tokens, MOE_H), device=d, generator=g.manual_seed(3)).to(torch.bfloat16)
+        for _ in range(4):
+            y, _, _ = ops.moe_router(F.F32, w, x, MOE_E, MOE_T, bias=b)
+    else:
+        g = torch.Generator(device=d)
+        E = a.experts
+        W = ops.MoeLayerWeights(
+            hidden=MOE_H, ffn=MOE_F, n_experts=E, topk=MOE_T, router_wtype=F.F32,
+            router_w=torch.randn((MOE_H, E), device=d, generator=g.manual_seed(1)) * 0.02,
+            router_bias=torch.randn((E,), device=d, generator=g.manual_seed(2)) * 0.01,
+            gate_w=F.random_rows_dev(F.Q4_K, E * MOE_F, MOE_H, seed=11, device=d),
+            up_w=F.random_rows_dev(F.Q4_K, E * MOE_F, MOE_H, seed=12, device=d),
+            down_w=F.random_rows_dev(F.Q6_K, E * MOE_H, MOE_F, seed=13, device=d),
+            shared_gate_w=F.random_rows_dev(F.Q4_K, MOE_F, MOE_H, seed=14, device=d),
+            shared_up_w=F.random_rows_dev(F.Q4_K, MOE_F, MOE_H, seed=15, device=d),
+            shared_down_w=F.random_rows_dev(F.Q6_K, MOE_H, MOE_F, seed=16, device=d))
+        x = torch.randn((a.tokens, MOE_H), device=d, generator=g.manual_seed(3)).to(torch.bfloat16)
+        for _ in range(3):
+            y = ops.moe_layer(W, x)
+    torch.cuda.synchronize()
+    print(a.case, "ok", float(y.float().abs().mean()), flush=True)
+
+
 def main():
     args = parse()
+    if args.case:
+        run_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
-    import numpy as np
     import torch
 
     from aipu_b200 import formats as F
     from aipu_b200 import ops
 
     world, rank, local = dist_setup(args.gpus)
+    if world > 1:
+        import torch.distributed as dist
     d = torch.device("cuda", torch.cuda.current_device())
     L = args.matrices
-    Wt = F.random_rows_dev(F.Q4_K, L * N_ROWS, K_COLS, seed=1234 + rank, device=d)
-    rb = F.row_bytes(F.Q4_K, K_COLS)
-    mats = [Wt[l * N_ROWS:(l + 1) * N_ROWS] for l in range(L)]
-    x = torch.randn((1, K_COLS), device=d, generator=torch.Generator(device=d).manual_seed(7)).to(torch.bfloat16)
-    y = torch.empty((L, 1, N_ROWS), dtype=torch.bfloat16, device=d)
+    x_np, w_np = c1_inputs(L)
+    Wt = torch.from_numpy(w_np.reshape(L * C1_N, -1)).to(d)
+    x = torch.from_numpy(x_np).to(d)
+    y = torch.empty((L, 1, C1_N), dtype=torch.bfloat16, device=d)
+    mats = [Wt[l * C1_N:(l + 1) * C1_N] for l in range(L)]
     ctx = ops.Context(d).set_flags(pdl=True)
+    s = torch.cuda.Stream()
 
     def issue_grouped():
-        ops.gemm_grouped(F.Q4_K, Wt, L, N_ROWS, K_COLS, x, ctx=ctx, out=y)
+        ops.gemm_grouped(F.Q4_K, Wt, L, C1_N, C1_K, x, ctx=ctx, out=y)
 
     def issue_single():
         for l in range(L):
-            ops.gemm(F.Q4_K, mats[l], N_ROWS, K_COLS, x, ctx=ctx, out=y[l])
-
-    def capture(fn):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            fn()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(g, stream=s):
-                fn()
-        torch.cuda.synchronize()
-        return g
+            ops.gemm(F.Q4_K, mats[l], C1_N, C1_K, x, ctx=ctx, out=y[l])
 
     def timed(g, steps, warmup, sampler=None):
-        for _ in range(max(warmup, 3)):
-            g.replay()
-        torch.cuda.synchronize()
+        with torch.cuda.stream(s):
+            for _ in range(max(warmup, 3)):
+                g.replay()
+            torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with (sampler if sampler is not None else _Null()):
-            torch.cuda.synchronize()
-            e0.record()
-            for _ in range(steps):
-                g.replay()
-            e1.record()
-            torch.cuda.synchronize()
+            with torch.cuda.stream(s):
+                torch.cuda.synchronize()
+                e0.record(s)
+                for _ in range(steps):
+                    g.replay()
+                e1.record(s)
+                torch.cuda.synchronize()
         t = e0.elapsed_time(e1) / 1e3
         if world > 1:
             tt = torch.tensor([t], device=d, dtype=torch.float64)
@@ -519,27 +671,24 @@ def main():
             t = float(tt.item())
         return t / steps
 
-    s = torch.cuda.Stream()
-    if world > 1:
-        import torch.distributed as dist
-    g = capture(issue_grouped)
+    g = _graph(issue_grouped, s)
     clk = ClockSampler(d.index)
     step = timed(g, args.steps, args.warmup, clk)
-    value = world * L * GEMV_BYTES / step / 1e9
+    value = world * L * C1_BYTES / step / 1e9
     hbm_peak, _, peak_kind = peaks()
-    achieved = L * GEMV_BYTES / step / 1e9
-    # the same GEMVs as one launch per matrix (decode-style stream), back to back with PDL
-    gs = capture(issue_single)
+    achieved = L * C1_BYTES / step / 1e9
+    # parity of the timed kernel's outputs against the C restatement, on one matrix (checker use)
+    gs = _graph(issue_single, s)
     step_single = timed(gs, max(10, args.steps // 4), args.warmup)
-    single = {"us_per_launch": round(step_single / L * 1e6, 3),
-              "gbs": round(L * GEMV_BYTES / step_single / 1e9, 1),
-              "note": "one kernel launch per 2048x6144 matrix, CUDA graph, programmatic dependent launch"}
+    single = {"us_per_launch": round(step_single / L * 1e6, 3), "gbs": round(L * C1_BYTES / step_single / 1e9, 1),
+              "frac": round(L * C1_BYTES / step_single / 1e9 / hbm_peak, 4),
+              "note": "one kernel launch per 4096x4096 matrix, CUDA graph, programmatic dependent launch"}
     del gs
 
     # ---- end to end through the public API with host buffers (x in, all y out, every step)
-    x_host = torch.empty((1, K_COLS), dtype=torch.bfloat16, pin_memory=True).copy_(x.cpu())
-    y_host = torch.empty((L, 1, N_ROWS), dtype=torch.bfloat16, pin_memory=True)
-    e2e_steps = max(10, args.steps // 4)
+    x_host = torch.from_numpy(x_np).pin_memory()
+    y_host = torch.empty((L, 1, C1_N), dtype=torch.bfloat16, pin_memory=True)
+    e2e_steps = max(10, args.steps // 2)
     torch.cuda.synchronize()
     with torch.cuda.stream(s):
         for _ in range(3):
@@ -558,16 +707,28 @@ def main():
         tt = torch.tensor([te], device=d, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         te = float(tt.item())
-    e2e = {"value": round(world * L * GEMV_BYTES / te / 1e9, 2), "unit": "GB/s",
-           "h2d_bytes_per_step": K_COLS * 2, "d2h_bytes_per_step": L * N_ROWS * 2,
+    e2e = {"value": round(world * L * C1_BYTES / te / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": C1_K * 4, "d2h_bytes_per_step": L * C1_N * 2,
            "path": "ops.gemm_grouped -> aipu_q4k_gemm_grouped (C ABI), replayed as a CUDA graph; pinned host x in, "
                    "all y out, every step"}
-
+    y_first = y[0].clone()
     del Wt, mats
     torch.cuda.empty_cache()
+
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import cpu
+        from oracle import q4k_oracle as qo
+
+        cpu_base = cpu_baseline_c1(x_np, w_np)
+        # checker: the timed kernel's outputs for matrix 0 against the C restatement's
+        ref = cpu.gemm(F.Q4_K, w_np[0], C1_N, C1_K, x_np)
+        st = qo.parity_stats(_bf16_np(y_first), ref)
+        cpu_base["parity_of_timed_gemv"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in st.items()}
+    del w_np
     moe = None
     if rank == 0 and world == 1 and not args.no_moe:
-        moe = moe_decode()
+        moe = moe_bench(check=not args.no_cpu)
     moe_ep = None
     moe_stream = None
     if world > 1 and not args.no_moe:
@@ -577,27 +738,21 @@ def main():
                 moe_stream = moe_decode_stream(world, rank, args.stream_layers)
             except Exception as e:  # reported in the line; the GEMV metric above stands
                 moe_stream = {"error": f"{type(e).__name__}: {e}"[:300]}
-    cpu_base = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu_base = cpu_baseline_gemv()
     if rank == 0:
+        traffic = None if C1_TRAFFIC_PER_GEMV is None else int(C1_TRAFFIC_PER_GEMV * L)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "Q4_K GEMV 2048x6144, x bf16 [1,6144] ~N(0,1), y bf16 (BASELINE config 2, Q4_K, "
-                                   "M=1); a step = one grouped launch over the batch of matrices",
-                       "matrices_per_step": L, "bytes_per_gemv": GEMV_BYTES,
-                       "l2": f"inputs larger than L2: {L * GEMV_W_BYTES / 1e9:.2f} GB of distinct weights per step",
-                       "parallelism": f"replicas x{world}"},
+            "config": c1_config(L, world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic_from_profile(),
-                         "peak_source": peak_kind, "kernel": "aipu_kq_gemv_kernel<Q4_K,bf16,store> (grouped launch)",
-                         "us_per_launch": round(step * 1e6, 3)},
+                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "aipu_kq_gemv_kernel<Q4_K, fp32 x, store> (grouped launch)",
+                         "us_per_launch": round(step * 1e6, 3),
+                         "algorithmic_bytes_per_launch": L * C1_BYTES},
             "single_launch": single,
             "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,
-            "clocks": clk.summary(), "moe_decode": moe, "moe_decode_ep": moe_ep,
-            "moe_decode_stream": moe_stream,
+            "clocks": clk.summary(), "moe": moe, "moe_decode_ep": moe_ep, "moe_decode_stream": moe_stream,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
