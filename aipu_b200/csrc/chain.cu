@@ -607,8 +607,10 @@ int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bo
   p.w_bytes = 2 * NT * pitch;
   p.stage_bytes = p.w_bytes + mt * 256 * 8;
   const int limit = 232448 - 1024;
-  // NT = 64: at most three CTAs per SM, two stages each when that fits
-  const int per_cta = (NT == 64) ? std::max(2 * p.stage_bytes + 128, (limit - 3 * 1024) / 3) : limit;
+  // Several CTAs per SM when there are more items than SMs (more warps per scheduler hide the chains'
+  // latencies): NT = 64 tiles three per SM, NT = 128 tiles two per SM, two or more stages each.
+  const int ctas_per_sm = (NT == 64) ? 3 : (items_of(NT) > num_sms ? 2 : 1);
+  const int per_cta = std::max(2 * p.stage_bytes + 128, (limit - ctas_per_sm * 1024) / ctas_per_sm);
   p.nstages = std::min(CH_MAXS, (std::min(per_cta, limit) - 128) / p.stage_bytes);
   if (p.nstages < 2) {
     p.nstages = std::min(CH_MAXS, (limit - 128) / p.stage_bytes);
