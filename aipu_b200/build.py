@@ -14,6 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaipu_q4k.so")
+DUMP = os.path.join(HERE, "aipu_dequant_dump")  # CLI over the C ABI (csrc/dequant_dump.cpp)
 
 SOURCES = ["capi.cu", "chain.cu", "ep.cu", "gemv.cu", "kernels.cu", "lmhead.cu", "tc_gemm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -63,6 +64,13 @@ def build(verbose: bool = False, force: bool = False, extra: list[str] | None = 
         raise subprocess.CalledProcessError(1, failed[0])
     if force or _stale(LIB, objs):
         cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    src = os.path.join(CSRC, "dequant_dump.cpp")
+    if force or _stale(DUMP, [src, LIB, os.path.join(ROOT, "include", "aipu_q4k.h")]):
+        cmd = [nvcc()] + ARCH + ["-O2", "-std=c++17", "-I" + os.path.join(ROOT, "include"), "-o", DUMP, src, "-L" + HERE,
+               "-laipu_q4k", "-Xlinker", "-rpath,$ORIGIN"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

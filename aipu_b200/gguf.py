@@ -364,3 +364,52 @@ def synthetic_moe_gguf(path: str, layers: int, H: int, Fd: int, E: int, topk: in
     write_gguf(path, specs, {"general.architecture": arch, f"{arch}.block_count": layers,
                              f"{arch}.expert_count": E, f"{arch}.expert_used_count": topk,
                              f"{arch}.expert_weights_scale": 2.5, "general.quantization_version": 2})
+
+
+# -------------------------------------------------------------------- integrity manifest
+GGML_TYPE_NAMES = {GGML_F32: "F32", GGML_F16: "F16", GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K", GGML_Q6_K: "Q6_K"}
+
+
+def tensor_manifest(gf: GGUFFile) -> Dict[str, object]:
+    """Per-tensor integrity manifest of a GGUF: for every tensor its name, type name, ggml type id,
+    shape (ne), absolute source offset, byte length and sha256 of its bytes. The per-tensor field
+    names are those of the reference's provisioning manifest (tools/provision_image.py:295-340), so a
+    manifest written by either side can be checked against a GGUF by verify_manifest; the
+    reference's flash-image fields (image offsets, segments, image hash) belong to its FPGA boot
+    image and are not produced here."""
+    import hashlib
+
+    out = []
+    for name, t in sorted(gf.tensors.items(), key=lambda kv: kv[1].offset):
+        out.append({"name": name, "type": GGML_TYPE_NAMES.get(t.ggml_type, str(t.ggml_type)),
+                    "ggml_type": t.ggml_type, "shape": list(t.ne), "src_offset": t.offset, "length": t.nbytes,
+                    "sha256": hashlib.sha256(bytes(gf.raw(name))).hexdigest()})
+    import os
+
+    return {"source_gguf": os.path.basename(gf.path), "tensor_count": len(out), "tensors": out}
+
+
+def verify_manifest(gf: GGUFFile, manifest: Dict[str, object]) -> List[str]:
+    """Check every tensor a manifest lists against the GGUF: present, same ggml type, shape and byte
+    length, and the sha256 of its bytes equal to the manifest's (tools/provision_image.py:385-440 does
+    the same for the reference's flash image). Returns the failures (empty when all match)."""
+    import hashlib
+
+    fails = []
+    for t in manifest.get("tensors", []):
+        name = t["name"]
+        if name not in gf.tensors:
+            fails.append(f"{name}: not present in the GGUF")
+            continue
+        info = gf.tensors[name]
+        if "ggml_type" in t and int(t["ggml_type"]) != info.ggml_type:
+            fails.append(f"{name}: ggml type {info.ggml_type} != manifest {t['ggml_type']}")
+        if "shape" in t and [int(v) for v in t["shape"]] != list(info.ne):
+            fails.append(f"{name}: shape {list(info.ne)} != manifest {t['shape']}")
+        if "length" in t and int(t["length"]) != info.nbytes:
+            fails.append(f"{name}: length {info.nbytes} != manifest {t['length']}")
+            continue
+        sha = hashlib.sha256(bytes(gf.raw(name))).hexdigest()
+        if sha != t.get("sha256"):
+            fails.append(f"{name}: sha256 {sha} != manifest {t.get('sha256')}")
+    return fails

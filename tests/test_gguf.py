@@ -121,3 +121,32 @@ def test_load_matrix_rejects_non_gemm_tensors(tmp_path):
             gguf.load_matrix(gf, "q8w", "cpu")
         m = gguf.load_matrix(gf, "okw", "cpu")
         assert (m.wtype, m.N, m.K) == (F.Q8_0, 4, 256)
+
+
+def test_manifest_round_trip_and_corruption(tmp_path):
+    """The per-tensor integrity manifest (the reference provisioning manifest's per-tensor fields) of a
+    reference-written GGUF verifies against it; a manifest in the reference's layout (extra image
+    fields) is accepted; a flipped byte, a wrong shape or a missing tensor is reported."""
+    import json
+
+    with gguf.GGUFFile(os.path.join(GOLDEN, "ref_synthetic.gguf")) as gf:
+        m = gguf.tensor_manifest(gf)
+        assert m["tensor_count"] == len(gf.tensors) and gguf.verify_manifest(gf, m) == []
+        ref_style = {"format_version": "provimg-1.0", "image_sha256": "0" * 64, "segments": [],
+                     "tensors": [dict(t, offset=i * 4096, segment="resident_hot") for i, t in enumerate(m["tensors"])]}
+        assert gguf.verify_manifest(gf, json.loads(json.dumps(ref_style))) == []
+        bad = json.loads(json.dumps(m))
+        bad["tensors"][0]["sha256"] = "f" * 64
+        bad["tensors"][1]["shape"] = [1, 2]
+        bad["tensors"].append({"name": "missing.weight", "sha256": "0" * 64})
+        fails = gguf.verify_manifest(gf, bad)
+        assert len(fails) == 3 and "sha256" in fails[0] and "shape" in fails[1] and "not present" in fails[2]
+    # a corrupted copy of the file fails against the manifest of the original
+    data = bytearray(open(os.path.join(GOLDEN, "ref_synthetic.gguf"), "rb").read())
+    t0 = m["tensors"][0]
+    data[t0["src_offset"] + 7] ^= 0x10
+    p = tmp_path / "corrupt.gguf"
+    p.write_bytes(bytes(data))
+    with gguf.GGUFFile(str(p)) as gf:
+        fails = gguf.verify_manifest(gf, m)
+        assert len(fails) == 1 and t0["name"] in fails[0]
