@@ -278,3 +278,99 @@ class Config:
         self.LM_TN = 4
         for k, v in kw.items():
             setattr(self, k, v)
+
+    # derived dimensions (tools/glm_model_q4k_ref.py:586-606), used by Weights
+    @property
+    def QK_DIM(self):
+        return self.NOPE + self.ROPE
+
+    @property
+    def HQK(self):
+        return self.H_HEADS * self.QK_DIM
+
+    @property
+    def HNOPE(self):
+        return self.H_HEADS * self.NOPE
+
+    @property
+    def HV(self):
+        return self.H_HEADS * self.V_DIM
+
+    @property
+    def SWIN(self):
+        return min(self.S_MAX, self.TOPK_ATTN)
+
+
+# the spec-decode slice configuration of the reference's full-model test bench
+# (tools/glm_model_q4k_ref.py:609-612)
+SPEC_SLICE = dict(MODEL_DIM=16, L=2, N_DENSE=1, VOCAB=16, H_HEADS=2, NOPE=4, ROPE=4, V_DIM=4, Q_LORA=8, KV_LORA=8,
+                  S_MAX=2, TOPK_ATTN=2, PE_N=2, N_EXPERT=4, TOPK=2, INTER_MOE=8, INTER_DENSE=32)
+
+
+# ---------------------------------------------------------------- seeded weights
+# These generators reproduce the reference's seeded weight draws (tools/glm_model_q4k_ref.py:522-544,
+# 619-658): the same numpy Generator calls in the same order, so Weights(cfg, seed) holds exactly the
+# reference's weights and tests written against the reference's seeds see the same numbers.
+def _mk_qw(rng, nout, nin):
+    """A QW of nout columns x nin: codes uniform 0..15; d = dmin = fp16(U(0.004, 0.012)) per column;
+    6-bit scales U{1..4} per sub-block with mins round(7.5 sc) + U{-1, 0, 1} clamped to 0..63, which
+    centres every sub-block's weights near zero."""
+    codes = [[int(v) for v in rng.integers(0, 16, nin)] for _ in range(nout)]
+    d = [f32_to_f16bits(rng.uniform(0.004, 0.012)) for _ in range(nout)]
+    dmin = list(d)
+    scales = []
+    for _ in range(nout):
+        sc = [int(v) for v in rng.integers(1, 5, 8)]
+        mn = [min(63, max(0, int(round(7.5 * v)) + int(rng.integers(-1, 2)))) for v in sc]
+        scales.append(list(_pack_6bit_scales(sc, mn)))
+    return QW(nout, nin, codes, d, dmin, scales)
+
+
+def _mk_bf16(rng, n, lo=-1.0, hi=1.0):
+    """n bf16 values drawn uniform in [lo, hi)."""
+    return [bf16(F32(v)) for v in rng.uniform(lo, hi, n)]
+
+
+def _mk_gamma(rng, n):
+    """RMSNorm scales: n bf16 values uniform in [0.6, 1.4)."""
+    return [bf16(F32(v)) for v in rng.uniform(0.6, 1.4, n)]
+
+
+class Weights:
+    """Every weight of one model, per layer, drawn from `seed` in the reference's order
+    (tools/glm_model_q4k_ref.py:619-658): embeddings, then per layer the two norm scales, the MLA
+    projections (W_dq, W_uq, W_uk, W_uv, W_o) and KV-cache rows, the router (k-major, a QW of
+    N_EXPERT columns), the dense FFN, the routed experts (gate, up, down) and the shared expert;
+    then the final norm and the LM head. This library computes the MoE and GEMM parts; the
+    attention weights are held for callers that run the rest of the block elsewhere."""
+
+    def __init__(self, cfg, seed=424242):
+        self.cfg = c = cfg
+        rng = np.random.default_rng(seed)
+        self.EMB = [_mk_bf16(rng, c.MODEL_DIM) for _ in range(c.VOCAB)]
+        names = ("G1", "G2", "W_dq", "W_uq", "W_uk", "W_uv", "W_o", "CKV", "KRP", "Wg", "Dg", "Du", "Dd", "Mg",
+                 "Mu", "Md", "SHg", "SHu", "SHd")
+        for n in names:
+            setattr(self, n, [])
+        for _ in range(c.L):
+            self.G1.append(_mk_gamma(rng, c.MODEL_DIM))
+            self.G2.append(_mk_gamma(rng, c.MODEL_DIM))
+            self.W_dq.append(_mk_qw(rng, c.Q_LORA, c.MODEL_DIM))
+            self.W_uq.append(_mk_qw(rng, c.HQK, c.Q_LORA))
+            self.W_uk.append(_mk_qw(rng, c.HNOPE, c.KV_LORA))
+            self.W_uv.append(_mk_qw(rng, c.HV, c.KV_LORA))
+            self.W_o.append(_mk_qw(rng, c.MODEL_DIM, c.HV))
+            self.CKV.append([_mk_bf16(rng, c.KV_LORA) for _ in range(c.S_MAX)])
+            self.KRP.append([_mk_bf16(rng, c.ROPE) for _ in range(c.S_MAX)])
+            self.Wg.append(_mk_qw(rng, c.N_EXPERT, c.MODEL_DIM))
+            self.Dg.append(_mk_qw(rng, c.INTER_DENSE, c.MODEL_DIM))
+            self.Du.append(_mk_qw(rng, c.INTER_DENSE, c.MODEL_DIM))
+            self.Dd.append(_mk_qw(rng, c.MODEL_DIM, c.INTER_DENSE))
+            self.Mg.append([_mk_qw(rng, c.INTER_MOE, c.MODEL_DIM) for _ in range(c.N_EXPERT)])
+            self.Mu.append([_mk_qw(rng, c.INTER_MOE, c.MODEL_DIM) for _ in range(c.N_EXPERT)])
+            self.Md.append([_mk_qw(rng, c.MODEL_DIM, c.INTER_MOE) for _ in range(c.N_EXPERT)])
+            self.SHg.append(_mk_qw(rng, c.INTER_MOE, c.MODEL_DIM))
+            self.SHu.append(_mk_qw(rng, c.INTER_MOE, c.MODEL_DIM))
+            self.SHd.append(_mk_qw(rng, c.MODEL_DIM, c.INTER_MOE))
+        self.GF = _mk_gamma(rng, c.MODEL_DIM)
+        self.Wlm = [_mk_bf16(rng, c.MODEL_DIM) for _ in range(c.VOCAB)]
