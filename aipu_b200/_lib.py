@@ -52,6 +52,8 @@ SIGNATURES = {
     "aipu_ctx_destroy": (c_int, [c_void_p]),
     "aipu_ctx_status": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
     "aipu_ctx_set_flags": (c_int, [c_void_p, c_int]),
+    "aipu_ctx_set_wait_limit": (c_int, [c_void_p, c_int64]),
+    "aipu_selftest_wait": (c_int, [c_void_p, c_void_p]),
     "aipu_q4k_dequant": (c_int, [c_int, c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p]),
     "aipu_act_eval": (c_int, [c_int, c_void_p, c_int64, c_void_p, c_void_p]),
     "aipu_q4k_gemm": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p,

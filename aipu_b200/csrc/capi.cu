@@ -178,7 +178,8 @@ int aipu_ctx_create(aipu_ctx** out, int device) {
     aipu_ctx_destroy(c);
     return rc;
   }
-  if (cudaMalloc(&c->status, sizeof(int)) != cudaSuccess || cudaMemset(c->status, 0, sizeof(int)) != cudaSuccess ||
+  // status word + 64-bit bounded-wait limit (0 = default), see wait_limit() in common.cuh
+  if (cudaMalloc(&c->status, 16) != cudaSuccess || cudaMemset(c->status, 0, 16) != cudaSuccess ||
       cudaMalloc(&c->router_counters, sizeof(int) * 1040) != cudaSuccess ||
       cudaMemset(c->router_counters, 0, sizeof(int) * 1040) != cudaSuccess) {
     aipu_ctx_destroy(c);
@@ -230,6 +231,20 @@ int aipu_ctx_status(aipu_ctx* c, int* status) {
   cudaMemset(c->status, 0, sizeof(int));
   *status = v;
   return OK;
+}
+
+int aipu_ctx_set_wait_limit(aipu_ctx* c, int64_t cycles) {
+  if (!c) return set_error(EINVAL_, "ctx_set_wait_limit: null context");
+  DeviceGuard dg(c->device);
+  const long long v = cycles > 0 ? static_cast<long long>(cycles) : 0;
+  return set_cuda_error(cudaMemcpy(reinterpret_cast<char*>(c->status) + 8, &v, sizeof(v), cudaMemcpyHostToDevice),
+                        "ctx_set_wait_limit");
+}
+
+int aipu_selftest_wait(aipu_ctx* c, void* stream) {
+  if (!c) return set_error(EINVAL_, "selftest_wait: null context");
+  DeviceGuard dg(c->device);
+  return wait_selftest_launch(c->status, static_cast<cudaStream_t>(stream));
 }
 
 int aipu_q4k_dequant(int wtype, const void* w, int64_t nrows, int64_t K, void* out, int out_dtype, void* stream) {

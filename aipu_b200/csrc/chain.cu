@@ -570,7 +570,9 @@ template <int WT, int EPI, int MT, int NT>
 static int chain_launch_t(ChainParams& p, int grid, int smem, cudaStream_t s) {
   auto kern = aipu_chain_kernel<WT, EPI, MT, NT>;
   static bool attr[64] = {false};
-  const int rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, attr, "cudaFuncSetAttribute(chain)");
+  // the attribute is the largest dynamic shared memory any launch of this kernel uses (launches size it
+  // differently: one or several CTAs per SM)
+  const int rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), 232448 - 1024, attr, "cudaFuncSetAttribute(chain)");
   if (rc) return rc;
   return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NT + 32), smem, s, false, &p);
 }

@@ -56,14 +56,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: gives up after `limit_cycles` SM clock cycles (~2 s by default), sets the status
-// bit and returns false. No wait in this library can spin forever.
+// Every bounded wait's limit in SM clock cycles. The device status word passed to the kernels is the
+// first int of a 16-byte block whose 64-bit word at byte 8 holds the wait limit set for the context
+// (aipu_ctx_set_wait_limit; 0 = the default of 4e9 cycles, about 2 s). Read only after a first
+// try failed, so the common path costs nothing.
+constexpr long long kDefaultWaitCycles = 4000000000LL;
+__device__ __forceinline__ long long wait_limit(const int* status) {
+  if (!status) return kDefaultWaitCycles;
+  const long long v = *reinterpret_cast<const volatile long long*>(status + 2);
+  return v > 0 ? v : kDefaultWaitCycles;
+}
+
+// Bounded wait: gives up after the context's wait limit (or `limit_cycles` when positive), sets the
+// status bit and returns false. No wait in this library can spin forever.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int bit,
-                                                  long long limit_cycles = 4000000000LL) {
+                                                  long long limit_cycles = 0) {
   if (mbar_try_wait(bar, parity)) return true;
+  const long long limit = limit_cycles > 0 ? limit_cycles : wait_limit(status);
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > limit_cycles) {
+    if (clock64() - t0 > limit) {
       if (status) atomicOr(status, bit);
       return false;
     }
@@ -85,15 +97,16 @@ __device__ __forceinline__ void st_release_cta_shared(uint32_t* f, uint32_t v) {
 // Warp-uniform bounded wait until *f >= target (wrapping compare). Returns the value seen (>= target),
 // or target - 1 after `limit_cycles` (status bit set).
 __device__ __forceinline__ uint32_t warp_wait_counter(const uint32_t* f, uint32_t target, int* status, int bit,
-                                                      long long limit_cycles = 4000000000LL) {
+                                                      long long limit_cycles = 0) {
   // every lane acquires; the value returned is the warp minimum (each lane saw at least that much)
   uint32_t v = ld_acquire_cta_shared(f) - target;
   if (__all_sync(0xffffffffu, static_cast<int32_t>(v) >= 0)) return __reduce_min_sync(0xffffffffu, v) + target;
+  const long long limit = limit_cycles > 0 ? limit_cycles : wait_limit(status);
   const long long t0 = clock64();
   while (true) {
     v = ld_acquire_cta_shared(f) - target;
     if (__all_sync(0xffffffffu, static_cast<int32_t>(v) >= 0)) return __reduce_min_sync(0xffffffffu, v) + target;
-    if (__any_sync(0xffffffffu, clock64() - t0 > limit_cycles)) {
+    if (__any_sync(0xffffffffu, clock64() - t0 > limit)) {
       if (status && (threadIdx.x & 31) == 0) atomicOr(status, bit);
       return target - 1u;
     }

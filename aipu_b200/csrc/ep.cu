@@ -54,9 +54,10 @@ __global__ void ep_wait_kernel(const EpParams p, int which) {
   if (q >= p.G) return;
   const uint32_t seq = *p.seq;
   const uint32_t* f = reinterpret_cast<const uint32_t*>(p.peers[p.rank] + p.off_flags) + which * p.G + q;
+  const long long limit = wait_limit(p.status);
   const long long t0 = clock64();
   while (static_cast<int32_t>(ld_acquire_sys(f) - seq) < 0) {
-    if (clock64() - t0 > 4000000000LL) {
+    if (clock64() - t0 > limit) {
       atomicOr(p.status, ST_TIMEOUT_FULL);
       return;
     }

@@ -37,6 +37,24 @@ int dequant_launch(int wt, const void* w, int64_t nrows, int64_t K, void* out, i
   return set_cuda_error(cudaGetLastError(), "dequant_kernel");
 }
 
+// ------------------------------------------------------------------ failure-detection self-test
+// One bounded wait on an mbarrier that nothing arrives at: it gives up at the context's wait limit,
+// sets ST_TIMEOUT_FULL in the status word and the kernel returns (the context stays usable).
+__global__ void wait_selftest_kernel(int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  mbar_wait_bounded(&bar, 0, status, ST_TIMEOUT_FULL);
+}
+
+int wait_selftest_launch(int* status, cudaStream_t s) {
+  wait_selftest_kernel<<<1, 32, 0, s>>>(status);
+  return set_cuda_error(cudaGetLastError(), "wait_selftest_kernel");
+}
+
 // ------------------------------------------------------------------ strict GEMM
 // y[m, n] = bf16( sequential fp32 sum_k fmul(x[m,k], w[n,k]) ), the reference's exact contract
 // (tools/q4k_ref.py:86-92). 32 rows per block, one thread per (row, token); weights of a 256-wide

@@ -151,6 +151,7 @@ int combine_launch(const CombineParams& p, cudaStream_t s, bool pdl);
 int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl, int min_smem = 0);
 int gemv_partials_floats(int num_sms);
 int act_launch(int kind, const void* x, int64_t n, void* out, cudaStream_t s);
+int wait_selftest_launch(int* status, cudaStream_t s);
 
 // Bit-exact sequential-chain GEMV (chain.cu): every output is the reference's sequential fp32 chain
 // over k (tools/q4k_ref.py:86-92), computed for many rows at once. Groups (experts) g use weights

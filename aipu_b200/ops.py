@@ -74,6 +74,15 @@ class Context:
         check(lib().aipu_ctx_set_flags(self.handle, flags))
         return self
 
+    def set_wait_limit(self, cycles: int) -> "Context":
+        """Limit of every bounded device wait of this context's kernels in SM cycles (<= 0: default)."""
+        check(lib().aipu_ctx_set_wait_limit(self.handle, int(cycles)))
+        return self
+
+    def selftest_wait(self) -> None:
+        """Run one bounded wait that nothing releases (the failure-detection path); read status()."""
+        check(lib().aipu_selftest_wait(self.handle, _stream(self.device)))
+
     def status(self) -> int:
         v = ctypes.c_int()
         check(lib().aipu_ctx_status(self.handle, ctypes.byref(v)))

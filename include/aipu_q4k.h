@@ -76,8 +76,20 @@ int aipu_ctx_destroy(aipu_ctx* ctx);
  * 1 bf16 ulp, the layer not bit-exact) instead of the default bit-exact chain kernel. */
 #define AIPU_FLAG_TC_DECODE 4
 int aipu_ctx_set_flags(aipu_ctx* ctx, int flags);
-/* device status word of the context (0 = no bounded wait ever gave up); resets it to 0 */
+/* device status word of the context (0 = no bounded wait ever gave up); resets it to 0. Bit 1: a
+ * wait for data gave up, bit 2: a wait for a free buffer gave up, bit 4: bad arguments seen on the
+ * device. */
 int aipu_ctx_status(aipu_ctx* ctx, int* status);
+/* Limit of every bounded device-side wait of kernels launched with this context, in SM clock cycles
+ * (<= 0 restores the default of 4e9 cycles, about 2 s). When a wait reaches it, the kernel sets the
+ * status word, drains its copies in flight and returns; the context stays usable. No counterpart in
+ * the reference (its RTL waits are cycle-exact by construction). */
+int aipu_ctx_set_wait_limit(aipu_ctx* ctx, int64_t cycles);
+/* Failure-detection self-test: launches one bounded wait on a barrier that nothing releases, so it
+ * runs out at the context's wait limit and sets the status word (read it with aipu_ctx_status). It
+ * exercises the same give-up path as a lost peer or a stalled copy, without faulting the GPU. No
+ * counterpart in the reference. */
+int aipu_selftest_wait(aipu_ctx* ctx, void* stream);
 
 /* Exact dequantisation of `nrows` rows of K weights to fp32 (out_dtype AIPU_DT_F32) or bf16
  * (AIPU_DT_BF16, RNE of the exact fp32). Bit-identical to the reference.
