@@ -84,23 +84,40 @@ class _RouterView:
 
 
 class ExpertParallelMoE:
-    """The MoE branch of a decoder block with experts sharded over ``group`` (default: WORLD)."""
+    """The MoE branch of a decoder block with experts sharded over ``group`` (default: WORLD).
 
-    def __init__(self, weights: ShardedMoeWeights, group=None, backend=None):
+    dispatch: "allgather" -- every rank receives every token and its selections (fixed sizes, so a
+    CUDA graph can capture the layer; the decode path); "alltoall" -- each token goes only to the
+    ranks that own one of its experts, and only the per-slot outputs of those experts come back
+    (variable sizes: the per-peer counts are exchanged first; the prefill path); "auto" -- all-to-all
+    from ``a2a_min_tokens`` tokens per rank."""
+
+    def __init__(self, weights: ShardedMoeWeights, group=None, backend=None, dispatch: str = "auto",
+                 a2a_min_tokens: int = 64):
         self.W = weights
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if weights.n_experts_total != weights.local.n_experts * self.world:
             raise ValueError("every rank must hold n_experts_total / world experts")
+        if dispatch not in ("auto", "allgather", "alltoall"):
+            raise ValueError("dispatch must be 'auto', 'allgather' or 'alltoall'")
         self.backend = backend or CudaBackend()
         self.router = _RouterView(weights)
+        self.dispatch = dispatch
+        self.a2a_min_tokens = a2a_min_tokens
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        M = x.shape[0]
+        use_a2a = self.world > 1 and (self.dispatch == "alltoall" or
+                                      (self.dispatch == "auto" and M >= self.a2a_min_tokens))
+        sel, sw = self.backend.route(self.router, x)
+        return self._alltoall(x, sel, sw) if use_a2a else self._allgather(x, sel, sw)
+
+    def _allgather(self, x, sel, sw):
         W, G, r = self.W, self.world, self.rank
         M, H = x.shape
         T = W.topk
-        sel, sw = self.backend.route(self.router, x)
         # dispatch: every rank sees every token and its selection
         x_all = torch.empty((G * M, H), dtype=x.dtype, device=x.device)
         sel_all = torch.empty((G * M, T), dtype=sel.dtype, device=sel.device)
@@ -112,6 +129,55 @@ class ExpertParallelMoE:
         pieces = torch.empty((G, M, T, H), dtype=y_slots.dtype, device=y_slots.device)
         dist.all_to_all_single(pieces.view(G * M, T, H), y_slots.contiguous(), group=self.group)
         return self.backend.combine(sel, sw, W.local.n_experts, pieces, y_sh)
+
+    def _alltoall(self, x, sel, sw):
+        W, G, r = self.W, self.world, self.rank
+        M, H = x.shape
+        T = W.topk
+        n = W.local.n_experts
+        dev = x.device
+        owner = (sel.long() // n).clamp_(0, G - 1)                        # [M, T]
+        # tokens for each destination rank, ascending token order within a destination
+        need = torch.zeros((G, M), dtype=torch.bool, device=dev)
+        need[owner.reshape(-1), torch.arange(M, device=dev).repeat_interleave(T)] = True
+        send_tok = [torch.nonzero(need[q]).reshape(-1) for q in range(G)]
+        send_counts = torch.tensor([int(t.numel()) for t in send_tok], dtype=torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        c_dev = send_counts.to(dev)
+        rc_dev = torch.empty_like(c_dev)
+        dist.all_to_all_single(rc_dev, c_dev, group=self.group)
+        recv_counts = rc_dev.cpu()
+        idx = torch.cat(send_tok)
+        sc, rcv = send_counts.tolist(), recv_counts.tolist()
+        Mr = sum(rcv)
+        x_recv = torch.empty((Mr, H), dtype=x.dtype, device=dev)
+        sel_recv = torch.empty((Mr, T), dtype=sel.dtype, device=dev)
+        dist.all_to_all_single(x_recv, x.index_select(0, idx).contiguous(), rcv, sc, group=self.group)
+        dist.all_to_all_single(sel_recv, sel.index_select(0, idx).contiguous(), rcv, sc, group=self.group)
+        # local experts on the received tokens; this rank's own tokens ride along only for the shared
+        # expert (their selections pointed at another rank's experts, so no routed work is done)
+        other = (W.expert_lo + n) % W.n_experts_total
+        x_cat = torch.cat([x_recv, x])
+        sel_cat = torch.cat([sel_recv, torch.full_like(sel, other)])
+        y_slots, y_sh = self.backend.experts(W.local, W.expert_lo, x_cat, sel_cat, (Mr, M))
+        # return the outputs of the local slots only, (token, slot) order per source rank
+        local = (sel_recv.long() // n) == r                               # [Mr, T]
+        rows = y_slots[:Mr][local]                                        # [P_r, H]
+        per_src = local.sum(dim=1)
+        ret_send = [int(c.sum()) for c in torch.split(per_src, rcv)]
+        ret_recv = [int(v) for v in (owner == torch.arange(G, device=dev).view(G, 1, 1)).reshape(G, -1).sum(1).tolist()]
+        back = torch.empty((sum(ret_recv), H), dtype=y_slots.dtype, device=dev)
+        dist.all_to_all_single(back, rows.contiguous(), ret_recv, ret_send, group=self.group)
+        # pieces[q][m, s] = the output of expert sel[m, s] when its owner is q
+        pieces = torch.zeros((G, M, T, H), dtype=y_slots.dtype, device=dev)
+        off = 0
+        for q in range(G):
+            mask = owner == q
+            cnt = ret_recv[q]
+            if cnt:
+                pieces[q][mask] = back[off:off + cnt]
+            off += cnt
+        return self.backend.combine(sel, sw, n, pieces, y_sh)
 
 
 class PeerExpertParallelMoE:

@@ -454,22 +454,18 @@ def _time_ep_layer(layer, x, reps):
     return {"t": float(t.item()), "graphed": graphed}
 
 
-def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
-    """BASELINE config 3/5 decode layer with the 256 routed experts sharded over the N ranks
-    (256/N per GPU, NCCL all-gather dispatch and all-to-all return); every rank decodes M tokens.
-    tokens/s = N * M / (max-over-ranks device time per layer)."""
+def _ep_local_weights(d, world, rank):
+    """Rank `rank`'s share of the BASELINE config 3/4 layer: experts [r*E/N, (r+1)*E/N), the router and
+    the shared expert replicated."""
     import torch
-    import torch.distributed as dist
 
-    from aipu_b200 import ep
     from aipu_b200 import formats as F
     from aipu_b200 import ops
 
-    d = torch.device("cuda", torch.cuda.current_device())
-    H, Fd, E, T = 6144, 2048, 256, 8
+    H, Fd, E, T = MOE_H, MOE_F, MOE_E, MOE_T
     n = E // world
     g = torch.Generator(device=d)
-    local = ops.MoeLayerWeights(
+    return ops.MoeLayerWeights(
         hidden=H, ffn=Fd, n_experts=n, topk=T, router_wtype=F.F32,
         router_w=torch.randn((H, E), device=d, generator=g.manual_seed(1)) * 0.02,
         router_bias=torch.randn((E,), device=d, generator=g.manual_seed(2)) * 0.01,
@@ -479,26 +475,127 @@ def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
         shared_gate_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=14, device=d),
         shared_up_w=F.random_rows_dev(F.Q4_K, Fd, H, seed=15, device=d),
         shared_down_w=F.random_rows_dev(F.Q6_K, H, Fd, seed=16, device=d))
+
+
+def _one_gpu_layer_us(d, M, reps=50, **flags):
+    """Device time of the whole BASELINE config 3/4 layer (all 256 experts) on this GPU for M tokens."""
+    import torch
+
+    from aipu_b200 import ops
+
+    W = moe_layer_weights(d)
+    x = torch.randn((M, MOE_H), device=d, generator=torch.Generator(device=d).manual_seed(55)).to(torch.bfloat16)
+    y = torch.empty((M, MOE_H), dtype=torch.bfloat16, device=d)
+    ctx = ops.Context(d).set_flags(**flags)
+    s = torch.cuda.Stream()
+    ops.moe_layer(W, x, ctx=ctx, out=y)
+    torch.cuda.synchronize()
+    g = _graph(lambda: ops.moe_layer(W, x, ctx=ctx, out=y), s)
+    t = _time_graph(g, reps, s)
+    del g, W
+    ctx.close()
+    torch.cuda.empty_cache()
+    return t
+
+
+def moe_decode_ep(world, rank, M_list=(1, 4), reps=100):
+    """BASELINE config 3 decode layer with the 256 routed experts sharded over the N ranks (256/N per
+    GPU); every rank decodes M tokens. Exchanges: NCCL (all-gather dispatch, all-to-all return) and
+    the NVLink peer-memory exchange inside the library. tokens/s = N * M / (max-over-ranks device time
+    per layer). Per rank: the HBM bytes it streams (router, the local experts its ranks' tokens
+    touched, the shared expert) and their fraction of the measured HBM peak; efficiency_vs_n1 = the
+    one-GPU layer's time for all N * M tokens / (N * the expert-parallel time)."""
+    import torch
+    import torch.distributed as dist
+
+    from aipu_b200 import ep
+    from aipu_b200 import formats as F
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    H, Fd, E, T = MOE_H, MOE_F, MOE_E, MOE_T
+    n = E // world
+    hbm, _, _ = peaks()
+    local = _ep_local_weights(d, world, rank)
     sharded = ep.ShardedMoeWeights(local, rank * n, E)
     layers = {"nccl": ep.ExpertParallelMoE(sharded, backend=ep.CudaBackend(ops.Context(d))),
               "peer": ep.PeerExpertParallelMoE(sharded, max_tokens=max(M_list))}
     expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
+    g = torch.Generator(device=d)
     out = {}
-    for kind, layer in layers.items():
-        for M in M_list:
-            x = torch.randn((M, H), device=d, generator=g.manual_seed(100 + M + 7 * rank)).to(torch.bfloat16)
+    t1 = {}
+    for M in M_list:
+        x = torch.randn((M, H), device=d, generator=g.manual_seed(100 + M + 7 * rank)).to(torch.bfloat16)
+        sel_all = torch.empty((world * M, T), dtype=torch.int32, device=d)
+        sel, _, _ = ops.moe_router(F.F32, local.router_w, x, E, T, bias=local.router_bias)
+        dist.all_gather_into_tensor(sel_all, sel)
+        touched = len(set(v for v in sel_all.cpu().numpy().reshape(-1).tolist() if rank * n <= v < (rank + 1) * n))
+        byts = H * E * 4 + (touched + 1) * expert_bytes
+        for kind, layer in layers.items():
             r = _time_ep_layer(layer, x, reps)
             t = r["t"]
-            # experts this rank touched in one layer (union of its local experts over all N*M tokens)
-            sel_all = torch.empty((world * M, T), dtype=torch.int32, device=d)
-            sel, _, _ = ops.moe_router(F.F32, local.router_w, x, E, T, bias=local.router_bias)
-            dist.all_gather_into_tensor(sel_all, sel)
-            touched = len(set(v for v in sel_all.cpu().numpy().reshape(-1).tolist() if rank * n <= v < (rank + 1) * n))
-            byts = H * E * 4 + (touched + 1) * expert_bytes
             out[f"{kind}_M{M}"] = {"us_per_layer": round(t * 1e6, 2), "tokens_per_s": round(world * M / t, 1),
                                    "tokens_per_rank": M, "experts_per_gpu": n, "rank0_touched_experts": touched,
-                                   "cuda_graph": r["graphed"], "rank0_hbm_gbs": round(byts / t / 1e9, 1)}
+                                   "cuda_graph": r["graphed"], "rank0_hbm_gbs": round(byts / t / 1e9, 1),
+                                   "rank0_hbm_frac": round(byts / t / 1e9 / hbm, 4)}
     layers["peer"].close()
+    del layers, local, sharded
+    torch.cuda.empty_cache()
+    if rank == 0:
+        for M in M_list:
+            t1[M] = _one_gpu_layer_us(d, world * M)
+            for kind in ("nccl", "peer"):
+                ent = out[f"{kind}_M{M}"]
+                ent["one_gpu_us_for_all_tokens"] = round(t1[M] * 1e6, 2)
+                ent["efficiency_vs_n1"] = round(t1[M] / (world * ent["us_per_layer"] * 1e-6), 4)
+    dist.barrier()
+    return out
+
+
+def moe_prefill_ep(world, rank, M=2048, reps=3):
+    """BASELINE config 4 expert-parallel: 2048 tokens per rank, all-to-all dispatch of each token to the
+    ranks owning its experts (NCCL), the tensor-core expert GEMMs on every rank's received tokens,
+    all-to-all return of the per-slot outputs, slot-order combine. tokens/s = N * 2048 / (max-over-
+    ranks time); efficiency_vs_n1 = the one-GPU layer's time for 2048 tokens / the expert-parallel
+    time (the same tokens per GPU)."""
+    import torch
+    import torch.distributed as dist
+
+    from aipu_b200 import ep
+    from aipu_b200 import ops
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    n = MOE_E // world
+    local = _ep_local_weights(d, world, rank)
+    layer = ep.ExpertParallelMoE(ep.ShardedMoeWeights(local, rank * n, MOE_E), backend=ep.CudaBackend(ops.Context(d)),
+                                 dispatch="alltoall")
+    x = torch.randn((M, MOE_H), device=d, generator=torch.Generator(device=d).manual_seed(9 + rank)).to(torch.bfloat16)
+    for _ in range(2):
+        layer(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        layer(x)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps / 1e3], device=d, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = float(t.item())
+    flops = 2.0 * (M * MOE_T + M) * 3 * MOE_H * MOE_F * world
+    _, tf_peak, _ = peaks()
+    out = {"tokens_per_rank": M, "ms_per_layer": round(t * 1e3, 3), "tokens_per_s": round(world * M / t, 1),
+           "dispatch": "all-to-all (NCCL), tokens only to the ranks owning their experts",
+           "tensor_tflops_total": round(flops / t / 1e12, 1),
+           "per_gpu_frac_of_bf16_peak": round(flops / world / t / 1e12 / tf_peak, 4)}
+    del layer, local
+    torch.cuda.empty_cache()
+    if rank == 0:
+        t1 = _one_gpu_layer_us(d, M, reps=3)
+        out["one_gpu_ms_same_tokens_per_gpu"] = round(t1 * 1e3, 3)
+        out["efficiency_vs_n1"] = round(t1 / t, 4)
+    dist.barrier()
     return out
 
 
@@ -731,8 +828,13 @@ def main():
         moe = moe_bench(check=not args.no_cpu)
     moe_ep = None
     moe_stream = None
+    moe_pre_ep = None
     if world > 1 and not args.no_moe:
         moe_ep = moe_decode_ep(world, rank)
+        try:
+            moe_pre_ep = moe_prefill_ep(world, rank)
+        except Exception as e:  # reported in the line; the GEMV metric above stands
+            moe_pre_ep = {"error": f"{type(e).__name__}: {e}"[:300]}
         if args.stream_layers > 0:
             try:
                 moe_stream = moe_decode_stream(world, rank, args.stream_layers)
@@ -752,7 +854,8 @@ def main():
                          "algorithmic_bytes_per_launch": L * C1_BYTES},
             "single_launch": single,
             "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,
-            "clocks": clk.summary(), "moe": moe, "moe_decode_ep": moe_ep, "moe_decode_stream": moe_stream,
+            "clocks": clk.summary(), "moe": moe, "moe_decode_ep": moe_ep, "moe_prefill_ep": moe_pre_ep,
+            "moe_decode_stream": moe_stream,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -80,13 +80,13 @@ def _weights(seed):
     return W, xs
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, dispatch="allgather"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         W, xs = _weights(7)
-        layer = ep.ExpertParallelMoE(ep.shard(W, rank, world), backend=OracleBackend())
+        layer = ep.ExpertParallelMoE(ep.shard(W, rank, world), backend=OracleBackend(), dispatch=dispatch)
         out = layer(_bf16_t(xs[rank]))
         q.put((rank, _np(out)))
     finally:
@@ -99,11 +99,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_expert_parallel_two_gloo_ranks_match_one_process_layer():
+@pytest.mark.parametrize("dispatch", ["allgather", "alltoall"])
+def test_expert_parallel_two_gloo_ranks_match_one_process_layer(dispatch):
+    """Both dispatches: all-gather of every token, and all-to-all of each token to the ranks owning its
+    experts with only the local slots' outputs returned."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, dispatch)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=240) for _ in procs)

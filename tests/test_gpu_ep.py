@@ -107,7 +107,7 @@ def test_expert_parallel_emulated_fast_within_reference_tolerance(M):
         assert not (np.abs(got - ref) > tol).any()
 
 
-def _nccl_worker(rank, world, port, q):
+def _nccl_worker(rank, world, port, q, dispatch="allgather"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
 
@@ -120,7 +120,7 @@ def _nccl_worker(rank, world, port, q):
         ctx = ops.Context(d).set_flags(strict=True)
         rng = np.random.default_rng(1000 + rank)
         x = torch.from_numpy(qo.bf16_round(rng.standard_normal((3, 6144)).astype(F32))).to(d).to(torch.bfloat16)
-        layer = ep.ExpertParallelMoE(ep.shard(W, rank, world), backend=ep.CudaBackend(ctx))
+        layer = ep.ExpertParallelMoE(ep.shard(W, rank, world), backend=ep.CudaBackend(ctx), dispatch=dispatch)
         out = layer(x)
         ref = ops.moe_layer(W, x, ctx=ctx)
         torch.cuda.synchronize()
@@ -129,7 +129,10 @@ def _nccl_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_two_gpus_nccl_strict():
+@pytest.mark.parametrize("dispatch", ["allgather", "alltoall"])
+def test_expert_parallel_two_gpus_nccl_strict(dispatch):
+    """NCCL expert parallelism on 2 GPUs equals the one-GPU layer bit for bit, with the all-gather
+    dispatch and with the all-to-all dispatch (tokens only to the ranks that own their experts)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -138,7 +141,7 @@ def test_expert_parallel_two_gpus_nccl_strict():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, dispatch)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)
