@@ -373,6 +373,187 @@ __device__ __forceinline__ void unit_f16(const uint8_t* rg, const uint8_t* rg8, 
     acc[j] = __fadd_rn(acc[j], __fadd_rn(__fadd_rn(P4[0][j], P4[1][j]), __fadd_rn(P4[2][j], P4[3][j])));
 }
 
+// ------------------------------------------------------------------ integer dot engine (Q4_K, one token)
+// The activation row is rounded once to integers X = rn(x * 2^-s) with max |X| in [2^21, 2^22] (a
+// power-of-two prescale s per row), and X is written as three balanced base-256 digits (int8,
+// X = d0 + 2^8 d1 + 2^16 d2). Q4_K codes need no conversion: masking the packed bytes gives u8
+// operands q (low nibbles) and 16 q (high nibbles), and one m16n8k32 u8 x s8 MMA covers 16 rows x one
+// 32-weight sub-block with exact int32 sums (the integer MMA runs natively; an fp8 MMA issued through
+// mma.sync costs a dozen operand conversions on this GPU). The MMA's 8 columns are (sub-block parity,
+// digit): the activation columns hold the digits only at the k of their parity, so the low-nibble
+// sub-block 2g and the high-nibble sub-block 2g + 1 of a 64-weight group share one accumulator set.
+// Each lane scales its sets by the 6-bit integer sub-block scales with integer multiply-adds (|sum| <
+// 2^28: exact), converts once per row and super-block and applies d; the min term dmin * sum_j m_j S_j
+// uses the sub-block sums S_j of X. The only roundings are X itself (2^-22 of the row's largest
+// value) and the fp32 steps per super-block.
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Stage one token row (group grp) as 8 masked int8 digit columns + fp32 sub-block sums of X (all
+// threads). Column c = 4 * parity + digit (digit < 3; columns 3 and 7 stay zero) holds, at every k
+// whose sub-block j has j % 2 == parity, digit `digit` of X; zero elsewhere. misc[0..1] = prescale
+// shift s (value = sum * 2^s). Leaves with a __syncthreads.
+template <int XT>
+__device__ void gemv_stage_x_i8(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int xs_slot,
+                                float* red) {
+  const int tid = threadIdx.x, NT = blockDim.x, NW = NT >> 5;
+  const int K = p.K;
+  int* misc = reinterpret_cast<int*>(smem + L.off_misc) + xs_slot * 8;
+  uint8_t* xs = smem + L.off_xs + xs_slot * 8 * p.xpitch;
+  float* sxs = reinterpret_cast<float*>(smem + L.off_sxs) + xs_slot * (K / 32);
+  const uint8_t* xr = static_cast<const uint8_t*>(p.x) +
+                      static_cast<int64_t>(grp) * p.x_group_stride * (XT == XT_F32 ? 4 : 2);
+  const int nvec = K / 8;  // 8 activations per vector
+  auto load8 = [&](int v, float (&f)[8]) {
+    if (XT == XT_F32) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(xr) + 2 * v);
+      const float4 b = __ldg(reinterpret_cast<const float4*>(xr) + 2 * v + 1);
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr) + v);
+      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w4[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+      }
+    }
+  };
+  float mx = 0.f;
+  for (int v = tid; v < nvec; v += NT) {
+    float f[8];
+    load8(v, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(f[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  float m = 0.f;
+  for (int w = 0; w < NW; ++w) m = fmaxf(m, red[w]);
+  // max * 2^-s in [2^21, 2^22): |X| <= 2^22 after rounding, so d2 stays within [-65, 65] and every
+  // integer sum below stays exact
+  const int e = static_cast<int>((__float_as_uint(m) >> 23) & 0xFFu);
+  int sh = (m == 0.f) ? 0 : (e - 127 - 21);
+  sh = sh < -100 ? -100 : (sh > 100 ? 100 : sh);
+  if (tid == 0) {
+    misc[0] = sh;
+    misc[1] = sh;
+  }
+  const float sc = exp2i(-sh);
+  for (int v = tid; v < nvec; v += NT) {
+    float f[8];
+    load8(v, f);
+    int sum = 0;
+    uint32_t dig[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // round to the nearest integer (ties to even): |x * 2^-s| < 2^22, so adding 1.5 * 2^23 leaves
+      // the integer in the low mantissa bits
+      const int X = static_cast<int>(__float_as_uint(__fadd_rn(__fmul_rn(f[i], sc), 12582912.f)) - 0x4B400000u);
+      sum += X;
+      const int d0 = static_cast<int8_t>(X & 0xFF);
+      const int x1 = (X - d0) >> 8;
+      const int d1 = static_cast<int8_t>(x1 & 0xFF);
+      const int d2 = (x1 - d1) >> 8;
+      const int word = i >> 2, sh8 = 8 * (i & 3);
+      dig[0][word] |= (static_cast<uint32_t>(d0) & 0xFFu) << sh8;
+      dig[1][word] |= (static_cast<uint32_t>(d1) & 0xFFu) << sh8;
+      dig[2][word] |= (static_cast<uint32_t>(d2) & 0xFFu) << sh8;
+    }
+    // the 4 threads of a 32-wide sub-block add their integer sums (exact)
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const int k0 = 8 * v, j = k0 >> 5;
+    if ((v & 3) == 0) sxs[j] = static_cast<float>(sum);
+    const int par = j & 1;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int cs = c >> 2, cd = c & 3;
+      const uint2 val = (cs == par && cd < 3) ? make_uint2(dig[cd < 3 ? cd : 0][0], dig[cd < 3 ? cd : 0][1])
+                                              : make_uint2(0u, 0u);
+      *reinterpret_cast<uint2*>(xs + c * p.xpitch + k0) = val;
+    }
+  }
+  __syncthreads();
+}
+
+// Q4_K unit (16 rows g, g + 8 x one super-block) on the integer engine, one token. acc[0] / acc[2]:
+// this lane's partial sums of rows g / g + 8 (its digit columns, and the min terms of sub-blocks 2t,
+// 2t + 1); q4k_i8_fold sums the 4 lanes. xb: the lane's activation column at this super-block (+ 8t);
+// sxb: the super-block's sub-block sums; w0 / w1: the digit weights of the lane's two columns (1/16
+// folded in for the high-nibble columns); ssel0/1: PRMT selectors of the lane's scale bytes, msel0/1:
+// of its min bytes.
+__device__ __forceinline__ void unit_q4k_i8(uint32_t rg, uint32_t rg8, uint32_t xb, uint32_t sxb, int t, float w0,
+                                            float w1, uint32_t ssel0, uint32_t ssel1, uint32_t msel0, uint32_t msel1,
+                                            float (&acc)[4]) {
+  const uint4 hg = lds_v4(rg), h8 = lds_v4(rg8);
+  int D[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint2 wg = lds_v2(rg + 16 + 32 * g + 8 * t), w8 = lds_v2(rg8 + 16 + 32 * g + 8 * t);
+    const uint2 xl = lds_v2(xb + 64 * g), xh = lds_v2(xb + 64 * g + 32);
+    const uint32_t alo[4] = {wg.x & 0x0F0F0F0Fu, w8.x & 0x0F0F0F0Fu, wg.y & 0x0F0F0F0Fu, w8.y & 0x0F0F0F0Fu};
+    mma_u8s8_16832(D[g], alo, xl.x, xl.y);
+    const uint32_t ahi[4] = {wg.x & 0xF0F0F0F0u, w8.x & 0xF0F0F0F0u, wg.y & 0xF0F0F0F0u, w8.y & 0xF0F0F0F0u};
+    mma_u8s8_16832(D[g], ahi, xh.x, xh.y);
+  }
+  // 6-bit scale / min tables of both rows (get_scale_min_k4 for j = 0..7 at once)
+  const uint32_t sc03g = hg.y & 0x3F3F3F3Fu, m03g = hg.z & 0x3F3F3F3Fu;
+  const uint32_t sc47g = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+  const uint32_t m47g = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+  const uint32_t sc038 = h8.y & 0x3F3F3F3Fu, m038 = h8.z & 0x3F3F3F3Fu;
+  const uint32_t sc478 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+  const uint32_t m478 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+  // set g covers sub-block 2g + parity: g = 0, 1 from the 0-3 tables, g = 2, 3 from the 4-7 tables
+  int c0g = 0, c1g = 0, c08 = 0, c18 = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t sl = (g & 1) ? ssel1 : ssel0;
+    const int sg = static_cast<int>(prmt(g < 2 ? sc03g : sc47g, 0u, sl));
+    const int s8 = static_cast<int>(prmt(g < 2 ? sc038 : sc478, 0u, sl));
+    c0g += sg * D[g][0];
+    c1g += sg * D[g][1];
+    c08 += s8 * D[g][2];
+    c18 += s8 * D[g][3];
+  }
+  const float vg = fmaf(__int2float_rn(c1g), w1, __fmul_rn(__int2float_rn(c0g), w0));
+  const float v8 = fmaf(__int2float_rn(c18), w1, __fmul_rn(__int2float_rn(c08), w0));
+  acc[0] = fmaf(f16_bits_to_f32(hg.x & 0xFFFFu), vg, acc[0]);
+  acc[2] = fmaf(f16_bits_to_f32(h8.x & 0xFFFFu), v8, acc[2]);
+  // min term: this lane takes sub-blocks 2t and 2t + 1 (table m03 for t < 2, m47 otherwise)
+  float2 S;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(S.x), "=f"(S.y) : "r"(sxb + 8 * t));
+  constexpr uint32_t MAG = 0x4B000000u;
+  auto ent = [&](uint32_t tab, uint32_t sl) { return __fsub_rn(__uint_as_float(prmt(tab, MAG, sl)), 8388608.f); };
+  const uint32_t tmg = (t < 2) ? m03g : m47g, tm8 = (t < 2) ? m038 : m478;
+  const float cmg = fmaf(ent(tmg, msel0), S.x, __fmul_rn(ent(tmg, msel1), S.y));
+  const float cm8 = fmaf(ent(tm8, msel0), S.x, __fmul_rn(ent(tm8, msel1), S.y));
+  acc[0] = fmaf(-f16_bits_to_f32(hg.x >> 16), cmg, acc[0]);
+  acc[2] = fmaf(-f16_bits_to_f32(h8.x >> 16), cm8, acc[2]);
+}
+
+// End of a tile for unit_q4k_i8: rows g and g + 8 summed over the 4 lanes, left in the standard
+// layout (column 0 of every lane; the other column slots zero).
+__device__ __forceinline__ void q4k_i8_fold(float (&acc)[4]) {
+  float v0 = acc[0], v2 = acc[2];
+  v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, 1));
+  v2 = __fadd_rn(v2, __shfl_xor_sync(0xffffffffu, v2, 1));
+  v0 = __fadd_rn(v0, __shfl_xor_sync(0xffffffffu, v0, 2));
+  v2 = __fadd_rn(v2, __shfl_xor_sync(0xffffffffu, v2, 2));
+  acc[0] = v0;
+  acc[2] = v2;
+  acc[1] = acc[3] = 0.f;
+}
+
 // ------------------------------------------------------------------ kernel
 template <int WT, int XT, int EPI>
 struct GemvGeom {
@@ -693,14 +874,15 @@ __device__ __forceinline__ void issue_chunk(const GemvParams& p, const Chunk& ch
   if (lane < 16) bulk_g2s(slot + lane * p.pitch, lo, bytes, bar);
 }
 
-template <int WT, int XT, int EPI>
+template <int WT, int XT, int EPI, int ENG>
 __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RPT = GemvGeom<WT, XT, EPI>::RPT;
   constexpr int UB = GemvGeom<WT, XT, EPI>::UB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NW = blockDim.x >> 5, S = p.nslots;
-  const int ncols = (XT == XT_F32) ? 2 * p.M : p.M;
+  // ENG = 1: the integer engine (Q4_K, one token) stages 8 masked int8 digit columns
+  const int ncols = ENG ? 8 : ((XT == XT_F32) ? 2 * p.M : p.M);
   const GemvLayout L = gemv_layout(WT, ncols, p.K, p.xg, NW, S, p.pitch, p.xpitch);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * GEMV_MAXS;
   uint8_t* ring = smem + L.off_ring + warp * S * 16 * p.pitch;
@@ -722,7 +904,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   // previous kernel
   int U = 0, a = 0, b = 0;  // unit counts fit in 32 bits (checked on the host)
   Cursor ci;                // issue cursor
-  int issued = 0, consumed = 0;
+  int issued = 0, consumed = 0, islot = 0;  // islot = issued % S, kept without a division
   auto setup_range = [&](int ngroups) {
     U = ngroups * tpg * nsb;
     a = static_cast<int>(static_cast<int64_t>(U) * wid / W);
@@ -732,9 +914,10 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   auto prefetch = [&]() {
     while (ci.u < b && issued - consumed < S) {
       const Chunk ch = chunk_at(ci, b, nsb, p.upc);
-      issue_chunk<WT, XT, EPI>(p, ch, tpg, ring + (issued % S) * stride_slot, &bars[issued % S], lane);
+      issue_chunk<WT, XT, EPI>(p, ch, tpg, ring + islot * stride_slot, &bars[islot], lane);
       advance(ci, ch.n, nsb, tpg);
       ++issued;
+      if (++islot == S) islot = 0;
     }
   };
   // (a dynamic group list is read before the wait only when the host marks it as already complete)
@@ -753,11 +936,29 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   const int64_t c1 = static_cast<int64_t>(U) * (static_cast<int64_t>(blockIdx.x + 1) * NW) / W;
   const int gfirst = (c1 > c0) ? static_cast<int>((c0 / nsb) / tpg) : 0;
   const int glast = (c1 > c0) ? static_cast<int>(((c1 - 1) / nsb) / tpg) : 0;
-  if (p.x_group_stride == 0) {
+  if (ENG) {
+    if (p.x_group_stride == 0) {
+      gemv_stage_x_i8<XT>(p, smem, L, 0, 0, red);
+    } else {
+      for (int g = gfirst; g <= glast && g - gfirst < p.xg; ++g) gemv_stage_x_i8<XT>(p, smem, L, g, g - gfirst, red);
+    }
+  } else if (p.x_group_stride == 0) {
     gemv_stage_x<WT, XT, EPI>(p, smem, L, 0, 0, ncols, red);
   } else {
     for (int g = gfirst; g <= glast && g - gfirst < p.xg; ++g) gemv_stage_x<WT, XT, EPI>(p, smem, L, g, g - gfirst, ncols, red);
   }
+
+  // integer engine: the digit weights of this lane's two MMA columns (t = 0: digits 0, 1; t = 1: digit
+  // 2 and a zero column; t = 2, 3 the same for the high-nibble columns, whose codes carry a factor 16),
+  // and the PRMT selectors of its scale bytes (sub-block 2g + t / 2 of the 0-3 / 4-7 tables: byte
+  // t / 2 for g even, 2 + t / 2 for g odd) and min bytes (sub-blocks 2t, 2t + 1)
+  const int tl = lane & 3;
+  const float w0 = (tl & 1) ? ((tl & 2) ? 4096.f : 65536.f) : ((tl & 2) ? 0.0625f : 1.f);
+  const float w1 = (tl & 1) ? 0.f : ((tl & 2) ? 16.f : 256.f);
+  const uint32_t ssel0 = 0x4440u | static_cast<uint32_t>(tl >> 1);
+  const uint32_t ssel1 = 0x4440u | static_cast<uint32_t>(2 + (tl >> 1));
+  const uint32_t msel0 = 0x7440u | static_cast<uint32_t>((2 * tl) & 3);
+  const uint32_t msel1 = 0x7440u | static_cast<uint32_t>((2 * tl + 1) & 3);
 
   // ------------------------------------------------------------------ per-warp main loop
   const int g = lane >> 2, t = lane & 3;
@@ -797,7 +998,11 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
     // a chunk is one or two units (upc <= 2): straight-line calls, no loop over a runtime count
     auto do_unit = [&](const int i) {
       const int sb = ch.sb + i;
-      if (WT == WT_Q4K) {
+      if (ENG && WT == WT_Q4K) {
+        const uint32_t xc8 = smem_u32(smem + L.off_xs + (xsl * 8 + g) * p.xpitch) + 256 * sb + 8 * t;
+        const uint32_t sxb = smem_u32(smem + L.off_sxs) + 4 * (xsl * (p.K / 32) + 8 * sb);
+        unit_q4k_i8(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, ssel0, ssel1, msel0, msel1, acc);
+      } else if (WT == WT_Q4K) {
         const uint32_t sxcol = smem_u32(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
         unit_q4k(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcol), sxcol, sb, t, acc);
       } else if (WT == WT_Q6K) {
@@ -833,6 +1038,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
     prefetch();  // refill the slot just freed
     if (ch.sb + ch.n == nsb || cc.u == b) {
       // ---------------- this worker's piece of `tile` is done
+      if (ENG) q4k_i8_fold(acc);
       if (WT == WT_Q6K) {
         if (mp == 1) q6k_fold<1>(acc);
         else if (mp == 2) q6k_fold<2>(acc);
@@ -898,9 +1104,9 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
 }
 
 // ------------------------------------------------------------------ host launch
-template <int WT, int XT, int EPI>
+template <int WT, int XT, int EPI, int ENG = 0>
 static int launch_one(GemvParams p, int grid, int nw, int smem, cudaStream_t stream, bool pdl) {
-  auto kern = aipu_kq_gemv_kernel<WT, XT, EPI>;
+  auto kern = aipu_kq_gemv_kernel<WT, XT, EPI, ENG>;
   static bool attr_set[64] = {false};
   const int arc = set_smem_attr_once(reinterpret_cast<const void*>(kern), 232448 - 1024, attr_set, "cudaFuncSetAttribute(gemv)");
   if (arc) return arc;
@@ -912,8 +1118,11 @@ static int launch_one(GemvParams p, int grid, int nw, int smem, cudaStream_t str
 static int gemv_upc(int wt) { return wt == WT_Q4K ? 2 : wt == WT_Q6K ? 2 : wt == WT_Q80 ? 2 : 1; }
 
 int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl, int min_smem) {
-  const int ncols = (xt == XT_F32) ? 2 * p.M : p.M;
-  if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ncols > 8) return set_error(-1, "gemv: bad shape");
+  if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ((xt == XT_F32) ? 2 * p.M : p.M) > 8)
+    return set_error(-1, "gemv: bad shape");
+  // the integer dot engine for Q4_K rows and one token (the decode GEMV); the f16 engine otherwise
+  const bool engi = (wt == WT_Q4K && epi == EPI_STORE && p.M == 1);
+  const int ncols = engi ? 8 : ((xt == XT_F32) ? 2 * p.M : p.M);
   if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
   if ((reinterpret_cast<uintptr_t>(p.x) & 15u) != 0) return set_error(-1, "gemv: activations must be 16-byte aligned");
   const int rpt = (epi == EPI_SWIGLU) ? 8 : 16;
@@ -946,7 +1155,9 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
     if (!rc && epi == EPI_SWIGLU) rc = encode_tiled(&p.tmap1, dt, 3, p.w1, dims, strides, box);
     if (rc) return rc;
   }
-  p.xpitch = ((p.K * 2 + 127) & ~127) + 64;
+  // f16 engine: K fp16 values per column; integer engine: K bytes per column, +32 so that the 8 columns
+  // read by a half-warp start 8 banks apart
+  p.xpitch = engi ? p.K + 32 : ((p.K * 2 + 127) & ~127) + 64;
   if (p.x_group_stride == 0) {
     p.xg = 1;
   } else {
@@ -972,6 +1183,10 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   if (!nw) return set_error(-1, "gemv: activation block too large for shared memory");
   p.nslots = ns;
   const int smem = std::min(limit, std::max(min_smem, gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch).total));
+  if (engi) {
+    if (xt == XT_F32) return launch_one<WT_Q4K, XT_F32, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
+    if (xt == XT_BF16) return launch_one<WT_Q4K, XT_BF16, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
+  }
 #define AIPU_GEMV_CASE(W, X, E)                                              \
   if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, nw, smem, stream, pdl);
   AIPU_GEMV_CASE(WT_Q4K, XT_BF16, EPI_STORE)
