@@ -1,6 +1,7 @@
 // Decode dequant GEMV kernel bodies and host launchers (design notes in gemv.cuh).
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "deq.cuh"
@@ -14,18 +15,20 @@ namespace aipu {
 // columns][Q4_K sub-block sums: per (column, super-block) 64 bytes = fp16 hi[8], lo[8], lo2[8], pad]
 // [per-warp rings: NW x S slots x 16 rows x pitch]
 struct GemvLayout {
-  int off_misc, off_xs, off_sxs, off_ring, total;
+  int off_misc, off_xs, off_sxs, off_ring, off_part, total;
 };
 
+// part_nw: warps whose tile pieces are summed in shared memory (cta mode), 1 KB each
 __host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int xg, int nw, int nslots, int pitch,
-                                                  int xpitch) {
+                                                  int xpitch, int part_nw) {
   GemvLayout L;
   L.off_misc = GEMV_MAXW * GEMV_MAXS * 8;
   L.off_xs = L.off_misc + 256;
   L.off_sxs = L.off_xs + xg * ncols * xpitch;
   const int sx = (wt == WT_Q4K) ? xg * ncols * (K / 256) * 64 : 0;
   L.off_ring = (L.off_sxs + sx + 127) & ~127;
-  L.total = L.off_ring + nw * nslots * 16 * pitch;
+  L.off_part = L.off_ring + nw * nslots * 16 * pitch;
+  L.total = L.off_part + part_nw * 2 * 32 * 16;
   return L;
 }
 
@@ -396,8 +399,8 @@ __device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[
 
 // Stage one token row (group grp) as 8 masked int8 digit columns + fp32 sub-block sums of X (all
 // threads). Column c = 4 * parity + digit (digit < 3; columns 3 and 7 stay zero) holds, at every k
-// whose sub-block j has j % 2 == parity, digit `digit` of X; zero elsewhere. misc[0..1] = prescale
-// shift s (value = sum * 2^s). Leaves with a __syncthreads.
+// whose sub-block j has j % 2 == parity, digit `digit` of X; zero elsewhere (the columns are zero on
+// entry). misc[0..1] = prescale shift s (value = sum * 2^s). Leaves with a __syncthreads.
 template <int XT>
 __device__ void gemv_stage_x_i8(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int xs_slot,
                                 float* red) {
@@ -424,12 +427,34 @@ __device__ void gemv_stage_x_i8(const GemvParams& p, uint8_t* smem, const GemvLa
       }
     }
   };
+  // up to kRegVec vectors per thread are loaded once, all at the same time, and kept in registers for
+  // the second pass (one L2 round trip instead of one per loop iteration and pass)
+  constexpr int kRegVec = 4;
+  const bool in_regs = nvec <= kRegVec * NT;
+  float fr[kRegVec][8];
   float mx = 0.f;
-  for (int v = tid; v < nvec; v += NT) {
-    float f[8];
-    load8(v, f);
+  if (in_regs) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(f[i]));
+    for (int r = 0; r < kRegVec; ++r) {
+      const int v = tid + r * NT;
+      if (v < nvec) {
+        load8(v, fr[r]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) fr[r][i] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRegVec; ++r)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(fr[r][i]));
+  } else {
+    for (int v = tid; v < nvec; v += NT) {
+      float f[8];
+      load8(v, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(f[i]));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -447,38 +472,50 @@ __device__ void gemv_stage_x_i8(const GemvParams& p, uint8_t* smem, const GemvLa
     misc[1] = sh;
   }
   const float sc = exp2i(-sh);
-  for (int v = tid; v < nvec; v += NT) {
-    float f[8];
-    load8(v, f);
+  auto stage8 = [&](int v, const float (&f)[8]) {
     int sum = 0;
-    uint32_t dig[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+    // balanced base-256 digits of X at once: the bytes of X + 0x808080 (in [0, 2^24) for |X| <= 2^22)
+    // are d_i + 128, so XOR with 0x808080 leaves d0, d1, d2 as int8 in bytes 0..2
+    uint32_t e[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       // round to the nearest integer (ties to even): |x * 2^-s| < 2^22, so adding 1.5 * 2^23 leaves
       // the integer in the low mantissa bits
       const int X = static_cast<int>(__float_as_uint(__fadd_rn(__fmul_rn(f[i], sc), 12582912.f)) - 0x4B400000u);
       sum += X;
-      const int d0 = static_cast<int8_t>(X & 0xFF);
-      const int x1 = (X - d0) >> 8;
-      const int d1 = static_cast<int8_t>(x1 & 0xFF);
-      const int d2 = (x1 - d1) >> 8;
-      const int word = i >> 2, sh8 = 8 * (i & 3);
-      dig[0][word] |= (static_cast<uint32_t>(d0) & 0xFFu) << sh8;
-      dig[1][word] |= (static_cast<uint32_t>(d1) & 0xFFu) << sh8;
-      dig[2][word] |= (static_cast<uint32_t>(d2) & 0xFFu) << sh8;
+      e[i] = (static_cast<uint32_t>(X) + 0x808080u) ^ 0x808080u;
     }
+    // digit planes: byte c of elements 0..3 and 4..7
+    uint32_t dig[3][2];
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t lo = prmt(e[4 * h], e[4 * h + 1], static_cast<uint32_t>(c | ((4 + c) << 4)));
+        const uint32_t hi = prmt(e[4 * h + 2], e[4 * h + 3], static_cast<uint32_t>(c | ((4 + c) << 4)));
+        dig[c][h] = prmt(lo, hi, 0x5410u);
+      }
     // the 4 threads of a 32-wide sub-block add their integer sums (exact)
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     const int k0 = 8 * v, j = k0 >> 5;
     if ((v & 3) == 0) sxs[j] = static_cast<float>(sum);
-    const int par = j & 1;
+    // the live digits only (column 4 * parity + digit); the kernel cleared all columns beforehand
+    uint8_t* xc = xs + 4 * (j & 1) * p.xpitch + k0;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int cs = c >> 2, cd = c & 3;
-      const uint2 val = (cs == par && cd < 3) ? make_uint2(dig[cd < 3 ? cd : 0][0], dig[cd < 3 ? cd : 0][1])
-                                              : make_uint2(0u, 0u);
-      *reinterpret_cast<uint2*>(xs + c * p.xpitch + k0) = val;
+    for (int c = 0; c < 3; ++c) *reinterpret_cast<uint2*>(xc + c * p.xpitch) = make_uint2(dig[c][0], dig[c][1]);
+  };
+  // (nvec and the warps' first vectors are multiples of 32, so every lane of a warp runs the same
+  // iterations: the sub-block sums shuffle across 4 lanes)
+  if (in_regs) {
+#pragma unroll
+    for (int r = 0; r < kRegVec; ++r)
+      if (tid + r * NT < nvec) stage8(tid + r * NT, fr[r]);
+  } else {
+    for (int v = tid; v < nvec; v += NT) {
+      float f[8];
+      load8(v, f);
+      stage8(v, f);
     }
   }
   __syncthreads();
@@ -796,6 +833,12 @@ __device__ void gemv_stage_x(const GemvParams& p, uint8_t* smem, const GemvLayou
   }
 }
 
+// floor(a * b / c) for a * b < 2^53 and c < 2^20, in double precision (exact: a quotient within
+// 1/c below an integer is not rounded up to it), instead of an emulated 64-bit integer division
+__device__ __forceinline__ int muldiv_floor(int64_t a, int64_t b, int64_t c) {
+  return static_cast<int>(floor(__ddiv_rn(static_cast<double>(a * b), static_cast<double>(c))));
+}
+
 __device__ __forceinline__ int worker_of_unit(int64_t u, int64_t U, int W) {
   return static_cast<int>(((u + 1) * W - 1) / U);
 }
@@ -883,7 +926,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   const int NW = blockDim.x >> 5, S = p.nslots;
   // ENG = 1: the integer engine (Q4_K, one token) stages 8 masked int8 digit columns
   const int ncols = ENG ? 8 : ((XT == XT_F32) ? 2 * p.M : p.M);
-  const GemvLayout L = gemv_layout(WT, ncols, p.K, p.xg, NW, S, p.pitch, p.xpitch);
+  const GemvLayout L = gemv_layout(WT, ncols, p.K, p.xg, NW, S, p.pitch, p.xpitch, p.cta_mode ? NW : 0);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * GEMV_MAXS;
   uint8_t* ring = smem + L.off_ring + warp * S * 16 * p.pitch;
   __shared__ float red[2 * GEMV_MAXW];
@@ -905,10 +948,19 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   int U = 0, a = 0, b = 0;  // unit counts fit in 32 bits (checked on the host)
   Cursor ci;                // issue cursor
   int issued = 0, consumed = 0, islot = 0;  // islot = issued % S, kept without a division
+  int ua = 0, ub = 0;  // cta mode: this CTA's units (whole tiles)
   auto setup_range = [&](int ngroups) {
     U = ngroups * tpg * nsb;
-    a = static_cast<int>(static_cast<int64_t>(U) * wid / W);
-    b = static_cast<int>(static_cast<int64_t>(U) * (wid + 1) / W);
+    if (p.cta_mode) {
+      const int T = ngroups * tpg;
+      ua = muldiv_floor(T, blockIdx.x, G) * nsb;
+      ub = muldiv_floor(T, blockIdx.x + 1, G) * nsb;
+      a = ua + (ub - ua) * warp / NW;
+      b = ua + (ub - ua) * (warp + 1) / NW;
+    } else {
+      a = muldiv_floor(U, wid, W);
+      b = muldiv_floor(U, wid + 1, W);
+    }
     ci = cursor_at(a, nsb, tpg);
   };
   auto prefetch = [&]() {
@@ -926,16 +978,23 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
     setup_range(p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
     prefetch();
   }
+  if (ENG) {
+    // the digit columns are zero outside their sub-blocks: clear them all before the wait (the
+    // staging after it writes only the live digits; its first __syncthreads orders the two)
+    uint4* z = reinterpret_cast<uint4*>(smem + L.off_xs);
+    const int nz = p.xg * 8 * p.xpitch / 16;
+    for (int i = threadIdx.x; i < nz; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
   pdl_wait();
   if (!early) {
     setup_range(p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
     prefetch();
   }
   // stage the activations of every group this CTA touches (one group when x is shared)
-  const int64_t c0 = static_cast<int64_t>(U) * (static_cast<int64_t>(blockIdx.x) * NW) / W;
-  const int64_t c1 = static_cast<int64_t>(U) * (static_cast<int64_t>(blockIdx.x + 1) * NW) / W;
-  const int gfirst = (c1 > c0) ? static_cast<int>((c0 / nsb) / tpg) : 0;
-  const int glast = (c1 > c0) ? static_cast<int>(((c1 - 1) / nsb) / tpg) : 0;
+  const int c0 = p.cta_mode ? ua : muldiv_floor(U, blockIdx.x * NW, W);
+  const int c1 = p.cta_mode ? ub : muldiv_floor(U, (blockIdx.x + 1) * NW, W);
+  const int gfirst = (c1 > c0) ? (c0 / nsb) / tpg : 0;
+  const int glast = (c1 > c0) ? ((c1 - 1) / nsb) / tpg : 0;
   if (ENG) {
     if (p.x_group_stride == 0) {
       gemv_stage_x_i8<XT>(p, smem, L, 0, 0, red);
@@ -974,6 +1033,7 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   const int* misc0 = reinterpret_cast<const int*>(smem + L.off_misc);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
+  int fin_tile = -1, fin_grp = 0, fin_lt = 0, fin_xsl = 0;  // cta mode: the tile this warp finishes
   Cursor cc = cursor_at(a, nsb, tpg);  // consume cursor
   int slot = 0, phase = 0;
   while (cc.u < b) {
@@ -1049,6 +1109,18 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
       const int* misc = misc0 + xsl * 8;
       if (whole) {
         gemv_epilogue<WT, XT, EPI>(p, misc, grp, lt, acc, lane);
+      } else if (p.cta_mode) {
+        // piece of a tile cut between warps of this CTA: slot 0 = this warp's first tile, 1 = its last;
+        // the warp holding the tile's last unit sums the pieces after the loop
+        const int slot2 = (seg0 == a) ? 0 : 1;
+        *reinterpret_cast<float4*>(smem + L.off_part + ((warp * 2 + slot2) * 32 + lane) * 16) =
+            make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (cc.u == (ch.tile + 1) * nsb) {
+          fin_tile = ch.tile;
+          fin_grp = grp;
+          fin_lt = lt;
+          fin_xsl = xsl;
+        }
       } else {
         // this worker holds units [seg0, cc.u) of the tile: slot 0 = its first tile, 1 = its last
         const int slot2 = (seg0 == a) ? 0 : 1;
@@ -1100,6 +1172,26 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
     // a bounded wait gave up: never leave with this warp's copies in flight
     for (int j = consumed; j < issued; ++j)
       mbar_wait_bounded(&bars[j % S], (j / S) & 1, p.status, ST_TIMEOUT_FULL, 200000000LL);
+  }
+  if (p.cta_mode) {
+    __syncthreads();
+    if (fin_tile >= 0) {
+      // the pieces of the tile in warp order (a warp's slot: 0 when the tile is its first tile)
+      const int t0u = fin_tile * nsb, t1u = t0u + nsb;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int w2 = 0; w2 < NW; ++w2) {
+        const int a2 = ua + (ub - ua) * w2 / NW, b2 = ua + (ub - ua) * (w2 + 1) / NW;
+        if (a2 < b2 && a2 < t1u && b2 > t0u) {
+          const float4 r = *reinterpret_cast<const float4*>(smem + L.off_part +
+                                                            ((w2 * 2 + (a2 >= t0u ? 0 : 1)) * 32 + lane) * 16);
+          v[0] = __fadd_rn(v[0], r.x);
+          v[1] = __fadd_rn(v[1], r.y);
+          v[2] = __fadd_rn(v[2], r.z);
+          v[3] = __fadd_rn(v[3], r.w);
+        }
+      }
+      gemv_epilogue<WT, XT, EPI>(p, misc0 + fin_xsl * 8, fin_grp, fin_lt, v, lane);
+    }
   }
 }
 
@@ -1158,31 +1250,51 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   // f16 engine: K fp16 values per column; integer engine: K bytes per column, +32 so that the 8 columns
   // read by a half-warp start 8 banks apart
   p.xpitch = engi ? p.K + 32 : ((p.K * 2 + 127) & ~127) + 64;
+  // at least ~4 units per worker: fewer pieces per tile when a launch has few units
+  const int64_t want_w = std::max<int64_t>(4, std::min<int64_t>(16, U / (4 * static_cast<int64_t>(grid))));
+  // A launch with few units per CTA (a single decode GEMV) is latency-bound: its weights are on the
+  // way before it may start, and what remains is the activation staging, each warp's short run of
+  // units and the sums of tiles cut between warps. It runs in cta mode: whole tiles per CTA, pieces
+  // summed in shared memory (no global partials, fences or arrival counters), down to one ring slot
+  // per warp.
+  const bool small = want_w < 16;
+  const int64_t T = static_cast<int64_t>(p.n_groups) * ((p.N + rpt - 1) / rpt);
+  p.cta_mode = small ? 1 : 0;
+  if (small) grid = static_cast<int>(std::min<int64_t>(num_sms, T));
+  // 8 warps and at most half an SM's shared memory, so that the next launch's CTAs become resident
+  // beside this one and prefetch their weights while it finishes (measured: 3.98 / 6.18 us per launch
+  // of 16 / 4096 rows x 4096 against 4.82 / 6.44 us with 16 warps that fill the SM)
+  const int small_w = 8;
   if (p.x_group_stride == 0) {
     p.xg = 1;
   } else {
-    const int64_t per_cta = (U + grid - 1) / grid;
+    const int64_t per_cta = small ? ((T + grid - 1) / grid) * (p.K / 256) : (U + grid - 1) / grid;
     p.xg = static_cast<int>(std::min<int64_t>(p.n_groups, (per_cta + upg - 1) / upg + 1));
     if (p.xg > GEMV_MAXXG) return set_error(-1, "gemv: too many activation groups per CTA");
   }
-  const int limit = 232448 - 1024 - 2 * GEMV_MAXW * 4;  // dynamic smem limit minus static
-  // at least ~4 units per worker: fewer pieces per tile when a launch has few units
-  const int64_t want_w = std::max<int64_t>(4, std::min<int64_t>(16, U / (4 * static_cast<int64_t>(grid))));
+  const int full_limit = 232448 - 1024 - 2 * GEMV_MAXW * 4;  // dynamic smem limit minus static
+  int limit = full_limit;
   int nw = 0, ns = 0;
-  for (int cand_w : {16, 12, 8, 4}) {
-    if (cand_w > want_w && cand_w > 4) continue;
-    for (int cand_s = GEMV_MAXS; cand_s >= 2; --cand_s) {
-      if (gemv_layout(wt, ncols, p.K, p.xg, cand_w, cand_s, p.pitch, p.xpitch).total <= limit) {
-        nw = cand_w;
-        ns = cand_s;
-        break;
+  // small launches try half an SM first (unless the caller asks for a minimum), then the whole SM
+  for (int pass = (small && min_smem == 0) ? 0 : 1; pass < 2 && !nw; ++pass) {
+    limit = pass == 0 ? 232448 / 2 - 1024 - 2 * GEMV_MAXW * 4 : full_limit;
+    for (int cand_w : {16, 12, 8, 4}) {
+      if (!small && cand_w > want_w && cand_w > 4) continue;
+      if (small && cand_w > small_w) continue;
+      for (int cand_s = GEMV_MAXS; cand_s >= (small ? 1 : 2); --cand_s) {
+        if (gemv_layout(wt, ncols, p.K, p.xg, cand_w, cand_s, p.pitch, p.xpitch, p.cta_mode ? cand_w : 0).total <=
+            limit) {
+          nw = cand_w;
+          ns = cand_s;
+          break;
+        }
       }
+      if (nw) break;
     }
-    if (nw) break;
   }
   if (!nw) return set_error(-1, "gemv: activation block too large for shared memory");
   p.nslots = ns;
-  const int smem = std::min(limit, std::max(min_smem, gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch).total));
+  const int smem = std::min(limit, std::max(min_smem, gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch, p.cta_mode ? nw : 0).total));
   if (engi) {
     if (xt == XT_F32) return launch_one<WT_Q4K, XT_F32, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
     if (xt == XT_BF16) return launch_one<WT_Q4K, XT_BF16, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);

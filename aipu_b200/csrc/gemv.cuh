@@ -71,6 +71,7 @@ struct GemvParams {
                              // griddepcontrol.wait
   int tm_esz;                // tensor-map element size (bytes)
   int tm_box;                // tensor-map box width (elements)
+  int cta_mode;              // 1: whole tiles per CTA, tiles cut between its warps summed in shared memory
   alignas(64) CUtensorMap tmap0;  // [expert][row][row bytes / esz] over w0
   alignas(64) CUtensorMap tmap1;  // same over w1 (EPI_SWIGLU)
 };
