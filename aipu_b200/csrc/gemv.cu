@@ -1213,7 +1213,7 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ((xt == XT_F32) ? 2 * p.M : p.M) > 8)
     return set_error(-1, "gemv: bad shape");
   // the integer dot engine for Q4_K rows and one token (the decode GEMV); the f16 engine otherwise
-  const bool engi = (wt == WT_Q4K && epi == EPI_STORE && p.M == 1);
+  const bool engi = (wt == WT_Q4K && p.M == 1 && (epi == EPI_STORE || xt == XT_BF16));
   const int ncols = engi ? 8 : ((xt == XT_F32) ? 2 * p.M : p.M);
   if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
   if ((reinterpret_cast<uintptr_t>(p.x) & 15u) != 0) return set_error(-1, "gemv: activations must be 16-byte aligned");
@@ -1297,7 +1297,8 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   const int smem = std::min(limit, std::max(min_smem, gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch, p.cta_mode ? nw : 0).total));
   if (engi) {
     if (xt == XT_F32) return launch_one<WT_Q4K, XT_F32, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
-    if (xt == XT_BF16) return launch_one<WT_Q4K, XT_BF16, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
+    if (xt == XT_BF16 && epi == EPI_STORE) return launch_one<WT_Q4K, XT_BF16, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
+    if (xt == XT_BF16 && epi == EPI_SWIGLU) return launch_one<WT_Q4K, XT_BF16, EPI_SWIGLU, 1>(p, grid, nw, smem, stream, pdl);
   }
 #define AIPU_GEMV_CASE(W, X, E)                                              \
   if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, nw, smem, stream, pdl);
