@@ -196,8 +196,13 @@ def moe_router(router_wtype: int, w: torch.Tensor, x: torch.Tensor, n_experts: i
     sw = torch.empty((M, topk), dtype=torch.bfloat16, device=x.device)
     gate = torch.empty((M, n_experts), dtype=torch.bfloat16, device=x.device)
     logits = torch.empty((M, n_experts), dtype=torch.bfloat16, device=x.device) if want_logits else None
-    check(lib().aipu_moe_router(ctx.handle, router_wtype, _ptr(w), _ptr(bias), _ptr(x), M, K, n_experts, topk,
-                                scale, _ptr(sel), _ptr(sw), _ptr(gate), _ptr(logits), _stream(x.device)))
+    # the C entry point takes up to 1024 tokens per call; rows are independent
+    x = x.contiguous()
+    for m0 in range(0, M, 1024):
+        m1 = min(M, m0 + 1024)
+        check(lib().aipu_moe_router(ctx.handle, router_wtype, _ptr(w), _ptr(bias), _ptr(x[m0:m1]), m1 - m0, K,
+                                    n_experts, topk, scale, _ptr(sel[m0:m1]), _ptr(sw[m0:m1]), _ptr(gate[m0:m1]),
+                                    _ptr(logits[m0:m1]) if logits is not None else None, _stream(x.device)))
     return (sel, sw, gate, logits) if want_logits else (sel, sw, gate)
 
 

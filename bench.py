@@ -39,9 +39,10 @@ C1_W_BYTES = C1_N * (C1_K // 256) * 144                # 9,437,184
 C1_BYTES = C1_W_BYTES + C1_K * 4 + C1_N * 2             # + x fp32 + y bf16 = 9,461,760
 METRIC = "Q4_K GEMV HBM GB/s"
 # DRAM bytes per C1 GEMV of the grouped kernel, from one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum) of an 8-matrix C1 launch divided by 8; the full launch reads every weight
-# byte once, so its traffic is this times the matrices per launch.
-C1_TRAFFIC_PER_GEMV = None
+# dram__bytes_write.sum = 75,807,744 + 2,077,696 B) of an 8-matrix C1 launch
+# (`bench.py --case gemv --x-f32 --groups 8`) divided by 8; the full launch reads every weight byte
+# once, so its traffic is this times the matrices per launch.
+C1_TRAFFIC_PER_GEMV = 9_735_680
 MOE_H, MOE_F, MOE_E, MOE_T = 6144, 2048, 256, 8
 
 
