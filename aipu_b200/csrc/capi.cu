@@ -1166,6 +1166,10 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
   MoeScratch sc = {};
   int rc = moe_scratch(c, Gtok, El, T, H, F, sc);
   if (rc) return rc;
+  // the shared expert runs on the side stream beside the router and the exchange (as in
+  // aipu_moe_layer: forked before the router, on the SMs the router leaves free), joined before the
+  // combine
+  if (shared && (rc = set_cuda_error(cudaEventRecord(c->ev_fork, s), "eventRecord"))) return rc;
   // 1. route the local tokens (all experts of the layer)
   RouterParams rp = {};
   rp.wt = W->router_wtype;
@@ -1183,14 +1187,20 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
   rp.counters = c->router_counters;
   rp.status = c->status;
   if ((rc = router_launch(rp, s, false))) return rc;
-  // 2. dispatch
+  // 2. shared expert on the local tokens (side stream)
+  if (shared) {
+    const int router_ctas = router_grid_ctas(rp);
+    const int side_sms = std::max(1, c->num_sms - router_ctas);
+    if ((rc = set_cuda_error(cudaStreamWaitEvent(c->side, c->ev_fork, 0), "streamWaitEvent"))) return rc;
+    rc = swiglu_groups(c, c->ws[1], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype, W->shared_down_w,
+                       H, F, 1, nullptr, nullptr, 1, nullptr, 0, x, M, sc.h_sh, y_sh, c->side, false, side_sms,
+                       kSmemPerSm - router_smem_bytes(rp));
+    if (rc) return rc;
+    if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
+  }
+  // 3. dispatch
   if ((rc = ep_bump_launch(e->p, s))) return rc;
   if ((rc = ep_dispatch_launch(e->p, static_cast<const uint16_t*>(x), sel, static_cast<int>(M), s))) return rc;
-  // 3. shared expert on the local tokens while the peers' tokens arrive
-  if (shared && (rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->shared_gate_w, W->shared_up_w, W->down_wtype,
-                                    W->shared_down_w, H, F, 1, nullptr, nullptr, 1, nullptr, 0, x, M, sc.h_sh, y_sh, s,
-                                    false)))
-    return rc;
   // 4. every rank's tokens: local experts
   if ((rc = ep_wait_launch(e->p, 0, s))) return rc;
   const uint8_t* inbox = static_cast<const uint8_t*>(e->buf);
@@ -1207,6 +1217,7 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
   // 5. per-slot outputs into the owners' outboxes
   if ((rc = ep_return_launch(e->p, sc.slot_map, sc.y, static_cast<int>(M), static_cast<int>(Gtok), s))) return rc;
   if ((rc = ep_wait_launch(e->p, 1, s))) return rc;
+  if (shared && (rc = set_cuda_error(cudaStreamWaitEvent(s, c->ev_join, 0), "streamWaitEvent"))) return rc;
   // 6. slot-order combine of this rank's tokens
   return combine_pieces_launch(sel, sel_w, static_cast<int>(M), T, H, static_cast<int>(El),
                                reinterpret_cast<const uint16_t*>(inbox + e->p.off_out), shared ? y_sh : nullptr,
