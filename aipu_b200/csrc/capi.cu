@@ -1,5 +1,6 @@
 // extern "C" entry points (include/aipu_q4k.h) and the per-device context.
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -594,7 +595,10 @@ static int moe_experts_tc(aipu_ctx* c, const aipu_moe_weights* W, const void* x,
                           cudaStream_t s) {
   const int64_t H = W->hidden, F = W->ffn, E = W->n_experts;
   const int T = W->topk;
-  const int nt = 64;  // tokens per tile: about the tokens an expert gets at top-8 of 256
+  // tokens per tile: top-8 of 256 experts gives ~64 tokens per expert at 2048 tokens, spread around
+  // that; a 128-token tile takes most experts whole (one dequantisation of each weight tile), and
+  // the MMA width follows the tile's tokens
+  const int nt = 128;
   const bool shared = W->shared_gate_w && W->shared_up_w && W->shared_down_w && shared_n > 0;
   const int64_t Pmax = M * T + (shared ? shared_n : 0) + 8 * (E + 1);
   const int64_t max_tiles = (M * T + nt - 1) / nt + E + (shared ? (shared_n + nt - 1) / nt : 0);
