@@ -192,6 +192,10 @@ int aipu_ctx_create(aipu_ctx** out, int device) {
     aipu_ctx_destroy(c);
     return set_error(ECUDA_, "ctx_create: stream/event");
   }
+  if (int trc = silu_table_init(c->side)) {
+    aipu_ctx_destroy(c);
+    return trc;
+  }
   *out = c;
   return OK;
 }

@@ -115,6 +115,8 @@ struct TcParams {
 };
 int tc_gemm_launch(TcParams& p, int nt, int n_experts, int max_tiles, int num_sms, cudaStream_t s, bool pdl);
 size_t xt_bytes(int64_t R, int64_t K);
+// builds the device's bf16 SiLU table used by the prefill SwiGLU epilogue (synchronises `s`)
+int silu_table_init(cudaStream_t s);
 int prescale_tiled_launch(const uint16_t* x, int R, int K, const int* rows, int rows_mask, int n_pos_max,
                           const int* n_pos_dev, uint8_t* xt, int* shift, cudaStream_t s, bool pdl);
 

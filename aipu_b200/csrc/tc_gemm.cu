@@ -46,6 +46,28 @@ namespace aipu {
 // sub-block sums at 16 t, lo parts at 128 + 16 t).
 constexpr int XT_SB = 4352;
 
+// ------------------------------------------------------------------ SiLU table
+// bf16(silu(x)) for every bf16 x (the reference's step sequence, glm_silu_bf), written once per
+// device at context creation: the SwiGLU epilogue of the prefill GEMM looks its gate values up
+// (one load instead of the ~60-instruction sequence per output), with identical bits.
+__device__ uint16_t g_silu_tab[65536];
+
+__global__ void silu_table_kernel() {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536u) g_silu_tab[i] = static_cast<uint16_t>(__float_as_uint(glm_silu_bf(__uint_as_float(i << 16))) >> 16);
+}
+
+int silu_table_init(cudaStream_t s) {
+  silu_table_kernel<<<256, 256, 0, s>>>();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error(e, "silu_table_kernel");
+  return set_cuda_error(cudaStreamSynchronize(s), "silu_table_kernel");
+}
+
+__device__ __forceinline__ float silu_lookup(float xbf) {
+  return __uint_as_float(static_cast<uint32_t>(__ldg(&g_silu_tab[__float_as_uint(xbf) >> 16])) << 16);
+}
+
 // ------------------------------------------------------------------ activation prescale (tiled)
 // Row p of the output (p < n_pos) takes source row src = rows ? rows[p] : p (rows_mask: src = p when
 // rows[p] >= 0); src < 0 or src >= R gives a zero row. fp16 values x * 2^-shift[p] (max |x| * 2^-s
@@ -730,7 +752,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) aipu_tc_gemm_kernel(const __gri
             const float s = exp2i(shn);
             const float gb = bf16_round_f(__fmul_rn(g, s));
             const float ub = bf16_round_f(__fmul_rn(u, s));
-            p.y[static_cast<int64_t>(it.t0 + col) * p.N + nrow] = bf16_rne_bits(__fmul_rn(glm_silu_bf(gb), ub));
+            p.y[static_cast<int64_t>(it.t0 + col) * p.N + nrow] = bf16_rne_bits(__fmul_rn(silu_lookup(gb), ub));
           }
         }
       } else {
