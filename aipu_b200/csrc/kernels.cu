@@ -304,6 +304,26 @@ __device__ void router_union(const RouterParams& p, const int* sel_s) {
 // activation slices by bulk copies) into a shared-memory ring, so the chains never wait on DRAM
 // latency. GGUF-row routers dequantise each weight exactly in the chain.
 constexpr int RT_CHUNK = 128;   // k rows per stage
+// EG = 64 (many tokens): each chain lane carries two experts (2 lane, 2 lane + 1) as one packed f32x2
+// chain: fl(acc + fl(x * w)) per lane of the pair with one product and one add instruction for both.
+// The product is fma(x, w, -0) with -0 read from the parameters (exactly fl(x * w), signed zeros
+// included), so the assembler cannot contract it with the following add.
+__device__ __forceinline__ unsigned long long rt_pk(float2 a) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+  return r;
+}
+__device__ __forceinline__ float2 rt_upk(unsigned long long r) {
+  float2 a;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
+  return a;
+}
+__device__ __forceinline__ float2 rt_step2(float2 acc, float2 x, float2 w, float2 nz) {
+  unsigned long long pr, d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(pr) : "l"(rt_pk(x)), "l"(rt_pk(w)), "l"(rt_pk(nz)));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(rt_pk(acc)), "l"(pr));
+  return rt_upk(d);
+}
 // experts per CTA: 8 for few tokens (lanes 0..7 run the chains, four times the CTAs stream the
 // router), 32 for many tokens (every lane runs a chain)
 constexpr int RT_MB = 8;        // tokens per CTA
@@ -314,7 +334,8 @@ constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
 template <int EG>
 struct RtCfg {
   static constexpr bool SPLIT = (EG == 8);
-  static constexpr int NST = SPLIT ? 8 : 6;  // input ring depth
+  static constexpr bool PAIR = (EG == 64);   // two experts per chain lane
+  static constexpr int NST = SPLIT ? 8 : (PAIR ? 3 : 6);  // input ring depth (PAIR: two CTAs per SM)
   static constexpr int WBYTES = RT_CHUNK * EG * 4;
   static constexpr int NWARP = SPLIT ? 2 * RT_MB + 1 : RT_MB + 1;
   static constexpr int PSTR = 132;            // floats per expert row of a product slot (padded)
@@ -343,7 +364,7 @@ extern "C" int aipu_debug_rt_gt(unsigned long long* out) {
 }
 #endif
 template <int RT_EG>
-__global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(const __grid_constant__ RouterParams p) {
+__global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP, RtCfg<RT_EG>::PAIR ? 2 : 1) router_strict_kernel(const __grid_constant__ RouterParams p) {
   using RC = RtCfg<RT_EG>;
   constexpr int RT_NST = RC::NST;
   constexpr int RT_WBYTES = RC::WBYTES;
@@ -356,8 +377,10 @@ __global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(con
   uint8_t* ring = smem + RC::OFF_RING;  // barriers first; TMA destinations 128-byte aligned
   __shared__ int last_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = blockIdx.x * RT_EG, e = e0 + lane;
-  const bool live = (lane < RT_EG) && (e < p.E);
+  // lane's expert(s): e (and e + 1 when two experts per lane)
+  const int e0 = blockIdx.x * RT_EG, e = RC::PAIR ? e0 + 2 * lane : e0 + lane;
+  const bool live = (RC::PAIR || lane < RT_EG) && (e < p.E);
+  const bool live1 = RC::PAIR && (e + 1 < p.E);
   const int m0 = blockIdx.y * RT_MB;
   const int mb = min(RT_MB, p.M - m0);
   // SPLIT: product slots per token (the RT_MB * NPS slots shared by the block's tokens, at most 16
@@ -483,8 +506,66 @@ __global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(con
   // consumer warp `warp` = token m0 + warp
   const int m = m0 + warp;
   if (warp < mb) {
-    float acc = 0.f;
-    if (RC::SPLIT && dense) {
+    float acc = 0.f, acc1 = 0.f;
+    if (RC::PAIR && dense) {
+      bool ok = true;
+      const float2 nz = make_float2(p.neg_zero, p.neg_zero);
+      float2 a2 = make_float2(0.f, 0.f);
+      for (int c = 0; c < nchunk; ++c) {
+        const int slot = c % RT_NST;
+        const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
+        if (ok) ok = mbar_wait_bounded(&full[slot], (c / RT_NST) & 1, p.status, ST_TIMEOUT_FULL);
+        if (ok) {
+          const uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
+          // row k of the box: 64 experts, this lane's pair at 8 lane bytes (64-bit loads, conflict-free)
+          const float2* ws = reinterpret_cast<const float2*>(st) + lane;
+          const uint16_t* xs = reinterpret_cast<const uint16_t*>(st + RT_WBYTES + warp * RT_CHUNK * 2);
+          if (kl == RT_CHUNK) {
+            // batches of 16 k: the next batch's operands loaded while this batch's chain runs
+            constexpr int BK = 16;
+            float2 wv[BK];
+            uint4 xv[2];
+#pragma unroll
+            for (int i = 0; i < BK; ++i) wv[i] = ws[i * 32];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) xv[i] = reinterpret_cast<const uint4*>(xs)[i];
+#pragma unroll
+            for (int k0b = 0; k0b < RT_CHUNK; k0b += BK) {
+              float2 wc[BK];
+              float xc[BK];
+#pragma unroll
+              for (int i = 0; i < BK; ++i) wc[i] = wv[i];
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  xc[8 * i + 2 * h] = __uint_as_float(xw[h] << 16);
+                  xc[8 * i + 2 * h + 1] = __uint_as_float(xw[h] & 0xFFFF0000u);
+                }
+              }
+              if (k0b + BK < RT_CHUNK) {
+#pragma unroll
+                for (int i = 0; i < BK; ++i) wv[i] = ws[(k0b + BK + i) * 32];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) xv[i] = reinterpret_cast<const uint4*>(xs + k0b + BK)[i];
+              }
+#pragma unroll
+              for (int i = 0; i < BK; ++i) a2 = rt_step2(a2, make_float2(xc[i], xc[i]), wc[i], nz);
+            }
+          } else {
+            for (int k = 0; k < kl; ++k) {
+              const float xk = bf16_bits_to_f32(xs[k]);
+              a2 = rt_step2(a2, make_float2(xk, xk), ws[k * 32], nz);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      acc = a2.x;
+      acc1 = a2.y;
+    } else if (RC::SPLIT && dense) {
       // the chain over the products, in k order; 32 of them loaded ahead of the adds
       bool ok = true;
       uint32_t ready_seen = 0u;
@@ -601,6 +682,11 @@ __global__ void __launch_bounds__(32 * (2 * RT_MB + 1)) router_strict_kernel(con
       p.gate[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(glm_sigmoid_bf(logit));
       if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
     }
+    if (live1) {
+      const float logit = bf16_round_f(acc1);
+      p.gate[static_cast<int64_t>(m) * E + e + 1] = bf16_rne_bits(glm_sigmoid_bf(logit));
+      if (p.logits) p.logits[static_cast<int64_t>(m) * E + e + 1] = bf16_rne_bits(logit);
+    }
   }
 #ifdef RT_GT
   if (threadIdx.x == 0) atomicMax(&g_rt_gt[1], rt_gtime());
@@ -648,6 +734,7 @@ static int router_launch_eg(const RouterParams& p, cudaStream_t s, bool pdl) {
     if (arc) return arc;
   }
   RouterParams q = p;
+  q.neg_zero = -0.0f;
   if (p.wt == WT_F32) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.K)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.E) * 4};
@@ -665,17 +752,22 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
   if (p.wt == WT_F32 && (p.E % 4 != 0 || (reinterpret_cast<uintptr_t>(p.w) & 15u) ||
                          (reinterpret_cast<uintptr_t>(p.x) & 15u) || (p.K % 8)))
     return set_error(EINVAL_, "router: fp32 router needs E % 4 == 0, K % 8 == 0 and 16-byte aligned w, x");
-  // few token blocks: spread the router over more SMs; many: every lane of a CTA runs a chain
-  return (p.M <= 4 * RT_MB) ? router_launch_eg<8>(p, s, pdl) : router_launch_eg<32>(p, s, pdl);
+  // few token blocks: spread the router over more SMs; many: every lane of a CTA runs a packed chain
+  // over two experts (dense fp32 router) or one (GGUF-row router)
+  if (p.M <= 4 * RT_MB) return router_launch_eg<8>(p, s, pdl);
+  return (p.wt == WT_F32) ? router_launch_eg<64>(p, s, pdl) : router_launch_eg<32>(p, s, pdl);
 }
 
+static int router_eg(const RouterParams& p) { return (p.M <= 4 * RT_MB) ? 8 : (p.wt == WT_F32 ? 64 : 32); }
+
 int router_grid_ctas(const RouterParams& p) {
-  const int eg = (p.M <= 4 * RT_MB) ? 8 : 32;
+  const int eg = router_eg(p);
   return ((p.E + eg - 1) / eg) * ((p.M + RT_MB - 1) / RT_MB);
 }
 
 int router_smem_bytes(const RouterParams& p) {
-  return (p.M <= 4 * RT_MB) ? RtCfg<8>::SMEM : RtCfg<32>::SMEM;
+  const int eg = router_eg(p);
+  return eg == 8 ? RtCfg<8>::SMEM : (eg == 64 ? RtCfg<64>::SMEM : RtCfg<32>::SMEM);
 }
 
 // ------------------------------------------------------------------ combine
