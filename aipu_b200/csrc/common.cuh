@@ -58,9 +58,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Every bounded wait's limit in SM clock cycles. The device status word passed to the kernels is the
 // first int of a 16-byte block whose 64-bit word at byte 8 holds the wait limit set for the context
-// (aipu_ctx_set_wait_limit; 0 = the default of 4e9 cycles, about 2 s). Read only after a first
-// try failed, so the common path costs nothing.
+// (aipu_ctx_set_wait_limit; 0 = the default of 4e9 cycles, about 2 s). Read only once a wait has
+// lasted kWaitGrace cycles: a wait that ends sooner never stalls on that global load (limits below
+// the grace act as the grace).
 constexpr long long kDefaultWaitCycles = 4000000000LL;
+constexpr long long kWaitGrace = 65536;
 __device__ __forceinline__ long long wait_limit(const int* status) {
   if (!status) return kDefaultWaitCycles;
   const long long v = *reinterpret_cast<const volatile long long*>(status + 2);
@@ -72,12 +74,16 @@ __device__ __forceinline__ long long wait_limit(const int* status) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int bit,
                                                   long long limit_cycles = 0) {
   if (mbar_try_wait(bar, parity)) return true;
-  const long long limit = limit_cycles > 0 ? limit_cycles : wait_limit(status);
+  long long limit = limit_cycles;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > limit) {
-      if (status) atomicOr(status, bit);
-      return false;
+    const long long el = clock64() - t0;
+    if (el > kWaitGrace) {
+      if (limit <= 0) limit = wait_limit(status);
+      if (el > limit) {
+        if (status) atomicOr(status, bit);
+        return false;
+      }
     }
   }
   return true;
@@ -101,12 +107,14 @@ __device__ __forceinline__ uint32_t warp_wait_counter(const uint32_t* f, uint32_
   // every lane acquires; the value returned is the warp minimum (each lane saw at least that much)
   uint32_t v = ld_acquire_cta_shared(f) - target;
   if (__all_sync(0xffffffffu, static_cast<int32_t>(v) >= 0)) return __reduce_min_sync(0xffffffffu, v) + target;
-  const long long limit = limit_cycles > 0 ? limit_cycles : wait_limit(status);
+  long long limit = limit_cycles;
   const long long t0 = clock64();
   while (true) {
     v = ld_acquire_cta_shared(f) - target;
     if (__all_sync(0xffffffffu, static_cast<int32_t>(v) >= 0)) return __reduce_min_sync(0xffffffffu, v) + target;
-    if (__any_sync(0xffffffffu, clock64() - t0 > limit)) {
+    const long long el = clock64() - t0;
+    if (el > kWaitGrace && limit <= 0) limit = wait_limit(status);
+    if (__any_sync(0xffffffffu, el > kWaitGrace && el > limit)) {
       if (status && (threadIdx.x & 31) == 0) atomicOr(status, bit);
       return target - 1u;
     }

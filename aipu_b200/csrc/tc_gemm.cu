@@ -221,11 +221,13 @@ static_assert(sizeof(TcBars) <= 1024, "barrier block");
 // bounded wait that also gives up as soon as another role of the CTA gave up
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcBars* sb, int* status, int bit) {
   if (mbar_try_wait(bar, parity)) return true;
-  const long long limit = wait_limit(status);
+  long long limit = 0;  // the context's limit, read once the wait outlasts the grace period
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*reinterpret_cast<volatile int*>(&sb->abort)) return false;
-    if (clock64() - t0 > limit) {
+    const long long el = clock64() - t0;
+    if (el > kWaitGrace && limit == 0) limit = wait_limit(status);
+    if (el > kWaitGrace && el > limit) {
       *reinterpret_cast<volatile int*>(&sb->abort) = 1;
       if (status) atomicOr(status, bit);
       return false;
