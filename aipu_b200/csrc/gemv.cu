@@ -25,7 +25,9 @@ __host__ __device__ inline GemvLayout gemv_layout(int wt, int ncols, int K, int 
   L.off_misc = GEMV_MAXW * GEMV_MAXS * 8;
   L.off_xs = L.off_misc + 256;
   L.off_sxs = L.off_xs + xg * ncols * xpitch;
-  const int sx = (wt == WT_Q4K) ? xg * ncols * (K / 256) * 64 : 0;
+  // Q4_K: f16-engine sub-block sums (>= the integer engine's K / 32 floats); Q6_K: the integer engine's
+  // K / 16 floats
+  const int sx = (wt == WT_Q4K) ? xg * ncols * (K / 256) * 64 : (wt == WT_Q6K ? xg * (K / 4) : 0);
   L.off_ring = (L.off_sxs + sx + 127) & ~127;
   L.off_part = L.off_ring + nw * nslots * 16 * pitch;
   L.total = L.off_part + part_nw * 2 * 32 * 16;
@@ -401,14 +403,16 @@ __device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[
 // threads). Column c = 4 * parity + digit (digit < 3; columns 3 and 7 stay zero) holds, at every k
 // whose sub-block j has j % 2 == parity, digit `digit` of X; zero elsewhere (the columns are zero on
 // entry). misc[0..1] = prescale shift s (value = sum * 2^s). Leaves with a __syncthreads.
-template <int XT>
+// Q4_K: 32-weight sub-blocks, sums sxs[j]; Q6_K: 16-weight sub-blocks, sums per super-block in
+// parity-major order (sxs[16 sb + 8 (j % 2) + (j % 16) / 2] for sub-block j).
+template <int WT, int XT>
 __device__ void gemv_stage_x_i8(const GemvParams& p, uint8_t* smem, const GemvLayout& L, int grp, int xs_slot,
                                 float* red) {
   const int tid = threadIdx.x, NT = blockDim.x, NW = NT >> 5;
   const int K = p.K;
   int* misc = reinterpret_cast<int*>(smem + L.off_misc) + xs_slot * 8;
   uint8_t* xs = smem + L.off_xs + xs_slot * 8 * p.xpitch;
-  float* sxs = reinterpret_cast<float*>(smem + L.off_sxs) + xs_slot * (K / 32);
+  float* sxs = reinterpret_cast<float*>(smem + L.off_sxs) + xs_slot * (WT == WT_Q6K ? K / 16 : K / 32);
   const uint8_t* xr = static_cast<const uint8_t*>(p.x) +
                       static_cast<int64_t>(grp) * p.x_group_stride * (XT == XT_F32 ? 4 : 2);
   const int nvec = K / 8;  // 8 activations per vector
@@ -495,13 +499,22 @@ __device__ void gemv_stage_x_i8(const GemvParams& p, uint8_t* smem, const GemvLa
         const uint32_t hi = prmt(e[4 * h + 2], e[4 * h + 3], static_cast<uint32_t>(c | ((4 + c) << 4)));
         dig[c][h] = prmt(lo, hi, 0x5410u);
       }
-    // the 4 threads of a 32-wide sub-block add their integer sums (exact)
+    // the threads of a sub-block (4 for 32 weights, 2 for 16) add their integer sums (exact)
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    const int k0 = 8 * v, j = k0 >> 5;
-    if ((v & 3) == 0) sxs[j] = static_cast<float>(sum);
+    const int k0 = 8 * v;
+    int par;
+    if (WT == WT_Q6K) {
+      const int j = k0 >> 4;
+      par = j & 1;
+      if ((v & 1) == 0) sxs[16 * (j >> 4) + 8 * par + ((j & 15) >> 1)] = static_cast<float>(sum);
+    } else {
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      const int j = k0 >> 5;
+      par = j & 1;
+      if ((v & 3) == 0) sxs[j] = static_cast<float>(sum);
+    }
     // the live digits only (column 4 * parity + digit); the kernel cleared all columns beforehand
-    uint8_t* xc = xs + 4 * (j & 1) * p.xpitch + k0;
+    uint8_t* xc = xs + 4 * par * p.xpitch + k0;
 #pragma unroll
     for (int c = 0; c < 3; ++c) *reinterpret_cast<uint2*>(xc + c * p.xpitch) = make_uint2(dig[c][0], dig[c][1]);
   };
@@ -589,6 +602,84 @@ __device__ __forceinline__ void q4k_i8_fold(float (&acc)[4]) {
   acc[0] = v0;
   acc[2] = v2;
   acc[1] = acc[3] = 0.f;
+}
+
+// Q6_K unit (16 rows g, g + 8 x one super-block) on the integer engine, one token. Block layout
+// [ql 128][qh 64][int8 sc 16][fp16 d] (tools/q4k_ref.py:99-124): weight w = 128 n + 32 c + l has the
+// 6-bit code (ql[64 n + 32 (c & 1) + l] >> 4 (c >> 1)) & 15 | ((qh[32 n + l] >> 2 c) & 3) << 4 and the
+// value d * sc[w / 16] * (code - 32). One u8 x s8 MMA per (n, c) covers 32 weights = two 16-weight
+// sub-blocks, told apart by the parity columns (activation k order = weight order). The codes are
+// assembled four at a time (mask the nibble plane, mask the 2-bit plane shifted into bits 4-5, OR);
+// the -32 offset is applied once per sub-block on the sums S_j of the staged activations. A4: the
+// unit's bytes start 4-byte aligned (else every word comes from two aligned loads; the offset is the
+// same for every row of a tiled slot, so the choice is warp-uniform).
+template <bool A4>
+__device__ __forceinline__ void unit_q6k_i8(uint32_t rg, uint32_t rg8, uint32_t xb, uint32_t sxb, int t, float w0,
+                                            float w1, float (&acc)[4]) {
+  const int par = t >> 1;
+  int D[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0;
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+    uint32_t la[2][2], lb[2][2], qh[2][2];  // [row g / g + 8][l = 4t / 16 + 4t]
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const uint32_t b = (rr ? rg8 : rg) + 4 * t;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        la[rr][hh] = lds4<A4>(b + 64 * n + 16 * hh);
+        lb[rr][hh] = lds4<A4>(b + 64 * n + 32 + 16 * hh);
+        qh[rr][hh] = lds4<A4>(b + 128 + 32 * n + 16 * hh);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t a[4];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t lw = (c & 1) ? lb[rr][hh] : la[rr][hh];
+          const uint32_t nib = (c >> 1) ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
+          const uint32_t hw = qh[rr][hh];
+          const uint32_t hb = (c == 0) ? (hw << 4) : (c == 1) ? (hw << 2) : (c == 2) ? hw : (hw >> 2);
+          a[2 * hh + rr] = nib | (hb & 0x30303030u);
+        }
+      const uint32_t xo = xb + 128 * n + 32 * c + 4 * t;
+      mma_u8s8_16832(D[4 * n + c], a, lds_v1(xo), lds_v1(xo + 16));
+    }
+  }
+  // sub-block j = 8 n + 2 c + parity: this lane's sets use the scales of its column parity
+  int scg[8], sc8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    scg[i] = lds_s8(rg + 192 + 2 * i + par);
+    sc8[i] = lds_s8(rg8 + 192 + 2 * i + par);
+  }
+  int c0g = 0, c1g = 0, c08 = 0, c18 = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c0g += scg[i] * D[i][0];
+    c1g += scg[i] * D[i][1];
+    c08 += sc8[i] * D[i][2];
+    c18 += sc8[i] * D[i][3];
+  }
+  // the -32 offset: this lane takes the sub-blocks 2 m + parity, m = 4 (t & 1) .. + 3 (sets n = t & 1)
+  const uint4 S = lds_v4(sxb + 4 * (8 * par + 4 * (t & 1)));
+  const float Sv[4] = {__uint_as_float(S.x), __uint_as_float(S.y), __uint_as_float(S.z), __uint_as_float(S.w)};
+  float og = 0.f, o8 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int sg = (t & 1) ? scg[4 + c] : scg[c], s8 = (t & 1) ? sc8[4 + c] : sc8[c];
+    og = fmaf(static_cast<float>(sg), Sv[c], og);
+    o8 = fmaf(static_cast<float>(s8), Sv[c], o8);
+  }
+  const float vg = fmaf(__int2float_rn(c1g), w1, __fmul_rn(__int2float_rn(c0g), w0));
+  const float v8 = fmaf(__int2float_rn(c18), w1, __fmul_rn(__int2float_rn(c08), w0));
+  const float dg = f16_bits_to_f32(lds_u16(rg + 208)), d8 = f16_bits_to_f32(lds_u16(rg8 + 208));
+  acc[0] = fmaf(dg, fmaf(-32.f, og, vg), acc[0]);
+  acc[2] = fmaf(d8, fmaf(-32.f, o8, v8), acc[2]);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -997,9 +1088,9 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   const int glast = (c1 > c0) ? ((c1 - 1) / nsb) / tpg : 0;
   if (ENG) {
     if (p.x_group_stride == 0) {
-      gemv_stage_x_i8<XT>(p, smem, L, 0, 0, red);
+      gemv_stage_x_i8<WT, XT>(p, smem, L, 0, 0, red);
     } else {
-      for (int g = gfirst; g <= glast && g - gfirst < p.xg; ++g) gemv_stage_x_i8<XT>(p, smem, L, g, g - gfirst, red);
+      for (int g = gfirst; g <= glast && g - gfirst < p.xg; ++g) gemv_stage_x_i8<WT, XT>(p, smem, L, g, g - gfirst, red);
     }
   } else if (p.x_group_stride == 0) {
     gemv_stage_x<WT, XT, EPI>(p, smem, L, 0, 0, ncols, red);
@@ -1012,8 +1103,10 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
   // and the PRMT selectors of its scale bytes (sub-block 2g + t / 2 of the 0-3 / 4-7 tables: byte
   // t / 2 for g even, 2 + t / 2 for g odd) and min bytes (sub-blocks 2t, 2t + 1)
   const int tl = lane & 3;
-  const float w0 = (tl & 1) ? ((tl & 2) ? 4096.f : 65536.f) : ((tl & 2) ? 0.0625f : 1.f);
-  const float w1 = (tl & 1) ? 0.f : ((tl & 2) ? 16.f : 256.f);
+  // (Q6_K codes are assembled whole: no factor 16 in either parity)
+  const bool x16 = (WT == WT_Q4K) && (tl & 2);
+  const float w0 = (tl & 1) ? (x16 ? 4096.f : 65536.f) : (x16 ? 0.0625f : 1.f);
+  const float w1 = (tl & 1) ? 0.f : (x16 ? 16.f : 256.f);
   const uint32_t ssel0 = 0x4440u | static_cast<uint32_t>(tl >> 1);
   const uint32_t ssel1 = 0x4440u | static_cast<uint32_t>(2 + (tl >> 1));
   const uint32_t msel0 = 0x7440u | static_cast<uint32_t>((2 * tl) & 3);
@@ -1062,6 +1155,12 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
         const uint32_t xc8 = smem_u32(smem + L.off_xs + (xsl * 8 + g) * p.xpitch) + 256 * sb + 8 * t;
         const uint32_t sxb = smem_u32(smem + L.off_sxs) + 4 * (xsl * (p.K / 32) + 8 * sb);
         unit_q4k_i8(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, ssel0, ssel1, msel0, msel1, acc);
+      } else if (ENG && WT == WT_Q6K) {
+        const uint32_t xc8 = smem_u32(smem + L.off_xs + (xsl * 8 + g) * p.xpitch) + 256 * sb;
+        const uint32_t sxb = smem_u32(smem + L.off_sxs) + 4 * (xsl * (p.K / 16) + 16 * sb);
+        const bool a4 = __shfl_sync(0xffffffffu, ((reinterpret_cast<uintptr_t>(rg) + i * UB) & 3u) == 0u, 0);
+        if (a4) unit_q6k_i8<true>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
+        else unit_q6k_i8<false>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
       } else if (WT == WT_Q4K) {
         const uint32_t sxcol = smem_u32(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
         unit_q4k(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcol), sxcol, sb, t, acc);
@@ -1212,8 +1311,13 @@ static int gemv_upc(int wt) { return wt == WT_Q4K ? 2 : wt == WT_Q6K ? 2 : wt ==
 int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t stream, bool pdl, int min_smem) {
   if (p.K % 256 != 0 || p.K <= 0 || p.N <= 0 || p.M <= 0 || ((xt == XT_F32) ? 2 * p.M : p.M) > 8)
     return set_error(-1, "gemv: bad shape");
-  // the integer dot engine for Q4_K rows and one token (the decode GEMV); the f16 engine otherwise
-  const bool engi = (wt == WT_Q4K && p.M == 1 && (epi == EPI_STORE || xt == XT_BF16));
+  // the integer dot engine for Q4_K and Q6_K rows and one token (the decode GEMV); the f16 engine
+  // otherwise
+  // (Q6_K: only with tiled copies, where every row of a slot starts at the same offset)
+  const bool tiled_rows = (p.row_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(p.w0) % 16 == 0) &&
+                          (!p.w1 || reinterpret_cast<uintptr_t>(p.w1) % 16 == 0) &&
+                          ((p.n_experts > 0 ? p.n_experts : p.n_groups) <= 1 || p.expert_stride % 16 == 0);
+  const bool engi = (wt == WT_Q4K || (wt == WT_Q6K && tiled_rows)) && p.M == 1 && (epi == EPI_STORE || xt == XT_BF16);
   const int ncols = engi ? 8 : ((xt == XT_F32) ? 2 * p.M : p.M);
   if (epi == EPI_SWIGLU && xt != XT_BF16) return set_error(-1, "gemv: swiglu needs bf16 activations");
   if ((reinterpret_cast<uintptr_t>(p.x) & 15u) != 0) return set_error(-1, "gemv: activations must be 16-byte aligned");
@@ -1295,10 +1399,15 @@ int gemv_launch(int wt, int xt, int epi, GemvParams p, int num_sms, cudaStream_t
   if (!nw) return set_error(-1, "gemv: activation block too large for shared memory");
   p.nslots = ns;
   const int smem = std::min(limit, std::max(min_smem, gemv_layout(wt, ncols, p.K, p.xg, nw, ns, p.pitch, p.xpitch, p.cta_mode ? nw : 0).total));
-  if (engi) {
+  if (engi && wt == WT_Q4K) {
     if (xt == XT_F32) return launch_one<WT_Q4K, XT_F32, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
     if (xt == XT_BF16 && epi == EPI_STORE) return launch_one<WT_Q4K, XT_BF16, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
     if (xt == XT_BF16 && epi == EPI_SWIGLU) return launch_one<WT_Q4K, XT_BF16, EPI_SWIGLU, 1>(p, grid, nw, smem, stream, pdl);
+  }
+  if (engi && wt == WT_Q6K) {
+    if (xt == XT_F32) return launch_one<WT_Q6K, XT_F32, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
+    if (xt == XT_BF16 && epi == EPI_STORE) return launch_one<WT_Q6K, XT_BF16, EPI_STORE, 1>(p, grid, nw, smem, stream, pdl);
+    if (xt == XT_BF16 && epi == EPI_SWIGLU) return launch_one<WT_Q6K, XT_BF16, EPI_SWIGLU, 1>(p, grid, nw, smem, stream, pdl);
   }
 #define AIPU_GEMV_CASE(W, X, E)                                              \
   if (wt == W && xt == X && epi == E) return launch_one<W, X, E>(p, grid, nw, smem, stream, pdl);
