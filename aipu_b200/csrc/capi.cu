@@ -1207,15 +1207,15 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
     if ((rc = set_cuda_error(cudaEventRecord(c->ev_join, c->side), "eventRecord"))) return rc;
   }
   // 3. dispatch
-  if ((rc = ep_bump_launch(e->p, s))) return rc;
   if ((rc = ep_dispatch_launch(e->p, static_cast<const uint16_t*>(x), sel, static_cast<int>(M), s))) return rc;
   // 4. every rank's tokens: local experts
-  if ((rc = ep_wait_launch(e->p, 0, s))) return rc;
   const uint8_t* inbox = static_cast<const uint8_t*>(e->buf);
   const int32_t* in_sel = reinterpret_cast<const int32_t*>(inbox + e->p.off_in_sel);
   const uint16_t* in_x = reinterpret_cast<const uint16_t*>(inbox + e->p.off_in_x);
+  // the union kernel waits for every rank's tokens (dispatch flags) before reading the inbox
+  const EpSync wait_in = ep_sync(e->p, 0, false);
   if ((rc = union_launch(in_sel, static_cast<int>(Gtok), T, static_cast<int>(expert_lo), static_cast<int>(El),
-                         sc.union_ids, sc.n_union, sc.slot_map, s)))
+                         sc.union_ids, sc.n_union, sc.slot_map, s, &wait_in)))
     return rc;
   const int Umax = static_cast<int>(std::min<int64_t>(El, Gtok * T));
   if ((rc = swiglu_groups(c, c->ws[0], W->gate_wtype, W->gate_w, W->up_w, W->down_wtype, W->down_w, H, F,
@@ -1224,12 +1224,12 @@ extern "C" int aipu_ep_moe_layer(aipu_ep* e, const aipu_moe_weights* W, int64_t 
     return rc;
   // 5. per-slot outputs into the owners' outboxes
   if ((rc = ep_return_launch(e->p, sc.slot_map, sc.y, static_cast<int>(M), static_cast<int>(Gtok), s))) return rc;
-  if ((rc = ep_wait_launch(e->p, 1, s))) return rc;
   if (shared && (rc = set_cuda_error(cudaStreamWaitEvent(s, c->ev_join, 0), "streamWaitEvent"))) return rc;
-  // 6. slot-order combine of this rank's tokens
+  // 6. slot-order combine of this rank's tokens: waits for every rank's returned pieces (return flags)
+  // and ends the layer call (advances the sequence number)
   return combine_pieces_launch(sel, sel_w, static_cast<int>(M), T, H, static_cast<int>(El),
                                reinterpret_cast<const uint16_t*>(inbox + e->p.off_out), shared ? y_sh : nullptr,
-                               static_cast<uint16_t*>(y), s);
+                               static_cast<uint16_t*>(y), s, ep_sync(e->p, 1, true));
 }
 
 extern "C" int aipu_swiglu_expert(aipu_ctx* c, int gwt, const void* gw, int uwt, const void* uw, int dwt,

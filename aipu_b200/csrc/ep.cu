@@ -5,37 +5,27 @@
 //   in_sel  [G][M][T]       selections of every rank's tokens (M = this call's tokens per rank, the
 //   in_x    [G][M][H]       bf16 tokens of every rank          same on every rank, <= capacity)
 //   out     [G][M][T][H]    bf16 per-slot expert outputs for this rank's tokens, one piece per rank
-// A layer call bumps a device-side sequence number; writers store data with plain peer stores,
-// make them visible system-wide, then release the flag (st.release.sys); readers acquire the flags
-// with a bounded spin (no wait can run forever: on expiry the status word is set and the kernel
-// returns). No TMA and no multicast touches peer memory; only plain loads and stores.
+// A layer call runs with the sequence number *seq + 1 (the device counter holds the last completed
+// call; the combine kernel advances it at the end); writers store data with plain peer stores, make
+// them visible system-wide, then release the flag (st.release.sys); the consuming kernels (union,
+// combine) acquire the flags with a bounded spin before reading (no wait can run forever: on expiry
+// the status word is set and the kernel skips the exchanged data). No TMA and no multicast touches peer memory; only plain loads and stores.
 #include <algorithm>
 #include <cstdio>
 
 #include "common.cuh"
+#include "ep_sync.cuh"
 #include "kernels.h"
 #include "launch.h"
 
 namespace aipu {
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// seq += 1 (one thread); every later kernel of the layer reads it
-__global__ void ep_bump_kernel(uint32_t* seq) { *seq += 1u; }
 
 // CTA q: copy this rank's M tokens and selections into peer q's inbox slot `rank`, then release
 // peer q's dispatch flag[rank] = seq.
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpParams p, const uint16_t* __restrict__ x,
                                                           const int32_t* __restrict__ sel, int M) {
   const int q = blockIdx.x;
-  const uint32_t seq = *p.seq;
+  const uint32_t seq = *p.seq + 1u;
   uint8_t* peer = p.peers[q];
   uint16_t* dx = reinterpret_cast<uint16_t*>(peer + p.off_in_x) + static_cast<int64_t>(p.rank) * M * p.H;
   int32_t* ds = reinterpret_cast<int32_t*>(peer + p.off_in_sel) + static_cast<int64_t>(p.rank) * M * p.T;
@@ -48,25 +38,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpParams p, cons
   if (threadIdx.x == 0) st_release_sys(reinterpret_cast<uint32_t*>(peer + p.off_flags) + p.rank, seq);
 }
 
-// Wait until flags[which][0..G) of this rank's buffer reach seq (bounded).
-__global__ void ep_wait_kernel(const EpParams p, int which) {
-  const int q = threadIdx.x;
-  if (q >= p.G) return;
-  const uint32_t seq = *p.seq;
-  const uint32_t* f = reinterpret_cast<const uint32_t*>(p.peers[p.rank] + p.off_flags) + which * p.G + q;
-  const long long limit = wait_limit(p.status);
-  const long long t0 = clock64();
-  while (static_cast<int32_t>(ld_acquire_sys(f) - seq) < 0) {
-    if (clock64() - t0 > limit) {
-      atomicOr(p.status, ST_TIMEOUT_FULL);
-      return;
-    }
-  }
-}
-
 // Return: for gathered token t (owner q = t / M, local row m = t % M), every slot s
 // whose expert is local (index >= 0 into the union rows `rows` [U][Gtok][H]) is stored into peer q's
-// out[rank][m][s]. Then each CTA makes its stores visible; ep_release_kernel sets the flags.
+// out[rank][m][s]. Each CTA makes its stores visible system-wide; the last CTA to arrive releases the
+// return flags of every peer.
 __global__ void __launch_bounds__(256) ep_return_kernel(const EpParams p, const int32_t* __restrict__ slot_map,
                                                         const uint16_t* __restrict__ rows, int M, int Gtok) {
   const int64_t hv = p.H / 8;
@@ -84,37 +59,36 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpParams p, const 
     reinterpret_cast<uint4*>(dst)[v] = val;
   }
   __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.seq + 1, 1u) == gridDim.x - 1) {
+    p.seq[1] = 0u;
+    __threadfence_system();
+    const uint32_t seq = *p.seq + 1u;
+    for (int q = 0; q < p.G; ++q)
+      st_release_sys(reinterpret_cast<uint32_t*>(p.peers[q] + p.off_flags) + p.G + p.rank, seq);
+  }
 }
 
-__global__ void ep_release_kernel(const EpParams p, int which) {
-  const int q = threadIdx.x;
-  if (q >= p.G) return;
-  __threadfence_system();
-  st_release_sys(reinterpret_cast<uint32_t*>(p.peers[q] + p.off_flags) + which * p.G + p.rank, *p.seq);
-}
-
-int ep_bump_launch(const EpParams& p, cudaStream_t s) {
-  ep_bump_kernel<<<1, 1, 0, s>>>(p.seq);
-  return set_cuda_error(cudaGetLastError(), "ep_bump_kernel");
+EpSync ep_sync(const EpParams& p, int which, bool bump) {
+  EpSync w;
+  w.flags = reinterpret_cast<const uint32_t*>(p.peers[p.rank] + p.off_flags) + which * p.G;
+  w.n = p.G;
+  w.seq = p.seq;
+  w.status = p.status;
+  w.bump_arrive = bump ? p.seq + 2 : nullptr;
+  return w;
 }
 int ep_dispatch_launch(const EpParams& p, const uint16_t* x, const int32_t* sel, int M, cudaStream_t s) {
   if (p.H % 8) return set_error(EINVAL_, "ep: H % 8 != 0");
   ep_dispatch_kernel<<<p.G, 256, 0, s>>>(p, x, sel, M);
   return set_cuda_error(cudaGetLastError(), "ep_dispatch_kernel");
 }
-int ep_wait_launch(const EpParams& p, int which, cudaStream_t s) {
-  ep_wait_kernel<<<1, 32, 0, s>>>(p, which);
-  return set_cuda_error(cudaGetLastError(), "ep_wait_kernel");
-}
 int ep_return_launch(const EpParams& p, const int32_t* slot_map, const uint16_t* rows, int M, int Gtok,
                      cudaStream_t s) {
   const int64_t total = static_cast<int64_t>(Gtok) * p.T * (p.H / 8);
   const int blocks = static_cast<int>(std::min<int64_t>(std::max<int64_t>((total + 255) / 256, 1), 1024));
   ep_return_kernel<<<blocks, 256, 0, s>>>(p, slot_map, rows, M, Gtok);
-  int rc = set_cuda_error(cudaGetLastError(), "ep_return_kernel");
-  if (rc) return rc;
-  ep_release_kernel<<<1, 32, 0, s>>>(p, 1);
-  return set_cuda_error(cudaGetLastError(), "ep_release_kernel");
+  return set_cuda_error(cudaGetLastError(), "ep_return_kernel");
 }
 
 }  // namespace aipu

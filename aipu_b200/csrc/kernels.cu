@@ -7,6 +7,7 @@
 #include "act.cuh"
 #include "deq.cuh"
 #include "kernels.h"
+#include "ep_sync.cuh"
 #include "launch.h"
 
 namespace aipu {
@@ -927,10 +928,14 @@ int perm_launch(const PermParams& p, cudaStream_t s) {
 // map every slot to its union index (-1: expert not local).
 __global__ void __launch_bounds__(1024) union_kernel(const int32_t* __restrict__ sel, int M, int topk, int expert_lo,
                                                      int E, int32_t* __restrict__ union_ids,
-                                                     int32_t* __restrict__ n_union, int32_t* __restrict__ slot_map) {
+                                                     int32_t* __restrict__ n_union, int32_t* __restrict__ slot_map,
+                                                     const EpSync w) {
   __shared__ int flag[1024];
   __shared__ int idx[1024];
   const int tid = threadIdx.x;
+  // peer exchange: the selections arrive from the other ranks (a wait that gave up leaves the union
+  // empty, and the status word reports it)
+  if (w.flags && !ep_sync_wait(w)) M = 0;
   for (int e = tid; e < E; e += 1024) flag[e] = 0;
   __syncthreads();
   for (int i = tid; i < M * topk; i += 1024) {
@@ -954,9 +959,9 @@ __global__ void __launch_bounds__(1024) union_kernel(const int32_t* __restrict__
 }
 
 int union_launch(const int32_t* sel, int M, int topk, int expert_lo, int E, int32_t* union_ids, int32_t* n_union,
-                 int32_t* slot_map, cudaStream_t s) {
+                 int32_t* slot_map, cudaStream_t s, const EpSync* w) {
   if (E <= 0 || E > 1024) return set_error(EINVAL_, "union: E must be 1..1024");
-  union_kernel<<<1, 1024, 0, s>>>(sel, M, topk, expert_lo, E, union_ids, n_union, slot_map);
+  union_kernel<<<1, 1024, 0, s>>>(sel, M, topk, expert_lo, E, union_ids, n_union, slot_map, w ? *w : EpSync());
   return set_cuda_error(cudaGetLastError(), "union_kernel");
 }
 
@@ -989,9 +994,12 @@ int gather_slots_launch(const int32_t* index, int M, int topk, int64_t H, const 
 
 __global__ void combine_pieces_kernel(const int32_t* __restrict__ sel, const uint16_t* __restrict__ sel_w, int M,
                                       int topk, int64_t H, int epp, const uint16_t* __restrict__ pieces,
-                                      const uint16_t* __restrict__ shared, uint16_t* __restrict__ out) {
+                                      const uint16_t* __restrict__ shared, uint16_t* __restrict__ out,
+                                      const EpSync w) {
   const int64_t hv = H / 8;
-  const int64_t total = static_cast<int64_t>(M) * hv;
+  // peer exchange: the pieces arrive from the other ranks (a wait that gave up skips the combine; the
+  // status word reports it)
+  const int64_t total = (w.flags && !ep_sync_wait(w)) ? 0 : static_cast<int64_t>(M) * hv;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int m = static_cast<int>(i / hv);
@@ -1027,15 +1035,19 @@ __global__ void combine_pieces_kernel(const int32_t* __restrict__ sel, const uin
     o.w = bf16_rne_bits(facc[6]) | (static_cast<uint32_t>(bf16_rne_bits(facc[7])) << 16);
     reinterpret_cast<uint4*>(out + static_cast<int64_t>(m) * H)[v] = o;
   }
+  ep_sync_bump(w);
 }
 
 int combine_pieces_launch(const int32_t* sel, const uint16_t* sel_w, int M, int topk, int64_t H, int epp,
-                          const uint16_t* pieces, const uint16_t* shared, uint16_t* out, cudaStream_t s) {
+                          const uint16_t* pieces, const uint16_t* shared, uint16_t* out, cudaStream_t s, EpSync w) {
   if (H % 8 || epp <= 0) return set_error(EINVAL_, "combine_pieces: bad arguments");
   const int64_t total = static_cast<int64_t>(M) * (H / 8);
   int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
-  if (blocks <= 0) return OK;
-  combine_pieces_kernel<<<blocks, 256, 0, s>>>(sel, sel_w, M, topk, H, epp, pieces, shared, out);
+  if (blocks <= 0) {
+    if (!w.bump_arrive) return OK;
+    blocks = 1;  // the layer call still ends here
+  }
+  combine_pieces_kernel<<<blocks, 256, 0, s>>>(sel, sel_w, M, topk, H, epp, pieces, shared, out, w);
   return set_cuda_error(cudaGetLastError(), "combine_pieces_kernel");
 }
 

@@ -61,8 +61,9 @@ int perm_launch(const PermParams& p, cudaStream_t s);
 
 // Union of the local experts selected by M tokens (sorted) and the index of each (token, slot) in
 // it, -1 when the slot's expert is not local (global id - expert_lo outside [0, E)).
+struct EpSync;
 int union_launch(const int32_t* sel, int M, int topk, int expert_lo, int E, int32_t* union_ids, int32_t* n_union,
-                 int32_t* slot_map, cudaStream_t s);
+                 int32_t* slot_map, cudaStream_t s, const EpSync* w = nullptr);
 // y_slots[m, s, :] = rows[index[m * topk + s]] (bf16 rows of H) for index >= 0; row index
 // r_of(i) = index * row_mul + m * row_add (decode: union-major [U, M, H] rows: row_mul = M, row_add = 1)
 int gather_slots_launch(const int32_t* index, int M, int topk, int64_t H, const uint16_t* rows, int64_t row_mul,
@@ -75,17 +76,28 @@ struct EpParams {
   int G, rank, Mmax, H, T;
   uint8_t* peers[EP_MAX_RANKS];  // every rank's symmetric buffer (this rank's own included)
   int64_t off_flags, off_in_sel, off_in_x, off_out;
-  uint32_t* seq;                 // device sequence number of the current layer call (local)
+  uint32_t* seq;                 // device sequence number of the last completed layer call (local);
+                                 // seq[1], seq[2]: arrival counters of the return and combine kernels
   int* status;
 };
-int ep_bump_launch(const EpParams& p, cudaStream_t s);
+// Arrival wait folded into a consuming kernel (peer exchange): before reading, the kernel waits
+// (bounded) until flags[0..n) reach *seq + 1, the current layer call's sequence number. bump_arrive
+// (nullable): the kernel's CTAs count their exits there, and the last one advances *seq, ending the
+// layer call (every CTA read *seq before).
+struct EpSync {
+  const uint32_t* flags = nullptr;
+  int n = 0;
+  uint32_t* seq = nullptr;
+  int* status = nullptr;
+  uint32_t* bump_arrive = nullptr;
+};
 int ep_dispatch_launch(const EpParams& p, const uint16_t* x, const int32_t* sel, int M, cudaStream_t s);
-int ep_wait_launch(const EpParams& p, int which, cudaStream_t s);
 int ep_return_launch(const EpParams& p, const int32_t* slot_map, const uint16_t* rows, int M, int Gtok,
                      cudaStream_t s);
+EpSync ep_sync(const EpParams& p, int which, bool bump);
 int combine_pieces_launch(const int32_t* sel, const uint16_t* sel_w, int M, int topk, int64_t H,
                           int experts_per_piece, const uint16_t* pieces, const uint16_t* shared, uint16_t* out,
-                          cudaStream_t s);
+                          cudaStream_t s, EpSync w = EpSync());
 // upper bound of the positions perm_kernel uses
 inline int64_t perm_max_positions(int64_t T, int topk, int E, int with_shared) {
   return T * topk + (with_shared ? T : 0) + 8 * static_cast<int64_t>(E + 1);
