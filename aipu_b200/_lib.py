@@ -19,6 +19,7 @@ MODE_FAST, MODE_STRICT = 0, 1
 FLAG_PDL = 1
 FLAG_STRICT = 2
 FLAG_TC_DECODE = 4
+FLAG_FAST_DOWN = 8
 
 c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 

@@ -477,6 +477,33 @@ static int swiglu_groups(aipu_ctx* c, Workspace& ws, int gwt, const void* gw, co
     g.y_group_stride = M * F;
     g.status = c->status;
     int rc = chain_launch(gwt, CHAIN_SWIGLU, g, num_sms, s, pdl);
+    if (rc == OK && (c->flags & AIPU_FLAG_FAST_DOWN)) {
+      // h bit-exact from the chains; the down projection on the GEMV (1-ulp bar). Rows of tokens that
+      // did not select an expert are computed from unwritten h and never read by the combine.
+      for (int64_t m0 = 0; m0 < M; m0 += 8) {
+        GemvParams q = {};
+        q.w0 = static_cast<const uint8_t*>(dw);
+        q.row_bytes = row_bytes_of(dwt, F);
+        q.expert_stride = dstride;
+        q.group_ids = group_ids;
+        q.n_experts = n_experts;
+        q.n_groups_dev = n_groups_dev;
+        q.n_groups = n_groups;
+        q.N = static_cast<int>(H);
+        q.K = static_cast<int>(F);
+        q.x = h + m0 * F;
+        q.x_group_stride = M * F;
+        q.M = static_cast<int>(std::min<int64_t>(8, M - m0));
+        q.y = y + m0 * H;
+        q.y_group_stride = M * H;
+        q.partials = ws.partials;
+        q.counters = ws.counters;
+        q.status = c->status;
+        rc = gemv_launch(dwt, XT_BF16, EPI_STORE, q, num_sms, s, pdl, min_smem);
+        if (rc) return rc;
+      }
+      return OK;
+    }
     if (rc == OK) {
       ChainParams d = g;
       d.w0 = static_cast<const uint8_t*>(dw);

@@ -63,14 +63,16 @@ class Context:
         except Exception:
             pass
 
-    def set_flags(self, pdl: bool = False, strict: bool = False, tc_decode: bool = False) -> "Context":
+    def set_flags(self, pdl: bool = False, strict: bool = False, tc_decode: bool = False,
+                  fast_down: bool = False) -> "Context":
         """pdl=True: fast GEMMs start streaming weights while the previous kernel drains (only when no
         kernel right before a GEMM writes its weights). strict=True: every MoE path (the many-token
         one included) is bit-exact (the reference's sequential fp32 chains). The decode MoE path is
         bit-exact by default (chain kernel); tc_decode=True runs it on the tensor-core GEMV instead
-        (each GEMM within 1 bf16 ulp, the layer not bit-exact)."""
+        (each GEMM within 1 bf16 ulp, the layer not bit-exact); fast_down=True keeps the exact chains
+        for gate/up (h bit-exact) and runs only the down projection on the GEMV (1-ulp bar)."""
         flags = ((L.FLAG_PDL if pdl else 0) | (L.FLAG_STRICT if strict else 0)
-                 | (L.FLAG_TC_DECODE if tc_decode else 0))
+                 | (L.FLAG_TC_DECODE if tc_decode else 0) | (L.FLAG_FAST_DOWN if fast_down else 0))
         check(lib().aipu_ctx_set_flags(self.handle, flags))
         return self
 

@@ -79,6 +79,34 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def q6k_grouped(F, ops, ctx, s, timed, hbm_peak, rank0, L=64, N=6144, K=2048):
+    """The Q6_K decode GEMV (MoE down-projection shape 6144 x 2048, bf16 x, M = 1) as one grouped
+    launch over L distinct seeded matrices (0.66 GB > L2), with the parity of matrix 0 against the
+    oracle (checker use, rank 0)."""
+    import numpy as np
+    import torch
+
+    d = torch.device("cuda", torch.cuda.current_device())
+    w = F.random_rows_dev(F.Q6_K, L * N, K, seed=21, device=d)
+    x = torch.randn((1, K), device=d, generator=torch.Generator(device=d).manual_seed(22)).to(torch.bfloat16)
+    y = torch.empty((L, 1, N), dtype=torch.bfloat16, device=d)
+    g = _graph(lambda: ops.gemm_grouped(F.Q6_K, w, L, N, K, x, ctx=ctx, out=y), s)
+    t = timed(g, 20, 3)
+    byts = L * (N * (K // 256) * 210 + K * 2 + N * 2)
+    out = {"matrices": L, "shape": f"{N}x{K}", "us_per_launch": round(t * 1e6, 2), "gbs": round(byts / t / 1e9, 1),
+           "frac": round(byts / t / 1e9 / hbm_peak, 4),
+           "kernel": "aipu_kq_gemv_kernel<Q6_K, bf16 x, store> (integer dot engine)"}
+    if rank0:
+        from oracle import q4k_oracle as qo
+
+        ref = qo.gemm(F.Q6_K, w[:N].cpu().numpy(), N, K, x.float().cpu().numpy())
+        got = _bf16_np(y[0])
+        st = qo.parity_stats(got, ref)
+        out["parity"] = {k: (round(v, 6) if isinstance(v, float) else v) for k, v in st.items()}
+    del g, w
+    return out
+
+
 def c1_inputs(L):
     """BASELINE config 1 inputs, identical in both arms: x = numpy default_rng(0) N(0,1) fp32 [1, 4096];
     matrix l = formats.random_rows_np(Q4_K, 4096, 4096, seed=1000 + l)."""
@@ -356,7 +384,7 @@ def moe_bench(check=True):
     hbm, tf_peak, kind = peaks()
     expert_bytes = 2 * Fd * (H // 256) * 144 + H * (Fd // 256) * 210
     out = {}
-    paths = {"exact": {}, "tensor_core": {"tc_decode": True}}
+    paths = {"exact": {}, "exact_gateup_fast_down": {"fast_down": True}, "tensor_core": {"tc_decode": True}}
     for M in (1, 4):
         x = (torch.randn((M, H), device=d, generator=torch.Generator(device=d).manual_seed(100 + M))).to(torch.bfloat16)
         y = torch.empty((M, H), dtype=torch.bfloat16, device=d)
@@ -782,6 +810,7 @@ def main():
               "frac": round(L * C1_BYTES / step_single / 1e9 / hbm_peak, 4),
               "note": "one kernel launch per 4096x4096 matrix, CUDA graph, programmatic dependent launch"}
     del gs
+    q6k = q6k_grouped(F, ops, ctx, s, timed, hbm_peak, rank0=(int(os.environ.get("RANK", "0")) == 0))
 
     # ---- end to end through the public API with host buffers (x in, all y out, every step)
     x_host = torch.from_numpy(x_np).pin_memory()
@@ -854,6 +883,7 @@ def main():
                          "us_per_launch": round(step * 1e6, 3),
                          "algorithmic_bytes_per_launch": L * C1_BYTES},
             "single_launch": single,
+            "q6k_grouped": q6k,
             "cpu_baseline": cpu_base, "e2e": e2e, "gpu_launches": args.steps,
             "clocks": clk.summary(), "moe": moe, "moe_decode_ep": moe_ep, "moe_prefill_ep": moe_pre_ep,
             "moe_decode_stream": moe_stream,

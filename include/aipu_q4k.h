@@ -75,6 +75,11 @@ int aipu_ctx_destroy(aipu_ctx* ctx);
  * aipu_moe_experts, aipu_swiglu_expert, aipu_ep_moe_layer) on the tensor-core GEMV (each GEMM within
  * 1 bf16 ulp, the layer not bit-exact) instead of the default bit-exact chain kernel. */
 #define AIPU_FLAG_TC_DECODE 4
+/* AIPU_FLAG_FAST_DOWN: on the default decode path, keep the bit-exact chains for gate/up (so the
+ * SwiGLU product h equals the reference's bit for bit) and run the down projection on the integer-
+ * engine GEMV (within 1 bf16 ulp of the sequential sum; the layer output is not bit-exact). Ignored
+ * with AIPU_FLAG_TC_DECODE. */
+#define AIPU_FLAG_FAST_DOWN 8
 int aipu_ctx_set_flags(aipu_ctx* ctx, int flags);
 /* device status word of the context (0 = no bounded wait ever gave up); resets it to 0. Bit 1: a
  * wait for data gave up, bit 2: a wait for a free buffer gave up, bit 4: bad arguments seen on the

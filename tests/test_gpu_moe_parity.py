@@ -94,6 +94,21 @@ def test_moe_decode_config3_bit_exact(layer, M):
     assert np.array_equal(_bf16_np(y).view(np.uint32), y_ref.view(np.uint32)), st
 
 
+@pytest.mark.parametrize("M", [1, 4, 5])
+def test_fast_down_decode_config3_meets_bar(layer, M):
+    """AIPU_FLAG_FAST_DOWN: exact chains for gate/up (h bit-exact), the down projection on the integer
+    GEMV: routing exact, outputs >= 99.9 % within 1 bf16 ulp and max_rel <= 1e-2 (the GEMM bar)."""
+    d = _dev()
+    W = layer[0]
+    x = qo.bf16_round(np.random.default_rng(720 + M).standard_normal((M, H)).astype(F32))
+    ctx = ops.Context(d).set_flags(fast_down=True)
+    y, sel, sw = ops.moe_layer(W, _bf16_dev(x, d), ctx=ctx, return_routing=True)
+    torch.cuda.synchronize()
+    st, _ = _check(_bf16_np(y), sel.cpu().numpy(), _bf16_np(sw), x, layer, f"fast-down decode C3 M={M}")
+    assert st["frac_within_1ulp"] >= 0.999 and st["max_rel"] <= 1e-2, st
+    ctx.close()
+
+
 def test_tc_decode_config3_distribution(layer):
     """The tensor-core GEMV decode path (AIPU_FLAG_TC_DECODE): routing exact, outputs within the
     reference's own SwiGLU tolerance (tools/swiglu_q4k_gen.py:91-95); not held to the 1-ulp bar."""
