@@ -222,7 +222,7 @@ int aipu_ctx_destroy(aipu_ctx* c) {
 }
 
 int aipu_ctx_set_flags(aipu_ctx* c, int flags) {
-  if (!c || (flags & ~(AIPU_FLAG_PDL | AIPU_FLAG_STRICT | AIPU_FLAG_TC_DECODE))) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
+  if (!c || (flags & ~(AIPU_FLAG_PDL | AIPU_FLAG_STRICT | AIPU_FLAG_TC_DECODE | AIPU_FLAG_FAST_DOWN))) return set_error(EINVAL_, "ctx_set_flags: bad arguments");
   c->flags = flags;
   return OK;
 }
