@@ -305,10 +305,10 @@ __device__ void router_union(const RouterParams& p, const int* sel_s) {
 // activation slices by bulk copies) into a shared-memory ring, so the chains never wait on DRAM
 // latency. GGUF-row routers dequantise each weight exactly in the chain.
 constexpr int RT_CHUNK = 128;   // k rows per stage
-// EG = 64 (many tokens): each chain lane carries two experts (2 lane, 2 lane + 1) as one packed f32x2
-// chain: fl(acc + fl(x * w)) per lane of the pair with one product and one add instruction for both.
-// The product is fma(x, w, -0) with -0 read from the parameters (exactly fl(x * w), signed zeros
-// included), so the assembler cannot contract it with the following add.
+// Packed f32x2 chain step (router_many_kernel: two experts per lane): fl(acc + fl(x * w)) per lane of
+// the pair with one product and one add instruction for both. The product is fma(x, w, -0) with -0
+// read from the parameters (exactly fl(x * w), signed zeros included), so the assembler cannot
+// contract it with the following add.
 __device__ __forceinline__ unsigned long long rt_pk(float2 a) {
   unsigned long long r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
@@ -335,8 +335,7 @@ constexpr int RT_XBYTES = RT_MB * RT_CHUNK * 2;
 template <int EG>
 struct RtCfg {
   static constexpr bool SPLIT = (EG == 8);
-  static constexpr bool PAIR = (EG == 64);   // two experts per chain lane
-  static constexpr int NST = SPLIT ? 8 : (PAIR ? 3 : 6);  // input ring depth (PAIR: two CTAs per SM)
+  static constexpr int NST = SPLIT ? 8 : 6;  // input ring depth
   static constexpr int WBYTES = RT_CHUNK * EG * 4;
   static constexpr int NWARP = SPLIT ? 2 * RT_MB + 1 : RT_MB + 1;
   static constexpr int PSTR = 132;            // floats per expert row of a product slot (padded)
@@ -365,7 +364,7 @@ extern "C" int aipu_debug_rt_gt(unsigned long long* out) {
 }
 #endif
 template <int RT_EG>
-__global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP, RtCfg<RT_EG>::PAIR ? 2 : 1) router_strict_kernel(const __grid_constant__ RouterParams p) {
+__global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP) router_strict_kernel(const __grid_constant__ RouterParams p) {
   using RC = RtCfg<RT_EG>;
   constexpr int RT_NST = RC::NST;
   constexpr int RT_WBYTES = RC::WBYTES;
@@ -378,10 +377,8 @@ __global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP, RtCfg<RT_EG>::PAIR ?
   uint8_t* ring = smem + RC::OFF_RING;  // barriers first; TMA destinations 128-byte aligned
   __shared__ int last_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // lane's expert(s): e (and e + 1 when two experts per lane)
-  const int e0 = blockIdx.x * RT_EG, e = RC::PAIR ? e0 + 2 * lane : e0 + lane;
-  const bool live = (RC::PAIR || lane < RT_EG) && (e < p.E);
-  const bool live1 = RC::PAIR && (e + 1 < p.E);
+  const int e0 = blockIdx.x * RT_EG, e = e0 + lane;
+  const bool live = (lane < RT_EG) && (e < p.E);
   const int m0 = blockIdx.y * RT_MB;
   const int mb = min(RT_MB, p.M - m0);
   // SPLIT: product slots per token (the RT_MB * NPS slots shared by the block's tokens, at most 16
@@ -507,66 +504,8 @@ __global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP, RtCfg<RT_EG>::PAIR ?
   // consumer warp `warp` = token m0 + warp
   const int m = m0 + warp;
   if (warp < mb) {
-    float acc = 0.f, acc1 = 0.f;
-    if (RC::PAIR && dense) {
-      bool ok = true;
-      const float2 nz = make_float2(p.neg_zero, p.neg_zero);
-      float2 a2 = make_float2(0.f, 0.f);
-      for (int c = 0; c < nchunk; ++c) {
-        const int slot = c % RT_NST;
-        const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
-        if (ok) ok = mbar_wait_bounded(&full[slot], (c / RT_NST) & 1, p.status, ST_TIMEOUT_FULL);
-        if (ok) {
-          const uint8_t* st = ring + slot * (RT_WBYTES + RT_XBYTES);
-          // row k of the box: 64 experts, this lane's pair at 8 lane bytes (64-bit loads, conflict-free)
-          const float2* ws = reinterpret_cast<const float2*>(st) + lane;
-          const uint16_t* xs = reinterpret_cast<const uint16_t*>(st + RT_WBYTES + warp * RT_CHUNK * 2);
-          if (kl == RT_CHUNK) {
-            // batches of 16 k: the next batch's operands loaded while this batch's chain runs
-            constexpr int BK = 16;
-            float2 wv[BK];
-            uint4 xv[2];
-#pragma unroll
-            for (int i = 0; i < BK; ++i) wv[i] = ws[i * 32];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) xv[i] = reinterpret_cast<const uint4*>(xs)[i];
-#pragma unroll
-            for (int k0b = 0; k0b < RT_CHUNK; k0b += BK) {
-              float2 wc[BK];
-              float xc[BK];
-#pragma unroll
-              for (int i = 0; i < BK; ++i) wc[i] = wv[i];
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const uint32_t xw[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  xc[8 * i + 2 * h] = __uint_as_float(xw[h] << 16);
-                  xc[8 * i + 2 * h + 1] = __uint_as_float(xw[h] & 0xFFFF0000u);
-                }
-              }
-              if (k0b + BK < RT_CHUNK) {
-#pragma unroll
-                for (int i = 0; i < BK; ++i) wv[i] = ws[(k0b + BK + i) * 32];
-#pragma unroll
-                for (int i = 0; i < 2; ++i) xv[i] = reinterpret_cast<const uint4*>(xs + k0b + BK)[i];
-              }
-#pragma unroll
-              for (int i = 0; i < BK; ++i) a2 = rt_step2(a2, make_float2(xc[i], xc[i]), wc[i], nz);
-            }
-          } else {
-            for (int k = 0; k < kl; ++k) {
-              const float xk = bf16_bits_to_f32(xs[k]);
-              a2 = rt_step2(a2, make_float2(xk, xk), ws[k * 32], nz);
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-      }
-      acc = a2.x;
-      acc1 = a2.y;
-    } else if (RC::SPLIT && dense) {
+    float acc = 0.f;
+    if (RC::SPLIT && dense) {
       // the chain over the products, in k order; 32 of them loaded ahead of the adds
       bool ok = true;
       uint32_t ready_seen = 0u;
@@ -683,11 +622,6 @@ __global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP, RtCfg<RT_EG>::PAIR ?
       p.gate[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(glm_sigmoid_bf(logit));
       if (p.logits) p.logits[static_cast<int64_t>(m) * E + e] = bf16_rne_bits(logit);
     }
-    if (live1) {
-      const float logit = bf16_round_f(acc1);
-      p.gate[static_cast<int64_t>(m) * E + e + 1] = bf16_rne_bits(glm_sigmoid_bf(logit));
-      if (p.logits) p.logits[static_cast<int64_t>(m) * E + e + 1] = bf16_rne_bits(logit);
-    }
   }
 #ifdef RT_GT
   if (threadIdx.x == 0) atomicMax(&g_rt_gt[1], rt_gtime());
@@ -720,6 +654,209 @@ __global__ void __launch_bounds__(32 * RtCfg<RT_EG>::NWARP, RtCfg<RT_EG>::PAIR ?
 #ifdef RT_GT
     if (lane == 0) atomicMax(&g_rt_gt[3], rt_gtime());
 #endif
+  }
+}
+
+// ------------------------------------------------------------------ router, many tokens (dense fp32)
+// One CTA = 64 experts x 56 tokens. A producer warp streams 128 k x 64 expert boxes of W (tiled TMA)
+// and the tokens' matching activation slices (bulk copies) into a 3-stage ring; each of the 7
+// compute warps runs the chains of 8 tokens, every lane two experts as packed f32x2 chains
+// (fl(acc + fl(x w)) per lane of the pair, k in order). A weight pair loaded once serves 8 tokens from
+// registers, so the loop costs about 1.2 instructions per (token, expert-pair, k) step.
+// (7 warps x 8 tokens: 2048 tokens x 256 experts make 37 x 4 = 148 CTAs, one per SM)
+constexpr int RM_WARPS = 7, RM_TOK = 8 * RM_WARPS, RM_EG = 64, RM_NST = 3;
+constexpr int RM_WB = RT_CHUNK * RM_EG * 4;   // 32 KB of W per stage
+constexpr int RM_XB = RM_TOK * RT_CHUNK * 2;  // 16 KB of activations per stage
+constexpr int RM_OFF_RING = 1024;
+constexpr int RM_SMEM = RM_OFF_RING + RM_NST * (RM_WB + RM_XB);
+
+template <int TPW>
+__global__ void __launch_bounds__(32 * (RM_WARPS + 1), 1) router_many_kernel(const __grid_constant__ RouterParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + RM_NST;
+  uint8_t* ring = smem + RM_OFF_RING;
+  __shared__ int last_flag;
+  __shared__ int sel_s[RM_TOK * 16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * RM_EG, e = e0 + 2 * lane;
+  constexpr int tpw = TPW;
+  const int tok_cta = RM_WARPS * tpw;
+  const int m0 = blockIdx.y * tok_cta;
+  const int mb = min(tok_cta, p.M - m0);
+  const int K = p.K, E = p.E;
+  const int nchunk = (K + RT_CHUNK - 1) / RT_CHUNK;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < RM_NST; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], RM_WARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == RM_WARPS) {
+    // producer: the first stages' W boxes before griddepcontrol.wait (static weights), activations after
+    auto issue_w = [&](int c) {
+      const int st = c % RM_NST;
+      const int k0 = c * RT_CHUNK, kl = min(RT_CHUNK, K - k0);
+      const uint32_t xrow = static_cast<uint32_t>((kl * 2 + 15) & ~15);
+      uint8_t* dst = ring + st * (RM_WB + RM_XB);
+      mbar_arrive_expect_tx(&full[st], RM_WB + xrow * mb);
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+              "r"(smem_u32(dst)),
+          "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(e0), "r"(k0), "r"(smem_u32(&full[st]))
+          : "memory");
+    };
+    auto issue_x = [&](int c) {
+      const int st = c % RM_NST;
+      const int k0 = c * RT_CHUNK, kl = min(RT_CHUNK, K - k0);
+      const uint32_t xrow = static_cast<uint32_t>((kl * 2 + 15) & ~15);
+      uint8_t* dst = ring + st * (RM_WB + RM_XB) + RM_WB;
+      for (int t = lane; t < mb; t += 32)
+        bulk_g2s(dst + t * RT_CHUNK * 2, p.x + static_cast<int64_t>(m0 + t) * K + k0, xrow, &full[st]);
+    };
+    const int npre = min(RM_NST, nchunk);
+    if (lane == 0)
+      for (int c = 0; c < npre; ++c) issue_w(c);
+    __syncwarp();
+    pdl_wait();
+    for (int c = 0; c < npre; ++c) issue_x(c);
+    for (int c = npre; c < nchunk; ++c) {
+      const int st = c % RM_NST;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait_bounded(&empty[st], ((c / RM_NST) - 1) & 1, p.status, ST_TIMEOUT_EMPTY);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return;
+      if (lane == 0) issue_w(c);
+      __syncwarp();
+      issue_x(c);
+    }
+    return;
+  }
+  pdl_wait();
+  // compute warp: tokens t0 .. t0 + tpw - 1 of the block (rows past mb compute on the ring's stale
+  // bytes and are never stored)
+  const int t0 = warp * tpw;
+  const float2 nz = make_float2(p.neg_zero, p.neg_zero);
+  float2 acc[TPW];
+#pragma unroll
+  for (int j = 0; j < TPW; ++j) acc[j] = make_float2(0.f, 0.f);
+  bool ok = true;
+  for (int c = 0; c < nchunk && ok; ++c) {
+    const int st = c % RM_NST;
+    const int kl = min(RT_CHUNK, K - c * RT_CHUNK);
+    ok = mbar_wait_bounded(&full[st], (c / RM_NST) & 1, p.status, ST_TIMEOUT_FULL);
+    if (!ok) break;
+    const uint8_t* base = ring + st * (RM_WB + RM_XB);
+    const float2* ws = reinterpret_cast<const float2*>(base) + lane;
+    const uint8_t* xs = base + RM_WB + t0 * RT_CHUNK * 2;
+    // k in groups of 4, then the rest of a short last chunk one by one (k < kl only)
+    const int kq = kl & ~3;
+    for (int k = 0; k < kq; k += 4) {
+      const float2 w0 = ws[(k + 0) * 32], w1 = ws[(k + 1) * 32], w2 = ws[(k + 2) * 32], w3 = ws[(k + 3) * 32];
+#pragma unroll
+      for (int j = 0; j < TPW; ++j) {
+        const uint2 xv = *reinterpret_cast<const uint2*>(xs + j * RT_CHUNK * 2 + 2 * k);
+        const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xFFFF0000u);
+        const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xFFFF0000u);
+        acc[j] = rt_step2(acc[j], make_float2(x0, x0), w0, nz);
+        acc[j] = rt_step2(acc[j], make_float2(x1, x1), w1, nz);
+        acc[j] = rt_step2(acc[j], make_float2(x2, x2), w2, nz);
+        acc[j] = rt_step2(acc[j], make_float2(x3, x3), w3, nz);
+      }
+    }
+    for (int k = kq; k < kl; ++k) {
+      const float2 wk = ws[k * 32];
+#pragma unroll
+      for (int j = 0; j < TPW; ++j) {
+        const float xk = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(xs + j * RT_CHUNK * 2 + 2 * k));
+        acc[j] = rt_step2(acc[j], make_float2(xk, xk), wk, nz);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (ok) {
+#pragma unroll
+    for (int j = 0; j < TPW; ++j) {
+      const int t = t0 + j;
+      if (t < mb) {
+        const int64_t m = m0 + t;
+        const float l0 = bf16_round_f(acc[j].x), l1 = bf16_round_f(acc[j].y);
+        if (e < E) {
+          p.gate[m * E + e] = bf16_rne_bits(glm_sigmoid_bf(l0));
+          if (p.logits) p.logits[m * E + e] = bf16_rne_bits(l0);
+        }
+        if (e + 1 < E) {
+          p.gate[m * E + e + 1] = bf16_rne_bits(glm_sigmoid_bf(l1));
+          if (p.logits) p.logits[m * E + e + 1] = bf16_rne_bits(l1);
+        }
+      }
+    }
+  }
+  // the last CTA of this token block selects top-K for its tokens; the last block builds the union
+  float bias_pre[8];
+  router_bias_pre(p, bias_pre);
+  named_bar_sync(1, 32 * RM_WARPS);
+  if (threadIdx.x == 0)
+    last_flag = (atom_add_acq_rel_gpu(&p.counters[blockIdx.y], 1) == static_cast<int>(gridDim.x) - 1);
+  named_bar_sync(1, 32 * RM_WARPS);
+  if (!last_flag) return;
+  for (int j = 0; j < tpw; ++j)
+    if (t0 + j < mb) router_topk_token(p, m0 + t0 + j, bias_pre, sel_s + (t0 + j) * p.topk);
+  named_bar_sync(1, 32 * RM_WARPS);
+  if (gridDim.y > 1) {
+    if (threadIdx.x == 0) {
+      p.counters[blockIdx.y] = 0;
+      last_flag = (atom_add_acq_rel_gpu(&p.counters[gridDim.y], 1) == static_cast<int>(gridDim.y) - 1);
+    }
+    named_bar_sync(1, 32 * RM_WARPS);
+    if (!last_flag) return;
+  }
+  if (warp == 0) {
+    if (lane == 0) p.counters[gridDim.y > 1 ? gridDim.y : blockIdx.y] = 0;
+    if (p.union_ids) router_union(p, gridDim.y > 1 ? nullptr : sel_s);
+  }
+}
+
+// tokens per compute warp: the fewest CTAs that still give every SM one (8 at 2048 tokens x 256 experts)
+static int router_many_tpw(const RouterParams& p) {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms[dev] = 148;
+  const int64_t eg = (p.E + RM_EG - 1) / RM_EG;
+  const int64_t want = (static_cast<int64_t>(p.M) * eg + static_cast<int64_t>(RM_WARPS) * sms[dev] - 1) /
+                       (static_cast<int64_t>(RM_WARPS) * sms[dev]);
+  const int64_t w = std::max<int64_t>(1, std::min<int64_t>(8, want));
+  return w <= 1 ? 1 : w <= 2 ? 2 : w <= 4 ? 4 : 8;  // the kernel's instantiations
+}
+
+template <int TPW>
+static int router_launch_many_t(RouterParams q, cudaStream_t s, bool pdl) {
+  static bool attr[64] = {false};
+  const int arc = set_smem_attr_once(reinterpret_cast<const void*>(router_many_kernel<TPW>), RM_SMEM, attr,
+                                     "cudaFuncSetAttribute(router_many)");
+  if (arc) return arc;
+  return launch_kernel(reinterpret_cast<const void*>(router_many_kernel<TPW>),
+                       dim3((q.E + RM_EG - 1) / RM_EG, (q.M + RM_WARPS * TPW - 1) / (RM_WARPS * TPW)),
+                       dim3(32 * (RM_WARPS + 1)), RM_SMEM, s, pdl, &q);
+}
+
+static int router_launch_many(const RouterParams& p, cudaStream_t s, bool pdl) {
+  RouterParams q = p;
+  q.neg_zero = -0.0f;
+  q.tpw = router_many_tpw(p);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.K)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.E) * 4};
+  const cuuint32_t box[2] = {RM_EG, RT_CHUNK};
+  const int rc = encode_tiled(&q.wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.w, dims, strides, box);
+  if (rc) return rc;
+  switch (q.tpw) {
+    case 1: return router_launch_many_t<1>(q, s, pdl);
+    case 2: return router_launch_many_t<2>(q, s, pdl);
+    case 4: return router_launch_many_t<4>(q, s, pdl);
+    default: return router_launch_many_t<8>(q, s, pdl);
   }
 }
 
@@ -756,19 +893,21 @@ int router_launch(const RouterParams& p, cudaStream_t s, bool pdl) {
   // few token blocks: spread the router over more SMs; many: every lane of a CTA runs a packed chain
   // over two experts (dense fp32 router) or one (GGUF-row router)
   if (p.M <= 4 * RT_MB) return router_launch_eg<8>(p, s, pdl);
-  return (p.wt == WT_F32) ? router_launch_eg<64>(p, s, pdl) : router_launch_eg<32>(p, s, pdl);
+  return (p.wt == WT_F32) ? router_launch_many(p, s, pdl) : router_launch_eg<32>(p, s, pdl);
 }
 
-static int router_eg(const RouterParams& p) { return (p.M <= 4 * RT_MB) ? 8 : (p.wt == WT_F32 ? 64 : 32); }
-
 int router_grid_ctas(const RouterParams& p) {
-  const int eg = router_eg(p);
+  if (p.M > 4 * RT_MB && p.wt == WT_F32) {
+    const int tok = RM_WARPS * router_many_tpw(p);
+    return ((p.E + RM_EG - 1) / RM_EG) * ((p.M + tok - 1) / tok);
+  }
+  const int eg = (p.M <= 4 * RT_MB) ? 8 : 32;
   return ((p.E + eg - 1) / eg) * ((p.M + RT_MB - 1) / RT_MB);
 }
 
 int router_smem_bytes(const RouterParams& p) {
-  const int eg = router_eg(p);
-  return eg == 8 ? RtCfg<8>::SMEM : (eg == 64 ? RtCfg<64>::SMEM : RtCfg<32>::SMEM);
+  if (p.M <= 4 * RT_MB) return RtCfg<8>::SMEM;
+  return (p.wt == WT_F32) ? RM_SMEM : RtCfg<32>::SMEM;
 }
 
 // ------------------------------------------------------------------ combine

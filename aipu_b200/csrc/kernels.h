@@ -16,7 +16,8 @@ struct RouterParams {
   const uint16_t* x;       // bf16 [M, K]
   int M, K, E, topk;
   float scale;             // renormalisation scale (the reference uses 2.5)
-  float neg_zero;          // -0.0f, set by the launcher (the packed product's addend: see router_strict_kernel)
+  float neg_zero;          // -0.0f, set by the launcher (the packed product's addend)
+  int tpw;                 // router_many_kernel: tokens per compute warp (1..8), set by the launcher
   uint16_t* gate;          // bf16 [M, E] sigmoid gates (scratch and output)
   uint16_t* logits;        // bf16 [M, E] (nullable)
   int32_t* sel;            // [M, topk] selected experts, slot order
