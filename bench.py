@@ -11,8 +11,9 @@ launch per matrix are reported as "single_launch".
 Also reported: the roofline of the GEMV kernel against MEASURED_PEAKS.json; the CPU baselines (the C
 restatement of the reference's contract on all host cores, and the numpy restatement on a sample);
 the end-to-end number through the public API with host buffers; SM clocks sampled through NVML during
-the timed region; the MoE layer of BASELINE configs 3 (decode, M = 1 and 4) and 4 (prefill, 2048
-tokens) on the default bit-exact path and on the tensor-core path, each with parity against the
+the timed region; the Q6_K decode GEMV (6144 x 2048, grouped) with its parity; the MoE layer of
+BASELINE configs 3 (decode, M = 1 and 4) and 4 (prefill, 2048 tokens) on the default bit-exact path,
+the exact-gate/up + GEMV-down path and the tensor-core path, each with parity against the
 oracle computed in the same run (the oracle's timed CPU run of the same sampled tokens is the CPU
 baseline of that layer); at N > 1 the expert-parallel decode layer and the full-depth decode stream.
 
