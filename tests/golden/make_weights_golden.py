@@ -59,4 +59,8 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference tree's root: first argument, else the AIPU_REFERENCE environment variable
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AIPU_REFERENCE", "")
+    if not root:
+        sys.exit("usage: make_weights_golden.py <reference tree root> (or set AIPU_REFERENCE)")
+    main(root)
