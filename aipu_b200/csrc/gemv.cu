@@ -610,10 +610,18 @@ __device__ __forceinline__ void q4k_i8_fold(float (&acc)[4]) {
 // value d * sc[w / 16] * (code - 32). One u8 x s8 MMA per (n, c) covers 32 weights = two 16-weight
 // sub-blocks, told apart by the parity columns (activation k order = weight order). The codes are
 // assembled four at a time (mask the nibble plane, mask the 2-bit plane shifted into bits 4-5, OR);
-// the -32 offset is applied once per sub-block on the sums S_j of the staged activations. A4: the
-// unit's bytes start 4-byte aligned (else every word comes from two aligned loads; the offset is the
-// same for every row of a tiled slot, so the choice is warp-uniform).
-template <bool A4>
+// the -32 offset is applied once per sub-block on the sums S_j of the staged activations. AL: the
+// unit's start offset mod 8 (the same for every row of a tiled slot, so the choice is warp-uniform).
+// 8 bytes at a shared address whose offset mod 8 is AL (0, 4, or 2 for 2 / 6 mod 8)
+template <int AL>
+__device__ __forceinline__ uint2 q6_ld8(uint32_t a) {
+  if (AL == 0) return lds_v2(a);
+  if (AL == 4) return make_uint2(lds_v1(a), lds_v1(a + 4));
+  const uint32_t w0 = lds_v1(a - 2), w1 = lds_v1(a + 2), w2 = lds_v1(a + 6);
+  return make_uint2(__byte_perm(w0, w1, 0x5432), __byte_perm(w1, w2, 0x5432));
+}
+
+template <int AL>
 __device__ __forceinline__ void unit_q6k_i8(uint32_t rg, uint32_t rg8, uint32_t xb, uint32_t sxb, int t, float w0,
                                             float w1, float (&acc)[4]) {
   const int par = t >> 1;
@@ -622,16 +630,17 @@ __device__ __forceinline__ void unit_q6k_i8(uint32_t rg, uint32_t rg8, uint32_t 
   for (int i = 0; i < 8; ++i) D[i][0] = D[i][1] = D[i][2] = D[i][3] = 0;
 #pragma unroll
   for (int n = 0; n < 2; ++n) {
-    uint32_t la[2][2], lb[2][2], qh[2][2];  // [row g / g + 8][l = 4t / 16 + 4t]
+    // MMA k rows 4t..4t+3 (a0, a1) <-> weights l = 8t..8t+3, rows 16+4t.. (a2, a3) <-> l = 8t+4..8t+7 of
+    // the 32-weight group (the activation columns are read with the same permutation): one 8-byte
+    // load per row and plane
+    uint32_t la[2][2], lb[2][2], qh[2][2];  // [row g / g + 8][half: l = 8t.. / 8t+4..]
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
-      const uint32_t b = (rr ? rg8 : rg) + 4 * t;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        la[rr][hh] = lds4<A4>(b + 64 * n + 16 * hh);
-        lb[rr][hh] = lds4<A4>(b + 64 * n + 32 + 16 * hh);
-        qh[rr][hh] = lds4<A4>(b + 128 + 32 * n + 16 * hh);
-      }
+      const uint32_t b = (rr ? rg8 : rg) + 8 * t;
+      const uint2 va = q6_ld8<AL>(b + 64 * n), vb = q6_ld8<AL>(b + 64 * n + 32), vh = q6_ld8<AL>(b + 128 + 32 * n);
+      la[rr][0] = va.x; la[rr][1] = va.y;
+      lb[rr][0] = vb.x; lb[rr][1] = vb.y;
+      qh[rr][0] = vh.x; qh[rr][1] = vh.y;
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -646,8 +655,8 @@ __device__ __forceinline__ void unit_q6k_i8(uint32_t rg, uint32_t rg8, uint32_t 
           const uint32_t hb = (c == 0) ? (hw << 4) : (c == 1) ? (hw << 2) : (c == 2) ? hw : (hw >> 2);
           a[2 * hh + rr] = nib | (hb & 0x30303030u);
         }
-      const uint32_t xo = xb + 128 * n + 32 * c + 4 * t;
-      mma_u8s8_16832(D[4 * n + c], a, lds_v1(xo), lds_v1(xo + 16));
+      const uint2 xv = lds_v2(xb + 128 * n + 32 * c + 8 * t);
+      mma_u8s8_16832(D[4 * n + c], a, xv.x, xv.y);
     }
   }
   // sub-block j = 8 n + 2 c + parity: this lane's sets use the scales of its column parity
@@ -1158,9 +1167,10 @@ __global__ void __launch_bounds__(GEMV_MAXW * 32, 1) aipu_kq_gemv_kernel(const _
       } else if (ENG && WT == WT_Q6K) {
         const uint32_t xc8 = smem_u32(smem + L.off_xs + (xsl * 8 + g) * p.xpitch) + 256 * sb;
         const uint32_t sxb = smem_u32(smem + L.off_sxs) + 4 * (xsl * (p.K / 16) + 16 * sb);
-        const bool a4 = __shfl_sync(0xffffffffu, ((reinterpret_cast<uintptr_t>(rg) + i * UB) & 3u) == 0u, 0);
-        if (a4) unit_q6k_i8<true>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
-        else unit_q6k_i8<false>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
+        const int al = __shfl_sync(0xffffffffu, static_cast<int>((reinterpret_cast<uintptr_t>(rg) + i * UB) & 7u), 0);
+        if (al == 0) unit_q6k_i8<0>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
+        else if (al == 4) unit_q6k_i8<4>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
+        else unit_q6k_i8<2>(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, xc8, sxb, t, w0, w1, acc);
       } else if (WT == WT_Q4K) {
         const uint32_t sxcol = smem_u32(smem + L.off_sxs + (xsl * ncols + gx) * nsb * 64);
         unit_q4k(smem_u32(rg) + i * UB, smem_u32(r8) + i * UB, smem_u32(xcol), sxcol, sb, t, acc);
