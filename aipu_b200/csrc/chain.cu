@@ -567,14 +567,14 @@ bool chain_supported(int wt, int64_t K, int64_t row_bytes) {
 }
 
 template <int WT, int EPI, int MT, int NT>
-static int chain_launch_t(ChainParams& p, int grid, int smem, cudaStream_t s) {
+static int chain_launch_t(ChainParams& p, int grid, int smem, cudaStream_t s, bool pdl) {
   auto kern = aipu_chain_kernel<WT, EPI, MT, NT>;
   static bool attr[64] = {false};
   // the attribute is the largest dynamic shared memory any launch of this kernel uses (launches size it
   // differently: one or several CTAs per SM)
   const int rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), 232448 - 1024, attr, "cudaFuncSetAttribute(chain)");
   if (rc) return rc;
-  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NT + 32), smem, s, false, &p);
+  return launch_kernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NT + 32), smem, s, pdl, &p);
 }
 
 int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bool pdl) {
@@ -631,8 +631,12 @@ int chain_launch(int wt, int epi, ChainParams p, int num_sms, cudaStream_t s, bo
   if (items > (1ll << 30)) return set_error(EINVAL_, "chain: too many items");
   const int64_t slots = static_cast<int64_t>(num_sms) * std::max(1, limit / smem);
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(slots, items)));
+  // Programmatic dependent launch only for a grid of at most one CTA per SM: its CTAs wait on SMs the
+  // preceding kernel leaves free. A larger grid would park waiting CTAs on SMs the preceding kernel
+  // still needs for its own later CTAs (measured: slower at four tokens).
+  const bool pdl_one = pdl && grid <= num_sms;
 #define AIPU_CHAIN_CASE(W, E, M_, N_)                                                      \
-  if (wt == W && epi == E && mt == M_ && NT == N_) return chain_launch_t<W, E, M_, N_>(p, grid, smem, s);
+  if (wt == W && epi == E && mt == M_ && NT == N_) return chain_launch_t<W, E, M_, N_>(p, grid, smem, s, pdl_one);
 #define AIPU_CHAIN_MT(W, E, N_) \
   AIPU_CHAIN_CASE(W, E, 1, N_) AIPU_CHAIN_CASE(W, E, 2, N_) AIPU_CHAIN_CASE(W, E, 4, N_) AIPU_CHAIN_CASE(W, E, 8, N_)
   AIPU_CHAIN_MT(WT_Q4K, CHAIN_STORE, 128)
