@@ -401,9 +401,8 @@ __global__ void __launch_bounds__(CH_NT + 32) aipu_chain_kernel(const __grid_con
     fence_mbar_init();
   }
   __syncthreads();
-  // the token lists and activations come from the preceding kernels (launched without programmatic
-  // dependent launch: a persistent CTA of this kernel fills an SM, and one that waited early for its
-  // predecessor would hold the SM idle)
+  // the token lists and activations come from the preceding kernels (programmatic dependent launch
+  // only for grids of at most one CTA per SM, see chain_launch)
   pdl_wait();
   const int ngroups = p.tiles ? min(*p.n_tiles_dev, p.max_tiles)
                               : (p.n_groups_dev ? min(*p.n_groups_dev, p.n_groups) : p.n_groups);
