@@ -802,6 +802,9 @@ def main():
                 for _ in range(steps):
                     g.replay()
                 e1.record(s)
+                # wait by polling with sleeps (the clock sampler thread runs meanwhile)
+                while not e1.query():
+                    time.sleep(0.0002)
                 torch.cuda.synchronize()
         t = e0.elapsed_time(e1) / 1e3
         if world > 1:
