@@ -129,9 +129,9 @@ __device__ __forceinline__ void q4k_sb(uint32_t ra, uint32_t rb, uint32_t xs, fl
   const uint32_t sb47 = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
   const uint32_t mb47 = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
   const float2 nmag = f2s(-MAGF);
-  // one 64-weight group per iteration, not unrolled: the fully unrolled 256-weight body overflowed the
-  // instruction cache (measured: instruction-fetch stalls dominated)
-#pragma unroll 1
+  // two 64-weight groups per iteration (measured: one per iteration leaves latency exposed, all four
+  // overflow the instruction cache)
+#pragma unroll 2
   for (int g = 0; g < 4; ++g) {
     // sub-blocks 2g (low nibbles) and 2g + 1 (high nibbles): d1 = d*sc, m1 = dmin*m, both exact
     const bool hi4 = g >= 2;
